@@ -1,0 +1,163 @@
+/* gten_b200 — C ABI of the B200 (sm_100a) implementation of the gten compute path of
+ * iangitonga/nanochatllms.cpp.
+ *
+ * Drop-in boundary. Each entry point replaces one function of the reference's operator API
+ * (namespace gten::ops, src/gten/ops.h) or of its model / sampler interface, keeps its argument
+ * meaning and computes rows [start_pos, dimsize(0)) into a caller-owned, pre-sized output, with
+ * the reference's numerics (results are bit-identical to the reference CPU build; see each
+ * entry). Differences in error behaviour: where the reference's GTEN_ASSERT prints and calls
+ * exit(1) (src/gten/log.h:6-23), these functions return a non-zero gtn_status and leave the
+ * output untouched.
+ *
+ * Memory: tensor data pointers are CUDA device pointers unless an entry says "host".
+ * Streams: `stream` is a cudaStream_t (NULL = the legacy default stream); calls are
+ * asynchronous with respect to the host unless stated otherwise.
+ * Threading: calls on distinct streams may run concurrently; a model handle is single-caller.
+ */
+#ifndef GTEN_B200_H
+#define GTEN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (0 = success). */
+typedef enum {
+    GTN_OK = 0,
+    GTN_ERR_ARG = 1,     /* shape / dtype / range check failed (a GTEN_ASSERT in the reference) */
+    GTN_ERR_CUDA = 2,    /* a CUDA runtime call or kernel launch failed */
+    GTN_ERR_OOM = 3,     /* device or host allocation failed */
+    GTN_ERR_FORMAT = 4,  /* malformed .gten checkpoint (bad magic, record size, truncation) */
+    GTN_ERR_DEVICE = 5   /* a kernel reported a device-side error (e.g. a bounded wait expired) */
+} gtn_status;
+
+/* Element types; values equal the reference enum gten::Dtype (src/gten/gten_types.h:20-26). */
+typedef enum { GTN_I32 = 0, GTN_F16 = 1, GTN_F32 = 2, GTN_Q8 = 3, GTN_Q4 = 4 } gtn_dtype;
+
+/* Plain descriptor of a gten::Tensor (src/gten/tensor.h:17-137): data pointer, dtype, 1-3 dims,
+ * element strides. Quantized tensors use the reference's block layout: rows of 32-element
+ * blocks, Q8 block = fp16 delta + 32 int8 (34 bytes), Q4 block = fp16 delta + 16 bytes where
+ * byte j holds element j (high nibble) and element j+16 (low nibble), both +7 biased
+ * (src/gten/quants.h:11-30). Rows must be contiguous (stride(ndim-1) == 1). */
+typedef struct gtn_tensor {
+    void* data;
+    int32_t dtype;
+    int32_t ndim;
+    int32_t shape[3];
+    int32_t strides[3];
+} gtn_tensor;
+
+/* Human-readable text of the last error on the calling thread ("" if none). */
+const char* gtn_last_error(void);
+
+/* ---- gten::ops (src/gten/ops.h) ----------------------------------------------------------- */
+
+/* ops.h:16 matmul_2d(x, w, out, start_pos): out[r,:] = x[r,:] . w^T for r in [start_pos, n_ctx),
+ * dot products in the reference order (ops.cpp:292-523), rows written in out's dtype. A 1-D out
+ * (EmbeddingLinear's fp32 logits, modules.cpp:111-122) requires n_ctx - start_pos == 1.
+ * For a Q8 or fp16 `out` the fp32 dot products are staged in stream-ordered device scratch
+ * (cudaMallocAsync / cudaFreeAsync on `stream`). */
+int gtn_matmul_2d(const gtn_tensor* x, const gtn_tensor* w, gtn_tensor* out, int start_pos, void* stream);
+
+/* ops.h:22 qkv_attn(q, k, v, qk, qkv, max_ctx, start_pos): causal attention with GQA, the
+ * probability rows stored in the activation dtype as the reference does (ops.cpp:1017-1220).
+ * `qk` is accepted for signature parity and may be NULL: the probabilities stay on chip. */
+int gtn_qkv_attn(const gtn_tensor* q, const gtn_tensor* k, const gtn_tensor* v, gtn_tensor* qk, gtn_tensor* qkv,
+                 int max_ctx, int start_pos, void* stream);
+
+/* ops.h:24 rms_norm(inp, weight, out, start_pos): 2-D, or 3-D [n_ctx, heads, d_head] with a
+ * d_head weight (ops.cpp:830-915). Weight fp16. */
+int gtn_rms_norm(const gtn_tensor* inp, const gtn_tensor* weight, gtn_tensor* out, int start_pos, void* stream);
+
+/* ops.h:14 layer_norm(inp, weight, bias, out, start_pos) (ops.cpp:669-730). Weight, bias fp16. */
+int gtn_layer_norm(const gtn_tensor* inp, const gtn_tensor* weight, const gtn_tensor* bias, gtn_tensor* out,
+                   int start_pos, void* stream);
+
+/* ops.h:26 rotary_emb(inp, out, d_head, rope_pct, start_pos) (ops.cpp:775-827). inp may equal out. */
+int gtn_rotary_emb(const gtn_tensor* inp, gtn_tensor* out, int d_head, float rope_pct, int start_pos, void* stream);
+
+/* ops.h:30,32 silu / silu_inplace (ops.cpp:733-772). */
+int gtn_silu(const gtn_tensor* inp, gtn_tensor* out, int start_pos, void* stream);
+int gtn_silu_inplace(gtn_tensor* inp, int start_pos, void* stream);
+
+/* ops.h:18,20 multiply / multiply_inplace (ops.cpp:918-970). */
+int gtn_multiply(const gtn_tensor* inp0, const gtn_tensor* inp1, gtn_tensor* out, int start_pos, void* stream);
+int gtn_multiply_inplace(gtn_tensor* inp0, const gtn_tensor* inp1, int start_pos, void* stream);
+
+/* ops.h:10 add (ops.cpp:973-1014). */
+int gtn_add(const gtn_tensor* inp0, const gtn_tensor* inp1, gtn_tensor* out, int start_pos, void* stream);
+
+/* ops.h:28 scale(inp, scaler, start_pos), in place (ops.cpp:125-164). */
+int gtn_scale(gtn_tensor* inp, float scaler, int start_pos, void* stream);
+
+/* ops.h:12 bias_add_inplace(inp, bias, start_pos) (ops.cpp:639-666). Bias fp16. */
+int gtn_bias_add_inplace(gtn_tensor* inp, const gtn_tensor* bias, int start_pos, void* stream);
+
+/* ops.h:40 token_embed(weight, tokens, out, start_pos) (ops.cpp:526-576). Tokens int32 on device;
+ * Q4 rows are requantized to Q8 as copy_row does. */
+int gtn_token_embed(const gtn_tensor* weight, const gtn_tensor* tokens, gtn_tensor* out, int start_pos,
+                    void* stream);
+
+/* ---- quantization (src/gten/quants.cpp, src/<model>/<model>_to_gten.py) ------------------- */
+
+/* Weight packer, bit-exact with the reference converters' q8_quantize / q4_quantize
+ * (src/tinyllama/tinyllama_to_gten.py:24-91; identical copies in the other converters).
+ * w: device fp32 [rows, cols], cols % 32 == 0, 16-byte aligned; out: rows*cols/32 blocks. */
+int gtn_pack_q8(const float* w, int64_t rows, int64_t cols, void* out, void* stream);
+int gtn_pack_q4(const float* w, int64_t rows, int64_t cols, void* out, void* stream);
+
+/* Activation quantizer q8_quantize_row (quants.cpp:140-158) applied to `rows` rows of `cols`
+ * fp32 values (partial last block allowed). out: rows * ceil(cols/32) Q8 blocks. */
+int gtn_quantize_q8_rows(const float* x, int64_t rows, int64_t cols, void* out, void* stream);
+
+/* ---- sampler (src/gten/sampler.cpp) ------------------------------------------------------ */
+
+/* Greedy pick of sampler.cpp:30-41: index of the first maximum of n fp32 values. out_index:
+ * device int32. */
+int gtn_argmax(const float* logits, int n, int32_t* out_index, void* stream);
+
+/* ---- models (src/gten/abc.h:12-28 Model; src/tinyllama, zephyr, minicpm, openelm) -------- */
+
+typedef struct gtn_model gtn_model;
+
+/* Model kinds (the reference's four families and OpenELM sizes, nanochat.cpp:186-229). */
+enum {
+    GTN_MODEL_TINYLLAMA = 0,
+    GTN_MODEL_ZEPHYR = 1,
+    GTN_MODEL_MINICPM = 2,
+    GTN_MODEL_OPENELM_SM = 3,
+    GTN_MODEL_OPENELM_MD = 4,
+    GTN_MODEL_OPENELM_LG = 5,
+    GTN_MODEL_CUSTOM = 6
+};
+
+/* Creates a model of `kind` with weight dtype `wdtype` (GTN_F16, GTN_Q8 or GTN_Q4; activations
+ * are fp16 for GTN_F16 and Q8 otherwise, gten_types.h:40-42) on the current CUDA device, with
+ * KV capacity for `max_ctx` tokens per sequence and `max_batch` independent sequences.
+ * The reference's constructor is Model(n_ctx, dtype) (tinyllama.h:52 and siblings).
+ * For GTN_MODEL_CUSTOM, dims = {n_vocab, n_embd, n_layers, n_heads, n_kv_heads, n_ffn, family}
+ * with family 0 = TinyLlama-like, 1 = Zephyr-like, 2 = MiniCPM-like; otherwise dims may be NULL. */
+int gtn_model_create(int kind, int wdtype, int max_ctx, int max_batch, const int32_t* dims, gtn_model** out);
+void gtn_model_free(gtn_model* m);
+int gtn_model_n_vocab(const gtn_model* m);
+
+/* load_from_ckpt (e.g. tinyllama.cpp:195-251; reader utils.cpp:29-61) from a complete .gten
+ * image in host memory (magic, then records in the model's load order). */
+int gtn_model_load(gtn_model* m, const void* host_image, size_t nbytes);
+
+/* Model::logits(tokens, start_pos) for sequence 0 (abc.h:25): tokens (host int32, n_tokens total,
+ * rows [start_pos, n_tokens) are new) -> host fp32 logits of the last row. Synchronous. */
+int gtn_model_logits(gtn_model* m, const int32_t* tokens, int n_tokens, int start_pos, float* logits);
+
+/* greedy_sample (sampler.cpp:11-53) without tokenization and without the EOS stop: prefill the
+ * prompt (host int32), then n_gen greedy steps; out_tokens (host) receives the n_gen ids.
+ * Synchronous. */
+int gtn_model_generate(gtn_model* m, const int32_t* prompt, int n_prompt, int n_gen, int32_t* out_tokens);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GTEN_B200_H */

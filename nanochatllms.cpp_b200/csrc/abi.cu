@@ -1,0 +1,461 @@
+// Op-level C ABI (include/gten_b200.h): gten::ops, the packer / quantizer and the argmax.
+// Argument checks mirror the reference's GTEN_ASSERTs (src/gten/ops.cpp) but return GTN_ERR_ARG.
+#include <cmath>
+#include <cstdarg>
+#include <mutex>
+
+#include "launch.cuh"
+
+namespace gtn {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+static int cuda_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return GTN_OK;
+    return fail(e == cudaErrorMemoryAllocation ? GTN_ERR_OOM : GTN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+__device__ unsigned int g_dev_err;
+
+unsigned int* device_error_word() {
+    static thread_local int dev_cached = -1;
+    static thread_local unsigned int* p = nullptr;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != dev_cached) {
+        p = nullptr;
+        if (cudaGetSymbolAddress((void**)&p, g_dev_err) != cudaSuccess) p = nullptr;
+        dev_cached = dev;
+    }
+    return p;
+}
+
+unsigned int take_device_error() {
+    unsigned int v = 0, zero = 0;
+    unsigned int* p = device_error_word();
+    if (!p) return 0;
+    cudaMemcpy(&v, p, sizeof v, cudaMemcpyDeviceToHost);
+    if (v) cudaMemcpy(p, &zero, sizeof zero, cudaMemcpyHostToDevice);
+    return v;
+}
+
+std::vector<float2> rope_table_host(int npos, int rd) {
+    const int half = rd / 2;
+    const float d = (float)rd;
+    std::vector<float2> t((size_t)npos * (half > 0 ? half : 1));
+    for (int i = 0; i < npos; ++i) {
+        const float m = (float)i;
+        for (int j = 0; j < half; ++j) {
+            const float e = -((2.0f * (float)j) / d);
+            const float th = m * powf(10000.0f, e);
+            t[(size_t)i * half + j] = make_float2(cosf(th), sinf(th));
+        }
+    }
+    return t;
+}
+
+template <int WDT, int NW>
+static cudaError_t launch_mm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y,
+                               long ldy, cudaStream_t st, int mt) {
+    const dim3 grid((N + NW * 8 - 1) / (NW * 8), (M + mt - 1) / mt);
+    const size_t smem = mm_q_smem<WDT>(NW, mt, K);
+    unsigned int* err = device_error_word();
+    cudaError_t e;
+#define GTN_MMQ(MTV)                                                                              \
+    case MTV:                                                                                     \
+        e = ensure_smem(k_mm_q<WDT, NW, MTV>, smem);                                              \
+        if (e != cudaSuccess) return e;                                                           \
+        return launch_pdl(k_mm_q<WDT, NW, MTV>, grid, dim3(NW * 32), smem, st, W, ws, N, K, X, xs, M, Y, ldy, err);
+    switch (mt) {
+        GTN_MMQ(1)
+        GTN_MMQ(2)
+        GTN_MMQ(4)
+        default:
+            GTN_MMQ(8)
+    }
+#undef GTN_MMQ
+}
+
+template <int NW>
+static cudaError_t launch_mm_f16(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y,
+                                 long ldy, cudaStream_t st, int mt) {
+    const dim3 grid((N + NW * 4 - 1) / (NW * 4), (M + mt - 1) / mt);
+    const size_t smem = mm_f16_smem(NW, mt, K);
+    unsigned int* err = device_error_word();
+    cudaError_t e;
+#define GTN_MMF(MTV)                                                                              \
+    case MTV:                                                                                     \
+        e = ensure_smem(k_mm_f16<NW, MTV>, smem);                                                 \
+        if (e != cudaSuccess) return e;                                                           \
+        return launch_pdl(k_mm_f16<NW, MTV>, grid, dim3(NW * 32), smem, st, W, ws, N, K, X, xs, M, Y, ldy, err);
+    switch (mt) {
+        GTN_MMF(1)
+        GTN_MMF(2)
+        GTN_MMF(4)
+        default:
+            GTN_MMF(8)
+    }
+#undef GTN_MMF
+}
+
+cudaError_t matmul_f32(const uint8_t* X, long xs, int xdt, int M, const uint8_t* W, long ws, int wdt, int N, int K,
+                       float* Y, long ldy, cudaStream_t st) {
+    (void)xdt;
+    const int mt = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
+    if (wdt == GTN_F16) {
+        int nw = 4;
+        while (nw > 1 && (N + nw * 4 - 1) / (nw * 4) < 296) nw >>= 1;
+        int mtv = mt;
+        while (mtv > 1 && mm_f16_smem(nw, mtv, K) > 200 * 1024) mtv >>= 1;
+        if (nw == 4) return launch_mm_f16<4>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv);
+        if (nw == 2) return launch_mm_f16<2>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv);
+        return launch_mm_f16<1>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv);
+    }
+    int nw = 4;
+    while (nw > 1 && (N + nw * 8 - 1) / (nw * 8) < 296) nw >>= 1;
+    int mtv = mt;
+    if (wdt == GTN_Q8) {
+        while (mtv > 1 && mm_q_smem<GTN_Q8>(nw, mtv, K) > 200 * 1024) mtv >>= 1;
+        if (nw == 4) return launch_mm_q<GTN_Q8, 4>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv);
+        if (nw == 2) return launch_mm_q<GTN_Q8, 2>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv);
+        return launch_mm_q<GTN_Q8, 1>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv);
+    }
+    while (mtv > 1 && mm_q_smem<GTN_Q4>(nw, mtv, K) > 200 * 1024) mtv >>= 1;
+    if (nw == 4) return launch_mm_q<GTN_Q4, 4>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv);
+    if (nw == 2) return launch_mm_q<GTN_Q4, 2>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv);
+    return launch_mm_q<GTN_Q4, 1>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv);
+}
+
+}  // namespace gtn
+
+using namespace gtn;
+
+// ---- tensor helpers (tensor.h:96-116 bstride) -------------------------------------------------
+static bool valid_dtype(int dt) { return dt >= GTN_I32 && dt <= GTN_Q4; }
+
+static long bstride(const gtn_tensor* t, int i) {
+    const long s = t->strides[i];
+    switch (t->dtype) {
+        case GTN_Q4: return s == 1 ? 1 : (s / GTN_QBLK) * GTN_Q4_BYTES;
+        case GTN_Q8: return s == 1 ? 1 : (s / GTN_QBLK) * GTN_Q8_BYTES;
+        case GTN_F16: return s * 2;
+        default: return s * 4;
+    }
+}
+
+static int check_tensor(const gtn_tensor* t, const char* name) {
+    if (!t) return fail(GTN_ERR_ARG, "%s is NULL", name);
+    if (!t->data) return fail(GTN_ERR_ARG, "%s has no data", name);
+    if (!valid_dtype(t->dtype)) return fail(GTN_ERR_ARG, "%s has invalid dtype %d", name, t->dtype);
+    if (t->ndim < 1 || t->ndim > 3) return fail(GTN_ERR_ARG, "%s has %d dims", name, t->ndim);
+    for (int i = 0; i < t->ndim; ++i)
+        if (t->shape[i] <= 0) return fail(GTN_ERR_ARG, "%s dim %d is %d", name, i, t->shape[i]);
+    return GTN_OK;
+}
+
+static bool shape_eq(const gtn_tensor* a, const gtn_tensor* b) {
+    if (a->ndim != b->ndim) return false;
+    for (int i = 0; i < a->ndim; ++i)
+        if (a->shape[i] != b->shape[i]) return false;
+    return true;
+}
+
+static cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+#define GTN_CHECK(expr)                 \
+    do {                                \
+        const int rc_ = (expr);         \
+        if (rc_ != GTN_OK) return rc_;  \
+    } while (0)
+#define GTN_REQUIRE(cond, ...)                              \
+    do {                                                    \
+        if (!(cond)) return fail(GTN_ERR_ARG, __VA_ARGS__); \
+    } while (0)
+
+static int launched(const char* what) { return cuda_status(cudaGetLastError(), what); }
+
+static int norm_common(const gtn_tensor* inp, const gtn_tensor* weight, const gtn_tensor* bias, gtn_tensor* out,
+                       int start_pos, void* stream, bool layer) {
+    GTN_CHECK(check_tensor(inp, "inp"));
+    GTN_CHECK(check_tensor(weight, "weight"));
+    GTN_CHECK(check_tensor(out, "out"));
+    GTN_REQUIRE(inp->dtype == out->dtype, "norm: inp/out dtype");
+    GTN_REQUIRE(inp->dtype == GTN_Q8 || inp->dtype == GTN_F16 || inp->dtype == GTN_F32, "norm: dtype");
+    GTN_REQUIRE(weight->ndim == 1 && weight->dtype == GTN_F16, "norm: weight must be 1-D fp16");
+    const int n_ctx = inp->shape[0];
+    GTN_REQUIRE(start_pos >= 0 && start_pos < n_ctx, "norm: start_pos");
+    int heads = 1, n = inp->ndim >= 2 ? inp->shape[1] : 0;
+    long hs = 0;
+    if (inp->ndim == 3) {
+        GTN_REQUIRE(!layer, "layer_norm: 2-D input");
+        heads = inp->shape[1];
+        n = inp->shape[2];
+        hs = bstride(inp, 1);
+        GTN_REQUIRE(inp->dtype != GTN_Q8 || n % GTN_QBLK == 0, "rms_norm: 3-D Q8 head size %d", n);
+    } else {
+        GTN_REQUIRE(inp->ndim == 2, "norm: 2-D or 3-D input");
+    }
+    GTN_REQUIRE(weight->shape[0] == n, "norm: weight size %d != %d", weight->shape[0], n);
+    if (layer) {
+        GTN_CHECK(check_tensor(bias, "bias"));
+        GTN_REQUIRE(bias->ndim == 1 && bias->dtype == GTN_F16 && bias->shape[0] == n, "layer_norm: bias");
+    }
+    const size_t smem = sizeof(float) * (size_t)n;
+    cudaError_t e;
+    if (layer) {
+        e = ensure_smem(k_norm<true>, smem);
+        if (e == cudaSuccess)
+            e = launch_pdl(k_norm<true>, dim3(heads, n_ctx - start_pos), dim3(256), smem, S(stream),
+                           (const uint8_t*)inp->data, bstride(inp, 0), hs, (uint8_t*)out->data, bstride(out, 0), hs,
+                           (int)inp->dtype, n, start_pos, (const uint16_t*)weight->data,
+                           (const uint16_t*)bias->data);
+    } else {
+        e = ensure_smem(k_norm<false>, smem);
+        // The 3-D path writes out with the input's strides (ops.cpp:879).
+        if (e == cudaSuccess)
+            e = launch_pdl(k_norm<false>, dim3(heads, n_ctx - start_pos), dim3(256), smem, S(stream),
+                           (const uint8_t*)inp->data, bstride(inp, 0), hs, (uint8_t*)out->data,
+                           inp->ndim == 3 ? bstride(inp, 0) : bstride(out, 0), hs, (int)inp->dtype, n, start_pos,
+                           (const uint16_t*)weight->data, (const uint16_t*)nullptr);
+    }
+    return cuda_status(e, "norm");
+}
+
+template <int OP>
+static int rowop(const gtn_tensor* a, const gtn_tensor* b, gtn_tensor* out, float s, const gtn_tensor* bias,
+                 int start_pos, void* stream, const char* name) {
+    GTN_CHECK(check_tensor(a, "inp0"));
+    GTN_CHECK(check_tensor(out, "out"));
+    GTN_REQUIRE(a->ndim == 2 && out->ndim == 2 && shape_eq(a, out), "%s: shapes", name);
+    GTN_REQUIRE(a->dtype == out->dtype, "%s: dtypes", name);
+    GTN_REQUIRE(a->dtype == GTN_Q8 || a->dtype == GTN_F16 || a->dtype == GTN_F32, "%s: dtype", name);
+    if (b) {
+        GTN_CHECK(check_tensor(b, "inp1"));
+        GTN_REQUIRE(shape_eq(a, b) && a->dtype == b->dtype, "%s: inp1", name);
+    }
+    if (OP == ROP_BIAS) {
+        GTN_CHECK(check_tensor(bias, "bias"));
+        GTN_REQUIRE(bias->ndim == 1 && bias->dtype == GTN_F16 && bias->shape[0] == a->shape[1], "%s: bias", name);
+    }
+    const int n_ctx = a->shape[0], n = a->shape[1];
+    GTN_REQUIRE(start_pos >= 0 && start_pos < n_ctx, "%s: start_pos", name);
+    const int nb = (n + GTN_QBLK - 1) / GTN_QBLK;
+    cudaError_t e = launch_pdl(k_rowop<OP>, dim3((nb + 3) / 4, n_ctx - start_pos), dim3(128), 0, S(stream),
+                               (const uint8_t*)a->data, bstride(a, 0), (const uint8_t*)(b ? b->data : nullptr),
+                               b ? bstride(b, 0) : 0L, (uint8_t*)out->data, bstride(out, 0), (int)a->dtype, n,
+                               start_pos, s, (const uint16_t*)(bias ? bias->data : nullptr));
+    return cuda_status(e, name);
+}
+
+extern "C" {
+
+const char* gtn_last_error(void) { return g_last_error.c_str(); }
+
+// ops.cpp:617-636
+int gtn_matmul_2d(const gtn_tensor* x, const gtn_tensor* w, gtn_tensor* out, int start_pos, void* stream) {
+    GTN_CHECK(check_tensor(x, "x"));
+    GTN_CHECK(check_tensor(w, "w"));
+    GTN_CHECK(check_tensor(out, "out"));
+    GTN_REQUIRE(x->ndim == 2, "matmul_2d: x must be 2-D");
+    GTN_REQUIRE(w->ndim == 2 && w->shape[1] == x->shape[1], "matmul_2d: w must be [n_out, n_embd]");
+    const int n_ctx = x->shape[0], K = x->shape[1], N = w->shape[0];
+    GTN_REQUIRE(start_pos >= 0 && start_pos < n_ctx, "matmul_2d: start_pos %d out of [0, %d)", start_pos, n_ctx);
+    if (out->ndim == 1) {
+        GTN_REQUIRE(n_ctx - start_pos == 1, "matmul_2d: 1-D out needs exactly one new row");
+        GTN_REQUIRE(out->shape[0] == N, "matmul_2d: out shape");
+    } else {
+        GTN_REQUIRE(out->ndim == 2 && out->shape[0] == n_ctx && out->shape[1] == N, "matmul_2d: out shape");
+    }
+    const bool q = x->dtype == GTN_Q8 && (w->dtype == GTN_Q8 || w->dtype == GTN_Q4);
+    const bool h = x->dtype == GTN_F16 && w->dtype == GTN_F16;
+    GTN_REQUIRE(q || h, "matmul_2d: unsupported dtypes x=%d w=%d", x->dtype, w->dtype);
+    GTN_REQUIRE(K % GTN_QBLK == 0 || h, "matmul_2d: n_embd %d not a multiple of 32", K);
+    GTN_REQUIRE(out->dtype == GTN_F32 || out->dtype == x->dtype, "matmul_2d: out dtype");
+    const int M = n_ctx - start_pos;
+    const uint8_t* X = (const uint8_t*)x->data + (long)start_pos * bstride(x, 0);
+    const long os = out->ndim == 1 ? 0 : bstride(out, 0);
+    cudaStream_t st = S(stream);
+    if (out->dtype == GTN_F32) {
+        float* Y = (float*)((uint8_t*)out->data + (long)start_pos * os);
+        return cuda_status(matmul_f32(X, bstride(x, 0), x->dtype, M, (const uint8_t*)w->data, bstride(w, 0),
+                                      w->dtype, N, K, Y, out->ndim == 1 ? 0 : N, st),
+                           "matmul_2d");
+    }
+    float* Y = nullptr;
+    GTN_CHECK(cuda_status(cudaMallocAsync((void**)&Y, sizeof(float) * (size_t)M * N, st), "matmul_2d scratch"));
+    cudaError_t e = matmul_f32(X, bstride(x, 0), x->dtype, M, (const uint8_t*)w->data, bstride(w, 0), w->dtype, N,
+                               K, Y, N, st);
+    if (e == cudaSuccess)
+        e = launch_pdl(k_write_rows, dim3(((N + GTN_QBLK - 1) / GTN_QBLK + 3) / 4, M), dim3(128), 0, st,
+                       (const float*)Y, (long)N, (uint8_t*)out->data, os, (int)out->dtype, N, start_pos);
+    cudaFreeAsync(Y, st);
+    return cuda_status(e, "matmul_2d");
+}
+
+// ops.cpp:1205-1220
+int gtn_qkv_attn(const gtn_tensor* q, const gtn_tensor* k, const gtn_tensor* v, gtn_tensor* qk, gtn_tensor* qkv,
+                 int max_ctx, int start_pos, void* stream) {
+    (void)qk;
+    GTN_CHECK(check_tensor(q, "q"));
+    GTN_CHECK(check_tensor(k, "k"));
+    GTN_CHECK(check_tensor(v, "v"));
+    GTN_CHECK(check_tensor(qkv, "qkv"));
+    GTN_REQUIRE(q->ndim == 2 && k->ndim == 2 && v->ndim == 2 && qkv->ndim == 2, "qkv_attn: 2-D tensors");
+    const int n_ctx = q->shape[0], q_dim = q->shape[1], kv_dim = k->shape[1];
+    GTN_REQUIRE(qkv->shape[0] == n_ctx && qkv->shape[1] == q_dim, "qkv_attn: qkv shape");
+    GTN_REQUIRE(k->shape[0] >= n_ctx && v->shape[0] >= n_ctx && v->shape[1] == kv_dim, "qkv_attn: k/v shape");
+    GTN_REQUIRE(q->dtype == k->dtype && k->dtype == v->dtype && v->dtype == qkv->dtype, "qkv_attn: dtypes differ");
+    GTN_REQUIRE(q->dtype == GTN_Q8 || q->dtype == GTN_F16, "qkv_attn: dtype must be Q8 or F16");
+    GTN_REQUIRE(max_ctx > 0 && max_ctx >= n_ctx, "qkv_attn: max_ctx");
+    GTN_REQUIRE(start_pos >= 0 && start_pos < n_ctx, "qkv_attn: start_pos");
+    const int d = 64;  // the reference's head size for every model
+    GTN_REQUIRE(q_dim % d == 0 && kv_dim % d == 0, "qkv_attn: dims not multiples of 64");
+    const int qh = q_dim / d, kvh = kv_dim / d;
+    GTN_REQUIRE(qh % kvh == 0, "qkv_attn: heads %d not a multiple of kv heads %d", qh, kvh);
+    const size_t smem = attn_smem(n_ctx, q->dtype, d);
+    GTN_REQUIRE(smem <= 200 * 1024, "qkv_attn: n_ctx %d too large", n_ctx);
+    cudaError_t e = ensure_smem(k_attn, smem);
+    if (e == cudaSuccess)
+        e = launch_pdl(k_attn, dim3(qh, n_ctx - start_pos), dim3(ATT_THREADS), smem, S(stream),
+                       (const uint8_t*)q->data, bstride(q, 0), (const uint8_t*)k->data, bstride(k, 0),
+                       (const uint8_t*)v->data, bstride(v, 0), (uint8_t*)qkv->data, bstride(qkv, 0), (int)q->dtype,
+                       n_ctx, start_pos, qh, kvh, d);
+    return cuda_status(e, "qkv_attn");
+}
+
+int gtn_rms_norm(const gtn_tensor* inp, const gtn_tensor* weight, gtn_tensor* out, int start_pos, void* stream) {
+    return norm_common(inp, weight, nullptr, out, start_pos, stream, false);
+}
+
+int gtn_layer_norm(const gtn_tensor* inp, const gtn_tensor* weight, const gtn_tensor* bias, gtn_tensor* out,
+                   int start_pos, void* stream) {
+    GTN_REQUIRE(inp && out && shape_eq(inp, out), "layer_norm: inp/out shapes differ");
+    return norm_common(inp, weight, bias, out, start_pos, stream, true);
+}
+
+// ops.cpp:775-827. The (cos, sin) table for this call's positions is computed on the host with the
+// reference's expression and uploaded once per (rd, device) and growth of the position count.
+int gtn_rotary_emb(const gtn_tensor* inp, gtn_tensor* out, int d_head, float rope_pct, int start_pos, void* stream) {
+    GTN_CHECK(check_tensor(inp, "inp"));
+    GTN_CHECK(check_tensor(out, "out"));
+    GTN_REQUIRE(inp->ndim == 2 && out->ndim == 2, "rotary_emb: 2-D tensors");
+    GTN_REQUIRE(rope_pct >= 0.0f && rope_pct <= 1.0f, "rotary_emb: rope_pct");
+    GTN_REQUIRE(d_head > 0 && d_head % 32 == 0 && d_head <= 256, "rotary_emb: d_head %d unsupported", d_head);
+    const int n_ctx = inp->shape[0], n_embd = inp->shape[1];
+    GTN_REQUIRE(n_embd % d_head == 0 && out->shape[0] >= n_ctx && out->shape[1] == n_embd, "rotary_emb: shapes");
+    GTN_REQUIRE(inp->dtype == out->dtype, "rotary_emb: dtypes");
+    GTN_REQUIRE(inp->dtype == GTN_Q8 || inp->dtype == GTN_F16 || inp->dtype == GTN_F32, "rotary_emb: dtype");
+    GTN_REQUIRE(start_pos >= 0 && start_pos < n_ctx, "rotary_emb: start_pos");
+    const int rd = (int)((float)d_head * rope_pct);
+    const int half = rd / 2;
+    static std::mutex mu;
+    struct Entry { int rd, dev, npos; float2* tab; };
+    static std::vector<Entry> cache;
+    float2* tab = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        int dev = 0;
+        cudaGetDevice(&dev);
+        for (auto& c : cache)
+            if (c.rd == rd && c.dev == dev && c.npos >= n_ctx) tab = c.tab;
+        if (!tab) {
+            const int npos = n_ctx < 4096 ? 4096 : n_ctx;
+            auto hst = rope_table_host(npos, rd);
+            GTN_CHECK(cuda_status(cudaMalloc((void**)&tab, hst.size() * sizeof(float2)), "rope table"));
+            GTN_CHECK(cuda_status(cudaMemcpy(tab, hst.data(), hst.size() * sizeof(float2), cudaMemcpyHostToDevice),
+                                  "rope table"));
+            cache.push_back({rd, dev, npos, tab});
+        }
+    }
+    cudaError_t e = launch_pdl(k_rope, dim3(n_embd / d_head, n_ctx - start_pos), dim3(32), 0, S(stream),
+                               (const uint8_t*)inp->data, bstride(inp, 0), (uint8_t*)out->data, bstride(inp, 0),
+                               (int)inp->dtype, n_embd, d_head, half, start_pos, (const float2*)tab,
+                               half > 0 ? half : 1);
+    return cuda_status(e, "rotary_emb");
+}
+
+int gtn_silu(const gtn_tensor* inp, gtn_tensor* out, int start_pos, void* stream) {
+    return rowop<ROP_SILU>(inp, nullptr, out, 0.0f, nullptr, start_pos, stream, "silu");
+}
+int gtn_silu_inplace(gtn_tensor* inp, int start_pos, void* stream) {
+    return rowop<ROP_SILU>(inp, nullptr, inp, 0.0f, nullptr, start_pos, stream, "silu_inplace");
+}
+int gtn_multiply(const gtn_tensor* inp0, const gtn_tensor* inp1, gtn_tensor* out, int start_pos, void* stream) {
+    return rowop<ROP_MUL>(inp0, inp1, out, 0.0f, nullptr, start_pos, stream, "multiply");
+}
+int gtn_multiply_inplace(gtn_tensor* inp0, const gtn_tensor* inp1, int start_pos, void* stream) {
+    return rowop<ROP_MUL>(inp0, inp1, inp0, 0.0f, nullptr, start_pos, stream, "multiply_inplace");
+}
+int gtn_add(const gtn_tensor* inp0, const gtn_tensor* inp1, gtn_tensor* out, int start_pos, void* stream) {
+    return rowop<ROP_ADD>(inp0, inp1, out, 0.0f, nullptr, start_pos, stream, "add");
+}
+int gtn_scale(gtn_tensor* inp, float scaler, int start_pos, void* stream) {
+    return rowop<ROP_SCALE>(inp, nullptr, inp, scaler, nullptr, start_pos, stream, "scale");
+}
+int gtn_bias_add_inplace(gtn_tensor* inp, const gtn_tensor* bias, int start_pos, void* stream) {
+    return rowop<ROP_BIAS>(inp, nullptr, inp, 0.0f, bias, start_pos, stream, "bias_add_inplace");
+}
+
+// ops.cpp:566-576
+int gtn_token_embed(const gtn_tensor* weight, const gtn_tensor* tokens, gtn_tensor* out, int start_pos,
+                    void* stream) {
+    GTN_CHECK(check_tensor(weight, "weight"));
+    GTN_CHECK(check_tensor(tokens, "tokens"));
+    GTN_CHECK(check_tensor(out, "out"));
+    GTN_REQUIRE(weight->ndim == 2, "token_embed: weight 2-D");
+    GTN_REQUIRE(tokens->ndim == 1 && tokens->dtype == GTN_I32, "token_embed: tokens 1-D int32");
+    const int n_ctx = tokens->shape[0], n = weight->shape[1];
+    GTN_REQUIRE(out->ndim == 2 && out->shape[0] == n_ctx && out->shape[1] == n, "token_embed: out shape");
+    GTN_REQUIRE(weight->dtype == GTN_Q4 ? out->dtype == GTN_Q8 : out->dtype == weight->dtype, "token_embed: dtypes");
+    GTN_REQUIRE(start_pos >= 0 && start_pos < n_ctx, "token_embed: start_pos");
+    const int nb = (n + GTN_QBLK - 1) / GTN_QBLK;
+    cudaError_t e = launch_pdl(k_embed, dim3((nb + 3) / 4, n_ctx - start_pos), dim3(128), 0, S(stream),
+                               (const uint8_t*)weight->data, bstride(weight, 0), (int)weight->dtype,
+                               (const int32_t*)tokens->data, (uint8_t*)out->data, bstride(out, 0), (int)out->dtype, n,
+                               start_pos);
+    return cuda_status(e, "token_embed");
+}
+
+int gtn_pack_q8(const float* w, int64_t rows, int64_t cols, void* out, void* stream) {
+    GTN_REQUIRE(w && out && rows > 0 && cols > 0 && cols % GTN_QBLK == 0, "pack_q8: arguments");
+    GTN_REQUIRE(((uintptr_t)w & 15) == 0, "pack_q8: w must be 16-byte aligned");
+    const long nb = rows * (cols / GTN_QBLK);
+    k_pack<false><<<(unsigned)((nb + 255) / 256), 256, 0, S(stream)>>>(w, nb, (uint8_t*)out);
+    return launched("pack_q8");
+}
+
+int gtn_pack_q4(const float* w, int64_t rows, int64_t cols, void* out, void* stream) {
+    GTN_REQUIRE(w && out && rows > 0 && cols > 0 && cols % GTN_QBLK == 0, "pack_q4: arguments");
+    GTN_REQUIRE(((uintptr_t)w & 15) == 0, "pack_q4: w must be 16-byte aligned");
+    const long nb = rows * (cols / GTN_QBLK);
+    k_pack<true><<<(unsigned)((nb + 255) / 256), 256, 0, S(stream)>>>(w, nb, (uint8_t*)out);
+    return launched("pack_q4");
+}
+
+int gtn_quantize_q8_rows(const float* x, int64_t rows, int64_t cols, void* out, void* stream) {
+    GTN_REQUIRE(x && out && rows > 0 && cols > 0 && rows < 65536, "quantize_q8_rows: arguments");
+    const int nb = (int)((cols + GTN_QBLK - 1) / GTN_QBLK);
+    cudaError_t e = launch_pdl(k_quant_rows, dim3((nb + 3) / 4, (unsigned)rows), dim3(128), 0, S(stream), x,
+                               (long)cols, (uint8_t*)out, (long)nb * GTN_Q8_BYTES, (int)cols);
+    return cuda_status(e, "quantize_q8_rows");
+}
+
+int gtn_argmax(const float* logits, int n, int32_t* out_index, void* stream) {
+    GTN_REQUIRE(logits && out_index && n > 0, "argmax: arguments");
+    cudaError_t e = launch_pdl(k_argmax, dim3(1), dim3(1024), 0, S(stream), logits, n, out_index, 0L, 0L);
+    return cuda_status(e, "argmax");
+}
+
+}  // extern "C"

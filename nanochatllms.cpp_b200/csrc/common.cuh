@@ -1,0 +1,128 @@
+// Shared device helpers for the gten B200 kernels.
+//
+// Numerics contract: every kernel reproduces the reference CPU build's arithmetic bit for bit
+// (iangitonga/nanochatllms.cpp, src/gten). The library is compiled with --fmad=false so that
+// no multiply-add is contracted (the reference is built with -mavx and no FMA, so each
+// multiply and add rounds separately); fmaf() is only written out where a fused operation is
+// provably exact. Division and square root are IEEE round-to-nearest (nvcc's defaults).
+#pragma once
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "../../include/gten_b200.h"
+
+#define GTN_QBLK 32
+#define GTN_Q8_BYTES 34  // quants.h:11-22: fp16 delta + 32 int8
+#define GTN_Q4_BYTES 18  // quants.h:24-30: fp16 delta + 16 bytes (two nibbles each)
+
+namespace gtn {
+
+__host__ __device__ inline long row_bytes(int dt, int n) {
+    switch (dt) {
+        case GTN_Q8: return (long)((n + GTN_QBLK - 1) / GTN_QBLK) * GTN_Q8_BYTES;
+        case GTN_Q4: return (long)(n / GTN_QBLK) * GTN_Q4_BYTES;
+        case GTN_F16: return 2L * n;
+        default: return 4L * n;
+    }
+}
+
+// fp16 <-> fp32: hardware conversions; fp16 -> fp32 is exact and fp32 -> fp16 rounds to nearest
+// even, as the reference's fp16_to_fp32 table and fp32_to_fp16 bit trick do (gten_types.h:69-109).
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+__device__ __forceinline__ uint16_t ld_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
+
+// exp rounded correctly to float: computed in double precision by CUDA's exp() and rounded once.
+// glibc's expf (what the reference calls) agrees with the correctly rounded value on all but
+// about 7.6e-5 of float inputs, where it is one ulp away.
+__device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
+
+// Quantize one 32-element block held one element per lane (quants.cpp:16-30): absmax over the
+// valid lanes, delta = absmax/127 (fp32, stored as fp16), scale = 1/delta of the UNROUNDED delta,
+// q = roundf(x*scale) (half away from zero). Lanes >= n hold 0 and write nothing.
+// Returns the quantized value; every lane receives the fp16 delta in *dh.
+__device__ __forceinline__ int8_t warp_quant_block(float x, int lane, int n, uint16_t* dh) {
+    float a = lane < n ? fabsf(x) : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    const float delta = a / 127.0f;
+    *dh = f2h(delta);
+    const float scale = delta != 0.0f ? 1.0f / delta : 0.0f;
+    return (int8_t)roundf(x * scale);
+}
+
+// Writes `n` (<= 32) floats, one per lane, as one Q8 block at `blk` (34 bytes).
+__device__ __forceinline__ void warp_store_q8_block(float x, int lane, int n, uint8_t* blk) {
+    uint16_t dh;
+    const int8_t q = warp_quant_block(x, lane, n, &dh);
+    if (lane == 0) *reinterpret_cast<uint16_t*>(blk) = dh;
+    if (lane < n) blk[2 + lane] = (uint8_t)q;
+}
+
+// Reads element `i` of a row in dtype dt (Q8/Q4/F16/F32) as float (quants.cpp:33-138).
+__device__ __forceinline__ float load_elem(const uint8_t* row, int dt, int i) {
+    switch (dt) {
+        case GTN_Q8: {
+            const uint8_t* b = row + (i / GTN_QBLK) * GTN_Q8_BYTES;
+            return (float)(int8_t)b[2 + (i % GTN_QBLK)] * h2f(ld_u16(b));
+        }
+        case GTN_Q4: {
+            const uint8_t* b = row + (i / GTN_QBLK) * GTN_Q4_BYTES;
+            const int j = i % GTN_QBLK;
+            const uint8_t p = b[2 + (j & 15)];
+            const int v = (j < 16 ? (p >> 4) : (p & 15)) - 7;
+            return (float)v * h2f(ld_u16(b));
+        }
+        case GTN_F16: return h2f(reinterpret_cast<const uint16_t*>(row)[i]);
+        default: return reinterpret_cast<const float*>(row)[i];
+    }
+}
+
+// ---- TMA bulk copies with bounded mbarrier waits --------------------------------------------
+// Every wait has an iteration limit; on expiry the kernel records GTN_DEVERR_TIMEOUT in the
+// caller-visible error word and returns instead of spinning forever.
+#define GTN_WAIT_LIMIT (1u << 26)
+#define GTN_DEVERR_TIMEOUT 1u
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+// Returns false (and flags *err) if the phase did not complete within the limit.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase, unsigned int* err) {
+    for (uint32_t it = 0; it < GTN_WAIT_LIMIT; ++it)
+        if (mbar_try_wait(bar, phase)) return true;
+    if (err) atomicOr(err, GTN_DEVERR_TIMEOUT);
+    return false;
+}
+// 1-D TMA bulk copy global -> shared, completion counted on `bar`. dst, src 16-byte aligned,
+// bytes a multiple of 16. (No multicast: the source may be any GPU's memory.)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+}  // namespace gtn

@@ -1,0 +1,521 @@
+// Model engine: the four reference model families (src/tinyllama, src/zephyr, src/minicpm,
+// src/openelm) on the B200 kernels, behind gtn_model_* (include/gten_b200.h).
+//
+// HBM layout. All weights live in one arena in the reference's block format. Per layer the q/k/v
+// weights are stacked row-wise into one [q_dim + 2*kv_dim, d] matrix and gate/up into one
+// [2*ffn, d] matrix, so each is streamed by one matmul launch; rows keep the reference layout and
+// the stacked outputs are split at multiples of 32 columns, so requantizing each slice equals
+// requantizing each Linear's output (modules.cpp:89-104). Row strides are padded to 16 bytes
+// where the reference row size is not a multiple of 16 (MiniCPM's 5760-wide down projection), and
+// every tensor is followed by 64 bytes of padding, which the TMA tile reads may touch.
+// The KV cache of layer l is the K/V Linear activation buffer of the reference (modules.cpp:78-87):
+// [max_batch][max_ctx][kv_dim] rows in the activation dtype, post-RoPE keys.
+// Activations of the rows being computed use local row indices 0..M-1.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <vector>
+
+#include "launch.cuh"
+
+namespace gtn {
+
+struct Layer {
+    int nh = 0, nkv = 0, nffn = 0;
+    const uint8_t *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wd = nullptr;
+    long rs_d = 0, rs_q = 0, rs_f = 0;  // weight row strides for inputs of width d, q_dim, ffn
+    const uint16_t *bq = nullptr, *bk = nullptr, *bv = nullptr;
+    const uint16_t *n1w = nullptr, *n1b = nullptr, *n2w = nullptr, *n2b = nullptr, *qnw = nullptr, *knw = nullptr;
+    uint8_t *kc = nullptr, *vc = nullptr;
+};
+
+}  // namespace gtn
+
+struct gtn_model {
+    int kind = 0, family = 0, wdt = 0, adt = 0, max_ctx = 0, max_batch = 0;
+    int n_vocab = 0, d = 0, nl = 0, dh = 64;
+    float rope_pct = 1.0f;
+    int rd = 64;
+    std::vector<gtn::Layer> L;
+    uint8_t* arena = nullptr;
+    size_t arena_bytes = 0;
+    const uint8_t *emb = nullptr, *lm_head = nullptr;
+    long emb_rs = 0;
+    const uint16_t *nfw = nullptr, *nfb = nullptr;
+    bool loaded = false;
+    // activations, capacity max_rows local rows
+    int max_rows = 0, max_q = 0, max_kv = 0, max_ffn = 0;
+    uint8_t *x = nullptr, *a = nullptr, *h = nullptr, *o = nullptr, *q = nullptr, *qn = nullptr, *att = nullptr;
+    uint8_t *g = nullptr, *u = nullptr, *kn = nullptr;
+    float* y = nullptr;
+    float* logits = nullptr;
+    int32_t* tok = nullptr;
+    int32_t* next = nullptr;
+    float2* rope = nullptr;
+    cudaStream_t st = nullptr;
+    std::vector<void*> allocs;
+};
+
+namespace gtn {
+
+static const int elm_sm_qh[] = {12, 12, 12, 12, 12, 16, 16, 16, 16, 16, 16, 16, 20, 20, 20, 20};
+static const int elm_sm_kv[] = {3, 3, 3, 3, 3, 4, 4, 4, 4, 4, 4, 4, 5, 5, 5, 5};
+static const int elm_sm_ff[] = {768, 1024, 1280, 1536, 1792, 2048, 2560, 2816, 3072, 3328, 3584, 3840, 4352, 4608, 4864, 5120};
+static const int elm_md_qh[] = {12, 12, 12, 16, 16, 16, 16, 16, 16, 16, 20, 20, 20, 20, 20, 20, 24, 24, 24, 24};
+static const int elm_md_kv[] = {3, 3, 3, 4, 4, 4, 4, 4, 4, 4, 5, 5, 5, 5, 5, 5, 6, 6, 6, 6};
+static const int elm_md_ff[] = {768, 1024, 1280, 1536, 1792, 2304, 2560, 2816, 3072, 3328, 3584, 3840, 4096, 4352, 4608, 5120, 5376, 5632, 5888, 6144};
+static const int elm_lg_qh[] = {16, 16, 16, 20, 20, 20, 20, 20, 20, 20, 24, 24, 24, 24, 24, 24, 24, 24, 28, 28, 28, 28, 28, 28, 32, 32, 32, 32};
+static const int elm_lg_kv[] = {4, 4, 4, 5, 5, 5, 5, 5, 5, 5, 6, 6, 6, 6, 6, 6, 6, 6, 7, 7, 7, 7, 7, 7, 8, 8, 8, 8};
+static const int elm_lg_ff[] = {1024, 1280, 1536, 1792, 2048, 2304, 2560, 2816, 3072, 3328, 3584, 3840, 4096, 4608, 4608, 5120, 5376, 5632, 5888, 6144, 6400, 6656, 6912, 7168, 7424, 7680, 7936, 8192};
+
+static long pad16(long b) { return (b + 15) & ~15L; }
+
+static int cuda_st(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return GTN_OK;
+    return fail(e == cudaErrorMemoryAllocation ? GTN_ERR_OOM : GTN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define ECHK(expr, what)                       \
+    do {                                       \
+        const int rc_ = cuda_st((expr), what); \
+        if (rc_ != GTN_OK) return rc_;         \
+    } while (0)
+
+template <typename T>
+static int dalloc(gtn_model* m, T** p, size_t bytes) {
+    void* v = nullptr;
+    ECHK(cudaMalloc(&v, bytes ? bytes : 16), "cudaMalloc");
+    m->allocs.push_back(v);
+    *p = reinterpret_cast<T*>(v);
+    return GTN_OK;
+}
+
+// Record reader (utils.cpp:29-61): int32 name length + name, twice, then int32 payload size.
+struct Reader {
+    const uint8_t* p;
+    const uint8_t* end;
+    int err = 0;
+    const uint8_t* next(long expect) {
+        if (err) return nullptr;
+        for (int t = 0; t < 2; ++t) {
+            int32_t n;
+            if (end - p < 4) { err = 1; return nullptr; }
+            memcpy(&n, p, 4);
+            if (n < 0 || end - p < 4 + (long)n) { err = 1; return nullptr; }
+            p += 4 + n;
+        }
+        int32_t sz;
+        if (end - p < 4) { err = 1; return nullptr; }
+        memcpy(&sz, p, 4);
+        p += 4;
+        if (sz != expect || end - p < sz) { err = 2; return nullptr; }
+        const uint8_t* r = p;
+        p += sz;
+        return r;
+    }
+};
+
+static void free_all(gtn_model* m) {
+    for (void* p : m->allocs) cudaFree(p);
+    m->allocs.clear();
+}
+
+}  // namespace gtn
+
+using namespace gtn;
+
+extern "C" {
+
+int gtn_model_create(int kind, int wdtype, int max_ctx, int max_batch, const int32_t* dims, gtn_model** out) {
+    if (!out) return fail(GTN_ERR_ARG, "model_create: out is NULL");
+    *out = nullptr;
+    if (wdtype != GTN_F16 && wdtype != GTN_Q8 && wdtype != GTN_Q4) return fail(GTN_ERR_ARG, "model_create: wdtype");
+    if (max_ctx <= 0 || max_batch <= 0) return fail(GTN_ERR_ARG, "model_create: max_ctx/max_batch");
+    std::unique_ptr<gtn_model> m(new gtn_model());
+    m->kind = kind;
+    m->wdt = wdtype;
+    m->adt = wdtype == GTN_F16 ? GTN_F16 : GTN_Q8;  // gten_types.h:40-42
+    m->max_ctx = max_ctx;
+    m->max_batch = max_batch;
+    int nh = 0, nkv = 0, nff = 0;
+    const int *qh = nullptr, *kv = nullptr, *ff = nullptr;
+    switch (kind) {  // tinyllama.h:12-24, zephyr.h:10-23, minicpm.h:9-24, openelm.h:26-51
+        case GTN_MODEL_TINYLLAMA: m->family = 0; m->n_vocab = 32003; m->d = 2048; m->nl = 22; nh = 32; nkv = 4; nff = 5632; break;
+        case GTN_MODEL_ZEPHYR: m->family = 1; m->n_vocab = 100352; m->d = 2048; m->nl = 24; nh = 32; nkv = 32; nff = 5632; m->rope_pct = 0.25f; break;
+        case GTN_MODEL_MINICPM: m->family = 2; m->n_vocab = 122753; m->d = 2304; m->nl = 40; nh = 36; nkv = 36; nff = 5760; break;
+        case GTN_MODEL_OPENELM_SM: m->family = 3; m->n_vocab = 32000; m->d = 1280; m->nl = 16; qh = elm_sm_qh; kv = elm_sm_kv; ff = elm_sm_ff; break;
+        case GTN_MODEL_OPENELM_MD: m->family = 3; m->n_vocab = 32000; m->d = 1536; m->nl = 20; qh = elm_md_qh; kv = elm_md_kv; ff = elm_md_ff; break;
+        case GTN_MODEL_OPENELM_LG: m->family = 3; m->n_vocab = 32000; m->d = 2048; m->nl = 28; qh = elm_lg_qh; kv = elm_lg_kv; ff = elm_lg_ff; break;
+        case GTN_MODEL_CUSTOM:
+            if (!dims) return fail(GTN_ERR_ARG, "model_create: custom model needs dims");
+            m->n_vocab = dims[0]; m->d = dims[1]; m->nl = dims[2]; nh = dims[3]; nkv = dims[4]; nff = dims[5];
+            m->family = dims[6];
+            if (m->family < 0 || m->family > 2) return fail(GTN_ERR_ARG, "model_create: family %d", m->family);
+            if (m->family == 1) m->rope_pct = 0.25f;
+            if (m->n_vocab <= 0 || m->d <= 0 || m->d % 64 || m->nl <= 0 || nh <= 0 || nkv <= 0 || nh % nkv ||
+                nff <= 0 || nff % 32)
+                return fail(GTN_ERR_ARG, "model_create: invalid custom dims");
+            break;
+        default: return fail(GTN_ERR_ARG, "model_create: kind %d", kind);
+    }
+    m->rd = (int)((float)m->dh * m->rope_pct);
+    m->L.resize(m->nl);
+    for (int l = 0; l < m->nl; ++l) {
+        m->L[l].nh = qh ? qh[l] : nh;
+        m->L[l].nkv = kv ? kv[l] : nkv;
+        m->L[l].nffn = ff ? ff[l] : nff;
+        m->max_q = std::max(m->max_q, m->L[l].nh * m->dh);
+        m->max_kv = std::max(m->max_kv, m->L[l].nkv * m->dh);
+        m->max_ffn = std::max(m->max_ffn, m->L[l].nffn);
+    }
+    ECHK(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking), "stream");
+    // activations: up to max_ctx rows (prefill of a full context)
+    m->max_rows = max_ctx;
+    const int adt = m->adt;
+    const long R = m->max_rows;
+    int rc = GTN_OK;
+    rc |= dalloc(m.get(), &m->x, R * row_bytes(adt, m->d));
+    rc |= dalloc(m.get(), &m->a, R * row_bytes(adt, m->d));
+    rc |= dalloc(m.get(), &m->h, R * row_bytes(adt, m->d));
+    rc |= dalloc(m.get(), &m->o, R * row_bytes(adt, m->d));
+    rc |= dalloc(m.get(), &m->q, R * row_bytes(adt, m->max_q));
+    rc |= dalloc(m.get(), &m->qn, R * row_bytes(adt, m->max_q));
+    rc |= dalloc(m.get(), &m->att, R * row_bytes(adt, m->max_q));
+    rc |= dalloc(m.get(), &m->kn, R * row_bytes(adt, m->max_kv));
+    rc |= dalloc(m.get(), &m->g, R * row_bytes(adt, m->max_ffn));
+    rc |= dalloc(m.get(), &m->u, R * row_bytes(adt, m->max_ffn));
+    const long ywidth = std::max<long>(m->max_q + 2L * m->max_kv, 2L * m->max_ffn);
+    rc |= dalloc(m.get(), &m->y, sizeof(float) * R * ywidth);
+    rc |= dalloc(m.get(), &m->logits, sizeof(float) * (size_t)m->n_vocab * max_batch);
+    rc |= dalloc(m.get(), &m->tok, sizeof(int32_t) * (size_t)max_ctx * max_batch);
+    rc |= dalloc(m.get(), &m->next, sizeof(int32_t) * (size_t)max_batch);
+    for (int l = 0; l < m->nl && rc == GTN_OK; ++l) {
+        const long kvb = (long)max_batch * max_ctx * row_bytes(adt, m->L[l].nkv * m->dh);
+        rc |= dalloc(m.get(), &m->L[l].kc, kvb);
+        rc |= dalloc(m.get(), &m->L[l].vc, kvb);
+    }
+    if (rc == GTN_OK && m->rd > 0) {
+        auto tab = rope_table_host(max_ctx, m->rd);
+        rc = dalloc(m.get(), &m->rope, tab.size() * sizeof(float2));
+        if (rc == GTN_OK)
+            rc = cuda_st(cudaMemcpy(m->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice),
+                         "rope table");
+    }
+    if (rc != GTN_OK) {
+        free_all(m.get());
+        cudaStreamDestroy(m->st);
+        return rc == GTN_ERR_OOM || (rc & GTN_ERR_OOM) ? GTN_ERR_OOM : rc;
+    }
+    *out = m.release();
+    return GTN_OK;
+}
+
+void gtn_model_free(gtn_model* m) {
+    if (!m) return;
+    if (m->st) cudaStreamSynchronize(m->st);
+    free_all(m);
+    if (m->arena) cudaFree(m->arena);
+    if (m->st) cudaStreamDestroy(m->st);
+    delete m;
+}
+
+int gtn_model_n_vocab(const gtn_model* m) { return m ? m->n_vocab : 0; }
+
+// load_from_ckpt: tinyllama.cpp:195-251, zephyr.cpp:79-150, minicpm.cpp:113-166, openelm.cpp:201-262.
+int gtn_model_load(gtn_model* m, const void* host_image, size_t nbytes) {
+    if (!m || !host_image) return fail(GTN_ERR_ARG, "model_load: arguments");
+    const uint8_t* img = (const uint8_t*)host_image;
+    int64_t magic = 0;
+    if (nbytes < 8) return fail(GTN_ERR_FORMAT, "model_load: truncated header");
+    memcpy(&magic, img, 8);
+    if (magic != 0x454c49464e455447LL) return fail(GTN_ERR_FORMAT, "model_load: bad magic");
+    Reader rd{img + 8, img + nbytes};
+    const int d = m->d, wdt = m->wdt, dh = m->dh;
+    const bool fam1 = m->family == 1, fam3 = m->family == 3;
+    // First pass: locate records and size the arena.
+    struct Piece { const uint8_t* src; long rows; long rb; long off; };
+    std::vector<Piece> pieces;
+    long off = 0;
+    auto place = [&](const uint8_t* src, long rows, long rb) -> long {
+        const long o = off;
+        pieces.push_back({src, rows, rb, o});
+        off += pad16(rows * pad16(rb)) + 64;
+        return o;
+    };
+    // stacked tensors: consecutive pieces share one padded row stride
+    auto place_rows = [&](const uint8_t* src, long rows, long rb) -> long {
+        const long o = off;
+        pieces.push_back({src, rows, rb, o});
+        off += rows * pad16(rb);
+        return o;
+    };
+    auto end_stack = [&]() { off = pad16(off) + 64; };
+    const long rbd = row_bytes(wdt, d);
+    struct LOff { long qkv, o, gu, dn, bq, bk, bv, n1w, n1b, n2w, n2b, qnw, knw; };
+    std::vector<LOff> lo(m->nl);
+    const uint8_t* emb = rd.next(rbd * m->n_vocab);
+    if (!emb) return fail(GTN_ERR_FORMAT, "model_load: embedding record (%d)", rd.err);
+    const long emb_off = place(emb, m->n_vocab, rbd);
+    for (int l = 0; l < m->nl; ++l) {
+        Layer& Ly = m->L[l];
+        const int qd = Ly.nh * dh, kvd = Ly.nkv * dh;
+        const uint8_t *bq = nullptr, *bk = nullptr, *bv = nullptr;
+        const uint8_t* wq = rd.next(rbd * qd);
+        if (fam1) bq = rd.next(2L * qd);
+        const uint8_t* wk = rd.next(rbd * kvd);
+        if (fam1) bk = rd.next(2L * kvd);
+        const uint8_t* wv = rd.next(rbd * kvd);
+        if (fam1) bv = rd.next(2L * kvd);
+        const uint8_t* wo = rd.next(row_bytes(wdt, qd) * d);
+        const uint8_t* wg = rd.next(rbd * Ly.nffn);
+        const uint8_t* wu = rd.next(rbd * Ly.nffn);
+        const uint8_t* wdn = rd.next(row_bytes(wdt, Ly.nffn) * d);
+        const uint8_t *qnw = nullptr, *knw = nullptr;
+        if (fam3) {
+            qnw = rd.next(2L * dh);
+            knw = rd.next(2L * dh);
+        }
+        const uint8_t* n1w = rd.next(2L * d);
+        const uint8_t* n1b = fam1 ? rd.next(2L * d) : nullptr;
+        const uint8_t* n2w = rd.next(2L * d);
+        const uint8_t* n2b = fam1 ? rd.next(2L * d) : nullptr;
+        if (rd.err) return fail(GTN_ERR_FORMAT, "model_load: layer %d records (%d)", l, rd.err);
+        lo[l].qkv = place_rows(wq, qd, rbd);
+        place_rows(wk, kvd, rbd);
+        place_rows(wv, kvd, rbd);
+        end_stack();
+        lo[l].o = place(wo, d, row_bytes(wdt, qd));
+        lo[l].gu = place_rows(wg, Ly.nffn, rbd);
+        place_rows(wu, Ly.nffn, rbd);
+        end_stack();
+        lo[l].dn = place(wdn, d, row_bytes(wdt, Ly.nffn));
+        lo[l].bq = fam1 ? place(bq, 1, 2L * qd) : -1;
+        lo[l].bk = fam1 ? place(bk, 1, 2L * kvd) : -1;
+        lo[l].bv = fam1 ? place(bv, 1, 2L * kvd) : -1;
+        lo[l].qnw = fam3 ? place(qnw, 1, 2L * dh) : -1;
+        lo[l].knw = fam3 ? place(knw, 1, 2L * dh) : -1;
+        lo[l].n1w = place(n1w, 1, 2L * d);
+        lo[l].n1b = fam1 ? place(n1b, 1, 2L * d) : -1;
+        lo[l].n2w = place(n2w, 1, 2L * d);
+        lo[l].n2b = fam1 ? place(n2b, 1, 2L * d) : -1;
+    }
+    const uint8_t* nfw = rd.next(2L * d);
+    const uint8_t* nfb = fam1 ? rd.next(2L * d) : nullptr;
+    const uint8_t* lmh = (m->family == 0 || m->family == 1) ? rd.next(rbd * m->n_vocab) : nullptr;
+    if (rd.err) return fail(GTN_ERR_FORMAT, "model_load: final records (%d)", rd.err);
+    const long nfw_off = place(nfw, 1, 2L * d);
+    const long nfb_off = fam1 ? place(nfb, 1, 2L * d) : -1;
+    const long lmh_off = lmh ? place(lmh, m->n_vocab, rbd) : -1;
+
+    if (m->arena) {
+        cudaFree(m->arena);
+        m->arena = nullptr;
+        m->loaded = false;
+    }
+    ECHK(cudaMalloc((void**)&m->arena, (size_t)off), "model_load: arena");
+    m->arena_bytes = (size_t)off;
+    ECHK(cudaMemset(m->arena, 0, (size_t)off), "model_load: arena clear");
+    for (const Piece& p : pieces) {
+        if (pad16(p.rb) == p.rb || p.rows == 1)
+            ECHK(cudaMemcpy(m->arena + p.off, p.src, (size_t)(p.rows * p.rb), cudaMemcpyHostToDevice), "model_load");
+        else
+            ECHK(cudaMemcpy2D(m->arena + p.off, (size_t)pad16(p.rb), p.src, (size_t)p.rb, (size_t)p.rb,
+                              (size_t)p.rows, cudaMemcpyHostToDevice),
+                 "model_load");
+    }
+    uint8_t* A = m->arena;
+    m->emb = A + emb_off;
+    m->emb_rs = pad16(rbd);
+    for (int l = 0; l < m->nl; ++l) {
+        Layer& Ly = m->L[l];
+        Ly.wqkv = A + lo[l].qkv;
+        Ly.wo = A + lo[l].o;
+        Ly.wgu = A + lo[l].gu;
+        Ly.wd = A + lo[l].dn;
+        Ly.rs_d = pad16(rbd);
+        Ly.rs_q = pad16(row_bytes(wdt, Ly.nh * dh));
+        Ly.rs_f = pad16(row_bytes(wdt, Ly.nffn));
+        Ly.bq = fam1 ? (const uint16_t*)(A + lo[l].bq) : nullptr;
+        Ly.bk = fam1 ? (const uint16_t*)(A + lo[l].bk) : nullptr;
+        Ly.bv = fam1 ? (const uint16_t*)(A + lo[l].bv) : nullptr;
+        Ly.qnw = fam3 ? (const uint16_t*)(A + lo[l].qnw) : nullptr;
+        Ly.knw = fam3 ? (const uint16_t*)(A + lo[l].knw) : nullptr;
+        Ly.n1w = (const uint16_t*)(A + lo[l].n1w);
+        Ly.n1b = fam1 ? (const uint16_t*)(A + lo[l].n1b) : nullptr;
+        Ly.n2w = (const uint16_t*)(A + lo[l].n2w);
+        Ly.n2b = fam1 ? (const uint16_t*)(A + lo[l].n2b) : nullptr;
+    }
+    m->nfw = (const uint16_t*)(A + nfw_off);
+    m->nfb = fam1 ? (const uint16_t*)(A + nfb_off) : nullptr;
+    m->lm_head = lmh ? A + lmh_off : m->emb;  // TiedEmbedding::forward_proj (modules.cpp:48-59)
+    m->loaded = true;
+    return GTN_OK;
+}
+
+}  // extern "C"
+
+namespace gtn {
+
+static cudaError_t rows_op(int op, const uint8_t* a, long as, const uint8_t* b, long bs, uint8_t* out, long os,
+                           int dt, int n, int M, float s, const uint16_t* bias, cudaStream_t st) {
+    const dim3 grid(((n + 31) / 32 + 3) / 4, M);
+    switch (op) {
+        case ROP_SILU: return launch_pdl(k_rowop<ROP_SILU>, grid, dim3(128), 0, st, a, as, b, bs, out, os, dt, n, 0, s, bias);
+        case ROP_MUL: return launch_pdl(k_rowop<ROP_MUL>, grid, dim3(128), 0, st, a, as, b, bs, out, os, dt, n, 0, s, bias);
+        case ROP_ADD: return launch_pdl(k_rowop<ROP_ADD>, grid, dim3(128), 0, st, a, as, b, bs, out, os, dt, n, 0, s, bias);
+        case ROP_SCALE: return launch_pdl(k_rowop<ROP_SCALE>, grid, dim3(128), 0, st, a, as, b, bs, out, os, dt, n, 0, s, bias);
+        default: return launch_pdl(k_rowop<ROP_BIAS>, grid, dim3(128), 0, st, a, as, b, bs, out, os, dt, n, 0, s, bias);
+    }
+}
+
+static cudaError_t norm_rows(const gtn_model* m, const uint8_t* x, uint8_t* out, const uint16_t* w, const uint16_t* b,
+                             int M, cudaStream_t st) {
+    const long rs = row_bytes(m->adt, m->d);
+    const size_t smem = sizeof(float) * m->d;
+    if (m->family == 1)
+        return launch_pdl(k_norm<true>, dim3(1, M), dim3(256), smem, st, x, rs, 0L, out, rs, 0L, m->adt, m->d, 0, w, b);
+    return launch_pdl(k_norm<false>, dim3(1, M), dim3(256), smem, st, x, rs, 0L, out, rs, 0L, m->adt, m->d, 0, w,
+                      (const uint16_t*)nullptr);
+}
+
+// fp32 columns [c0, c0+n) of Y (row stride ldy) -> rows of `out` in dtype dt (stride os).
+static cudaError_t write_cols(const float* Y, long ldy, int c0, int n, uint8_t* out, long os, int dt, int M,
+                              cudaStream_t st) {
+    return launch_pdl(k_write_rows, dim3(((n + 31) / 32 + 3) / 4, M), dim3(128), 0, st, Y + c0, ldy, out, os, dt, n, 0);
+}
+
+// Rows [sp, n) of sequence `seq` (tokens already on the device at m->tok + seq*max_ctx).
+// Writes the last row's fp32 logits to m->logits + seq*n_vocab and its argmax to m->next[seq].
+// Model::logits, e.g. tinyllama.cpp:122-138 with blocks :99-104 and ffn :88-97; zephyr.cpp:36-76;
+// minicpm.cpp:52-110; openelm.cpp:33-58,103-146; SelfAttention::forward modules.cpp:286-315.
+static int forward(gtn_model* m, int seq, int n, int sp) {
+    cudaStream_t st = m->st;
+    const int adt = m->adt, d = m->d, dh = m->dh, M = n - sp;
+    const long rd_ = row_bytes(adt, d);
+    const float depth = (float)(1.4f / std::sqrt(40.0));  // minicpm.cpp:57
+    cudaError_t e = cudaSuccess;
+#define GK(expr)                                            \
+    do {                                                    \
+        e = (expr);                                         \
+        if (e != cudaSuccess) return cuda_st(e, #expr);     \
+    } while (0)
+    const int32_t* toks = m->tok + (long)seq * m->max_ctx + sp;
+    GK(launch_pdl(k_embed, dim3(((d + 31) / 32 + 3) / 4, M), dim3(128), 0, st, m->emb, m->emb_rs, m->wdt, toks, m->x,
+                  rd_, adt, d, 0));
+    if (m->family == 2) GK(rows_op(ROP_SCALE, m->x, rd_, nullptr, 0, m->x, rd_, adt, d, M, 12.0f, nullptr, st));
+    for (int l = 0; l < m->nl; ++l) {
+        Layer& Ly = m->L[l];
+        const int qd = Ly.nh * dh, kvd = Ly.nkv * dh, nqkv = qd + 2 * kvd;
+        const long rq = row_bytes(adt, qd), rkv = row_bytes(adt, kvd), rf = row_bytes(adt, Ly.nffn);
+        uint8_t* kc = Ly.kc + ((long)seq * m->max_ctx) * rkv;
+        uint8_t* vc = Ly.vc + ((long)seq * m->max_ctx) * rkv;
+        GK(norm_rows(m, m->x, m->a, Ly.n1w, Ly.n1b, M, st));
+        GK(matmul_f32(m->a, rd_, adt, M, Ly.wqkv, Ly.rs_d, m->wdt, nqkv, d, m->y, nqkv, st));
+        GK(write_cols(m->y, nqkv, 0, qd, m->q, rq, adt, M, st));
+        GK(write_cols(m->y, nqkv, qd, kvd, kc + (long)sp * rkv, rkv, adt, M, st));
+        GK(write_cols(m->y, nqkv, qd + kvd, kvd, vc + (long)sp * rkv, rkv, adt, M, st));
+        if (Ly.bq) {
+            GK(rows_op(ROP_BIAS, m->q, rq, nullptr, 0, m->q, rq, adt, qd, M, 0.0f, Ly.bq, st));
+            GK(rows_op(ROP_BIAS, kc + (long)sp * rkv, rkv, nullptr, 0, kc + (long)sp * rkv, rkv, adt, kvd, M, 0.0f,
+                       Ly.bk, st));
+            GK(rows_op(ROP_BIAS, vc + (long)sp * rkv, rkv, nullptr, 0, vc + (long)sp * rkv, rkv, adt, kvd, M, 0.0f,
+                       Ly.bv, st));
+        }
+        const int half = m->rd / 2;
+        const long hb = row_bytes(adt, dh);
+        if (m->family == 3) {
+            // openelm.cpp:44-52: QK RMSNorm over heads, then RoPE into the cache / query buffer.
+            GK(launch_pdl(k_norm<false>, dim3(Ly.nh, M), dim3(256), sizeof(float) * dh, st, (const uint8_t*)m->q, rq,
+                          hb, m->qn, rq, hb, adt, dh, 0, Ly.qnw, (const uint16_t*)nullptr));
+            GK(launch_pdl(k_norm<false>, dim3(Ly.nkv, M), dim3(256), sizeof(float) * dh, st,
+                          (const uint8_t*)(kc + (long)sp * rkv), rkv, hb, m->kn, rkv, hb, adt, dh, 0, Ly.knw,
+                          (const uint16_t*)nullptr));
+            // the rope kernels index rows by absolute position; local buffers get bases shifted by -sp rows
+            GK(launch_pdl(k_rope, dim3(Ly.nh, M), dim3(32), 0, st, (const uint8_t*)(m->qn - (long)sp * rq), rq,
+                          m->q - (long)sp * rq, rq, adt, qd, dh, half, sp, (const float2*)m->rope, half));
+            GK(launch_pdl(k_rope, dim3(Ly.nkv, M), dim3(32), 0, st, (const uint8_t*)(m->kn - (long)sp * rkv), rkv,
+                          kc, rkv, adt, kvd, dh, half, sp, (const float2*)m->rope, half));
+        } else if (half > 0) {
+            GK(launch_pdl(k_rope, dim3(Ly.nh, M), dim3(32), 0, st, (const uint8_t*)(m->q - (long)sp * rq), rq,
+                          m->q - (long)sp * rq, rq, adt, qd, dh, half, sp, (const float2*)m->rope, half));
+            GK(launch_pdl(k_rope, dim3(Ly.nkv, M), dim3(32), 0, st, (const uint8_t*)kc, rkv, kc, rkv, adt, kvd, dh,
+                          half, sp, (const float2*)m->rope, half));
+        }
+        const size_t asmem = attn_smem(n, adt, dh);
+        GK(ensure_smem(k_attn, asmem));
+        GK(launch_pdl(k_attn, dim3(Ly.nh, M), dim3(ATT_THREADS), asmem, st, (const uint8_t*)(m->q - (long)sp * rq),
+                      rq, (const uint8_t*)kc, rkv, (const uint8_t*)vc, rkv, m->att - (long)sp * rq, rq, adt, n, sp,
+                      Ly.nh, Ly.nkv, dh));
+        GK(matmul_f32(m->att, rq, adt, M, Ly.wo, Ly.rs_q, m->wdt, d, qd, m->y, d, st));
+        GK(write_cols(m->y, d, 0, d, m->o, rd_, adt, M, st));
+        if (m->family == 2) GK(rows_op(ROP_SCALE, m->o, rd_, nullptr, 0, m->o, rd_, adt, d, M, depth, nullptr, st));
+        GK(rows_op(ROP_ADD, m->x, rd_, m->o, rd_, m->h, rd_, adt, d, M, 0.0f, nullptr, st));
+        GK(norm_rows(m, m->h, m->a, Ly.n2w, Ly.n2b, M, st));
+        GK(matmul_f32(m->a, rd_, adt, M, Ly.wgu, Ly.rs_d, m->wdt, 2 * Ly.nffn, d, m->y, 2L * Ly.nffn, st));
+        GK(write_cols(m->y, 2L * Ly.nffn, 0, Ly.nffn, m->g, rf, adt, M, st));
+        GK(write_cols(m->y, 2L * Ly.nffn, Ly.nffn, Ly.nffn, m->u, rf, adt, M, st));
+        GK(rows_op(ROP_SILU, m->g, rf, nullptr, 0, m->g, rf, adt, Ly.nffn, M, 0.0f, nullptr, st));
+        GK(rows_op(ROP_MUL, m->g, rf, m->u, rf, m->g, rf, adt, Ly.nffn, M, 0.0f, nullptr, st));
+        GK(matmul_f32(m->g, rf, adt, M, Ly.wd, Ly.rs_f, m->wdt, d, Ly.nffn, m->y, d, st));
+        GK(write_cols(m->y, d, 0, d, m->o, rd_, adt, M, st));
+        if (m->family == 2) GK(rows_op(ROP_SCALE, m->o, rd_, nullptr, 0, m->o, rd_, adt, d, M, depth, nullptr, st));
+        GK(rows_op(ROP_ADD, m->h, rd_, m->o, rd_, m->x, rd_, adt, d, M, 0.0f, nullptr, st));
+    }
+    // final norm and lm_head on the last row only (the other rows' logits are never read).
+    uint8_t* xl = m->x + (long)(M - 1) * rd_;
+    GK(norm_rows(m, xl, m->a, m->nfw, m->nfb, 1, st));
+    if (m->family == 2) GK(rows_op(ROP_SCALE, m->a, rd_, nullptr, 0, m->a, rd_, adt, d, 1, 1.0f / 9, nullptr, st));
+    float* lg = m->logits + (long)seq * m->n_vocab;
+    GK(matmul_f32(m->a, rd_, adt, 1, m->lm_head, m->emb_rs, m->wdt, m->n_vocab, d, lg, m->n_vocab, st));
+    GK(launch_pdl(k_argmax, dim3(1), dim3(1024), 0, st, (const float*)lg, m->n_vocab, m->next + seq, 0L, 0L));
+#undef GK
+    return GTN_OK;
+}
+
+static int check_dev_err() {
+    const unsigned int v = take_device_error();
+    if (v) return fail(GTN_ERR_DEVICE, "device-side bounded wait expired (code %u)", v);
+    return GTN_OK;
+}
+
+}  // namespace gtn
+
+extern "C" {
+
+int gtn_model_logits(gtn_model* m, const int32_t* tokens, int n_tokens, int start_pos, float* logits) {
+    if (!m || !m->loaded || !tokens || !logits) return fail(GTN_ERR_ARG, "model_logits: arguments");
+    if (n_tokens > m->max_ctx) return fail(GTN_ERR_ARG, "model_logits: %d tokens exceed max_ctx %d", n_tokens, m->max_ctx);
+    if (start_pos < 0 || start_pos >= n_tokens) return fail(GTN_ERR_ARG, "model_logits: start_pos");
+    for (int i = 0; i < n_tokens; ++i)
+        if (tokens[i] < 0 || tokens[i] >= m->n_vocab) return fail(GTN_ERR_ARG, "model_logits: token id %d", tokens[i]);
+    ECHK(cudaMemcpyAsync(m->tok, tokens, sizeof(int32_t) * n_tokens, cudaMemcpyHostToDevice, m->st), "tokens");
+    const int rc = forward(m, 0, n_tokens, start_pos);
+    if (rc != GTN_OK) return rc;
+    ECHK(cudaMemcpyAsync(logits, m->logits, sizeof(float) * m->n_vocab, cudaMemcpyDeviceToHost, m->st), "logits");
+    ECHK(cudaStreamSynchronize(m->st), "model_logits");
+    return check_dev_err();
+}
+
+int gtn_model_generate(gtn_model* m, const int32_t* prompt, int n_prompt, int n_gen, int32_t* out_tokens) {
+    if (!m || !m->loaded || !prompt || !out_tokens || n_prompt <= 0 || n_gen <= 0)
+        return fail(GTN_ERR_ARG, "model_generate: arguments");
+    if (n_prompt + n_gen - 1 > m->max_ctx) return fail(GTN_ERR_ARG, "model_generate: exceeds max_ctx");
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= m->n_vocab) return fail(GTN_ERR_ARG, "model_generate: token id %d", prompt[i]);
+    ECHK(cudaMemcpyAsync(m->tok, prompt, sizeof(int32_t) * n_prompt, cudaMemcpyHostToDevice, m->st), "prompt");
+    int n = n_prompt;
+    for (int i = 0; i < n_gen; ++i) {
+        const int rc = forward(m, 0, n, i == 0 ? 0 : n - 1);
+        if (rc != GTN_OK) return rc;
+        // the sampled id becomes the next input token on the device (sampler.cpp:206)
+        if (i + 1 < n_gen)
+            ECHK(cudaMemcpyAsync(m->tok + n, m->next, sizeof(int32_t), cudaMemcpyDeviceToDevice, m->st), "next");
+        ECHK(cudaMemcpyAsync(out_tokens + i, m->next, sizeof(int32_t), cudaMemcpyDeviceToHost, m->st), "out");
+        ++n;
+    }
+    ECHK(cudaStreamSynchronize(m->st), "model_generate");
+    return check_dev_err();
+}
+
+}  // extern "C"

@@ -1,0 +1,56 @@
+// Host-side launch helpers shared by the op-level ABI and the model engine.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "matmul.cuh"
+#include "rowops.cuh"
+
+namespace gtn {
+
+void set_error(const std::string& msg);
+int fail(int code, const char* fmt, ...);
+
+// Launches `kern` with programmatic dependent launch enabled (the kernel may start while the
+// previous kernel in the stream finishes; it calls griddepcontrol.wait before reading its inputs).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+template <typename K>
+inline cudaError_t ensure_smem(K kern, size_t smem) {
+    if (smem <= 48 * 1024) return cudaSuccess;
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
+// Device error word written by kernels whose bounded waits expired (GTN_DEVERR_*).
+unsigned int* device_error_word();
+// Reads and clears the device error word (synchronous).
+unsigned int take_device_error();
+
+// fp32 matmul core used by both layers: Y[M, N] (row stride ldy floats) = X[M, K] . W[N, K]^T.
+// xdt/wdt: (Q8, Q8), (Q8, Q4) or (F16, F16). Returns a cudaError_t.
+cudaError_t matmul_f32(const uint8_t* X, long x_stride, int xdt, int M, const uint8_t* W, long w_stride, int wdt,
+                       int N, int K, float* Y, long ldy, cudaStream_t st);
+
+// Host table of (cos, sin) for positions [0, npos) and j < rd/2, as rotary_emb_impl computes them
+// (ops.cpp:791-812): theta = m * powf(10000, -((2j)/rd)), then cosf / sinf.
+std::vector<float2> rope_table_host(int npos, int rd);
+
+}  // namespace gtn

@@ -1,0 +1,329 @@
+// Exact (reference-order) matmul kernels: Y[m, n] = dot(X[m, :], W[n, :]) in fp32.
+//
+// Reference: ops.cpp:579-636 matmul_2d_impl, with the dot products of ops.cpp:208-523.
+// The reference's AVX build accumulates
+//   * Q8 x Q8 and Q8 x Q4 (ops.cpp:292-490) in 4 fp32 lanes: lane l owns elements
+//     {c+2l, c+2l+1 : c in {0,8,16,24}} of each 32-element block; per block the exact int32 lane
+//     sum is converted to fp32, multiplied by fp16(da)*fp16(dw) and added to the lane, blocks in
+//     order; the result is (L0+L1)+(L2+L3);
+//   * fp16 x fp16 (ops.cpp:208-242) in 8 fp32 lanes over elements 8i+l (products are exact in
+//     fp32), lanes summed left to right, then the scalar tail.
+// Here one thread owns one (output row, lane) accumulator, so the per-lane chains keep exactly
+// that order and the results are bit-identical. Integer lane sums use dp4a on the lane's 8
+// bytes (2 words); Q4 nibbles are unpacked with shifts/masks and the +7 bias is removed with the
+// activation lane sum (sum((q-7)*a) = sum(q*a) - 7*sum(a), exact in int32).
+//
+// Weight streaming: W rows are read with 1-D TMA bulk copies (cp.async.bulk) into a 4-stage
+// shared-memory ring per CTA, one copy per row per K tile, completion on an mbarrier (waits are
+// bounded). Activations are prepared once per CTA in shared memory in lane order.
+#pragma once
+#include "common.cuh"
+
+namespace gtn {
+
+constexpr int MM_STAGES = 4;
+
+// After an aborted pipeline: wait (bounded again) for copies that may still be in flight into this
+// CTA's shared memory before it exits. Stage s has an outstanding phase for the last tile issued to it.
+__device__ __forceinline__ void drain_stages(uint64_t* bars, int nkt, int tid) {
+    if (tid != 0) return;
+    for (int s = 0; s < MM_STAGES && s < nkt; ++s) {
+        const int last = s + ((nkt - 1 - s) / MM_STAGES) * MM_STAGES;
+        for (uint32_t it = 0; it < GTN_WAIT_LIMIT; ++it)
+            if (mbar_try_wait(&bars[s], (last / MM_STAGES) & 1)) break;
+    }
+}
+
+// Per (activation row, block, lane): the lane's 8 activation int8 in two words ordered like the
+// weight words below, their sum (for the Q4 bias), and fp16(da) as float.
+struct __align__(16) LanePrep {
+    int a0, a1, s;
+    float da;
+};
+
+// Builds LanePrep for rows [m0, m0+mt) of a Q8 activation matrix; all threads of the CTA.
+__device__ __forceinline__ void build_prep_q8(const uint8_t* X, long x_stride, int m0, int mt, int nb,
+                                              LanePrep* prep) {
+    const int total = mt * nb * 4;
+    for (int i = threadIdx.x; i < total; i += blockDim.x) {
+        const int l = i & 3, b = (i >> 2) % nb, m = (i >> 2) / nb;
+        const uint8_t* blk = X + (long)(m0 + m) * x_stride + (long)b * GTN_Q8_BYTES;
+        const int8_t* q = reinterpret_cast<const int8_t*>(blk + 2);
+        const int e0 = q[2 * l], e1 = q[2 * l + 1], e2 = q[8 + 2 * l], e3 = q[9 + 2 * l];
+        const int e4 = q[16 + 2 * l], e5 = q[17 + 2 * l], e6 = q[24 + 2 * l], e7 = q[25 + 2 * l];
+        LanePrep p;
+        p.a0 = (e0 & 255) | ((e1 & 255) << 8) | ((e2 & 255) << 16) | ((e3 & 255) << 24);
+        p.a1 = (e4 & 255) | ((e5 & 255) << 8) | ((e6 & 255) << 16) | ((e7 & 255) << 24);
+        p.s = e0 + e1 + e2 + e3 + e4 + e5 + e6 + e7;
+        p.da = h2f(ld_u16(blk));
+        prep[i] = p;
+    }
+}
+
+// Weight lane words of one Q8 block (34 bytes at p): bytes {2l,2l+1,8+2l,9+2l} and
+// {16+2l,17+2l,24+2l,25+2l} of the data. All 16-bit loads are aligned (block starts are even).
+__device__ __forceinline__ int q8_block_lane_dot(const uint8_t* p, int l, const LanePrep& a) {
+    const uint8_t* d = p + 2;
+    const int w0 = (int)ld_u16(d + 2 * l) | ((int)ld_u16(d + 8 + 2 * l) << 16);
+    const int w1 = (int)ld_u16(d + 16 + 2 * l) | ((int)ld_u16(d + 24 + 2 * l) << 16);
+    return dp4a(w0, a.a0, dp4a(w1, a.a1, 0));
+}
+// Q4 block (18 bytes at p): byte j = (q[j] << 4) | q[j+16]; lane l's 8 weights are the high and low
+// nibbles of bytes {2l, 2l+1, 8+2l, 9+2l}.
+__device__ __forceinline__ int q4_block_lane_dot(const uint8_t* p, int l, const LanePrep& a) {
+    const uint8_t* d = p + 2;
+    const int wb = (int)ld_u16(d + 2 * l) | ((int)ld_u16(d + 8 + 2 * l) << 16);
+    const int hi = (wb >> 4) & 0x0f0f0f0f, lo = wb & 0x0f0f0f0f;
+    return dp4a(hi, a.a0, dp4a(lo, a.a1, 0)) - 7 * a.s;
+}
+
+template <int WDT>
+struct MMCfg;
+template <>
+struct MMCfg<GTN_Q8> {
+    static constexpr int LANES = 4, BLK_BYTES = GTN_Q8_BYTES, KT_BLOCKS = 16;
+};
+template <>
+struct MMCfg<GTN_Q4> {
+    static constexpr int LANES = 4, BLK_BYTES = GTN_Q4_BYTES, KT_BLOCKS = 32;
+};
+
+// Shared memory bytes of k_mm_q for (NW warps, MT activation rows, K).
+template <int WDT>
+__host__ __device__ inline int mm_q_tile_stride() {
+    return ((MMCfg<WDT>::KT_BLOCKS * MMCfg<WDT>::BLK_BYTES + 15) / 16) * 16 + 16;
+}
+template <int WDT>
+__host__ __device__ inline size_t mm_q_smem(int nw, int mt, int K) {
+    const int rows = nw * 8;
+    const int nb = K / GTN_QBLK;
+    return 128 + (size_t)MM_STAGES * rows * mm_q_tile_stride<WDT>() + (size_t)mt * nb * 4 * sizeof(LanePrep);
+}
+
+// Q8/Q4 weights x Q8 activations. grid.x = ceil(N / (8*NW)), grid.y = ceil(M / MT).
+// W: row stride w_stride bytes (any alignment: copies start at the 16-byte boundary below the
+// row tile and the tile is read at the remainder; the allocation must extend 16 bytes past the
+// last row unless rows and tiles are 16-byte multiples). X: Q8 rows, stride x_stride bytes.
+// Y: fp32, row stride y_stride elements.
+template <int WDT, int NW, int MT>
+__global__ void __launch_bounds__(NW * 32) k_mm_q(const uint8_t* __restrict__ W, long w_stride, int N, int K,
+                                                  const uint8_t* __restrict__ X, long x_stride, int M,
+                                                  float* __restrict__ Y, long y_stride, unsigned int* err) {
+    using C = MMCfg<WDT>;
+    constexpr int ROWS = NW * 8;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int abort_flag;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+    const int tstride = mm_q_tile_stride<WDT>();
+    uint8_t* stages = smem + 128;
+    const int nb = K / GTN_QBLK;
+    LanePrep* prep = reinterpret_cast<LanePrep*>(stages + (size_t)MM_STAGES * ROWS * tstride);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int r_local = warp * 8 + (lane >> 2), l = lane & 3;
+    const int row0 = blockIdx.x * ROWS;
+    const int nrows = min(ROWS, N - row0);
+    const int m0 = blockIdx.y * MT;
+    const int mt = min(MT, M - m0);
+    const int nkt = (nb + C::KT_BLOCKS - 1) / C::KT_BLOCKS;
+
+    auto issue = [&](int kt) {
+        // warp 0: lane 0 arms the stage barrier, then lane r copies row r's tile.
+        const int s = kt % MM_STAGES;
+        const int b0 = kt * C::KT_BLOCKS;
+        const int nbt = min(C::KT_BLOCKS, nb - b0);
+        uint32_t total = 0;
+        for (int r = 0; r < nrows; ++r) {
+            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + r) * w_stride +
+                                  (uintptr_t)b0 * C::BLK_BYTES;
+            const uint32_t off = (uint32_t)(src & 15);
+            total += (off + nbt * C::BLK_BYTES + 15) & ~15u;
+        }
+        if (lane == 0) mbar_arrive_expect_tx(&bars[s], total);
+        __syncwarp();
+        for (int r = lane; r < nrows; r += 32) {
+            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + r) * w_stride +
+                                  (uintptr_t)b0 * C::BLK_BYTES;
+            const uint32_t off = (uint32_t)(src & 15);
+            const uint32_t bytes = (off + nbt * C::BLK_BYTES + 15) & ~15u;
+            bulk_g2s(stages + ((size_t)s * ROWS + r) * tstride, reinterpret_cast<const void*>(src - off), bytes,
+                     &bars[s]);
+        }
+    };
+
+    if (tid == 0) {
+        for (int s = 0; s < MM_STAGES; ++s) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+    if (warp == 0)
+        for (int kt = 0; kt < min(MM_STAGES, nkt); ++kt) issue(kt);
+
+    // Weights do not depend on the previous kernel; activations do (programmatic dependent launch).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    build_prep_q8(X, x_stride, m0, mt, nb, prep);
+    __syncthreads();
+
+    float acc[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+    for (int kt = 0; kt < nkt; ++kt) {
+        const int s = kt % MM_STAGES;
+        // A timed-out wait marks the CTA aborted; every thread still reaches each barrier.
+        if (!abort_flag && !mbar_wait_bounded(&bars[s], (kt / MM_STAGES) & 1, err)) abort_flag = 1;
+        const int b0 = kt * C::KT_BLOCKS;
+        const int nbt = min(C::KT_BLOCKS, nb - b0);
+        if (!abort_flag && r_local < nrows) {
+            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + r_local) * w_stride +
+                                  (uintptr_t)b0 * C::BLK_BYTES;
+            const uint8_t* t = stages + ((size_t)s * ROWS + r_local) * tstride + (src & 15);
+            for (int b = 0; b < nbt; ++b) {
+                const uint8_t* p = t + b * C::BLK_BYTES;
+                const float dw = h2f(ld_u16(p));
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    if (m < mt) {
+                        const LanePrep a = prep[((size_t)m * nb + b0 + b) * 4 + l];
+                        const int L = WDT == GTN_Q8 ? q8_block_lane_dot(p, l, a) : q4_block_lane_dot(p, l, a);
+                        const float sc = a.da * dw;
+                        const float pr = (float)L * sc;
+                        acc[m] = acc[m] + pr;
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (warp == 0 && !abort_flag && kt + MM_STAGES < nkt) issue(kt + MM_STAGES);
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (abort_flag) {
+        drain_stages(bars, nkt, tid);
+        return;
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        const float t01 = acc[m] + __shfl_xor_sync(0xffffffffu, acc[m], 1);
+        const float t = t01 + __shfl_xor_sync(0xffffffffu, t01, 2);
+        if (l == 0 && r_local < nrows && m < mt) Y[(long)(m0 + m) * y_stride + row0 + r_local] = t;
+    }
+}
+
+// fp16 weights x fp16 activations, 8 lanes per row: CTA = NW warps x 4 rows.
+constexpr int MM_F16_KT = 256;  // elements per K tile (512 bytes per row)
+__host__ __device__ inline int mm_f16_tile_stride() { return MM_F16_KT * 2 + 16; }
+__host__ __device__ inline size_t mm_f16_smem(int nw, int mt, int K) {
+    return 128 + (size_t)MM_STAGES * nw * 4 * mm_f16_tile_stride() + (size_t)mt * K * 2 + 16;
+}
+
+template <int NW, int MT>
+__global__ void __launch_bounds__(NW * 32) k_mm_f16(const uint8_t* __restrict__ W, long w_stride, int N, int K,
+                                                    const uint8_t* __restrict__ X, long x_stride, int M,
+                                                    float* __restrict__ Y, long y_stride, unsigned int* err) {
+    constexpr int ROWS = NW * 4;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int abort_flag;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+    const int tstride = mm_f16_tile_stride();
+    uint8_t* stages = smem + 128;
+    uint16_t* xs = reinterpret_cast<uint16_t*>(stages + (size_t)MM_STAGES * ROWS * tstride);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int r_local = warp * 4 + (lane >> 3), l = lane & 7;
+    const int row0 = blockIdx.x * ROWS;
+    const int nrows = min(ROWS, N - row0);
+    const int m0 = blockIdx.y * MT;
+    const int mt = min(MT, M - m0);
+    const int K8 = (K / 8) * 8;
+    const int nkt = (K8 + MM_F16_KT - 1) / MM_F16_KT;
+
+    auto issue = [&](int kt) {
+        const int s = kt % MM_STAGES;
+        const int e0 = kt * MM_F16_KT;
+        const int ne = min(MM_F16_KT, K8 - e0);
+        uint32_t total = 0;
+        for (int r = 0; r < nrows; ++r) {
+            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + r) * w_stride + (uintptr_t)e0 * 2;
+            total += ((uint32_t)(src & 15) + ne * 2 + 15) & ~15u;
+        }
+        if (lane == 0) mbar_arrive_expect_tx(&bars[s], total);
+        __syncwarp();
+        for (int r = lane; r < nrows; r += 32) {
+            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + r) * w_stride + (uintptr_t)e0 * 2;
+            const uint32_t off = (uint32_t)(src & 15);
+            bulk_g2s(stages + ((size_t)s * ROWS + r) * tstride, reinterpret_cast<const void*>(src - off),
+                     (off + ne * 2 + 15) & ~15u, &bars[s]);
+        }
+    };
+
+    if (tid == 0) {
+        for (int s = 0; s < MM_STAGES; ++s) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+    if (warp == 0)
+        for (int kt = 0; kt < min(MM_STAGES, nkt); ++kt) issue(kt);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    for (int i = tid; i < mt * K; i += blockDim.x) {
+        const int m = i / K, k = i % K;
+        xs[i] = reinterpret_cast<const uint16_t*>(X + (long)(m0 + m) * x_stride)[k];
+    }
+    __syncthreads();
+
+    float acc[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+    for (int kt = 0; kt < nkt; ++kt) {
+        const int s = kt % MM_STAGES;
+        if (!abort_flag && !mbar_wait_bounded(&bars[s], (kt / MM_STAGES) & 1, err)) abort_flag = 1;
+        const int e0 = kt * MM_F16_KT;
+        const int ne = min(MM_F16_KT, K8 - e0);
+        if (!abort_flag && r_local < nrows) {
+            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + r_local) * w_stride + (uintptr_t)e0 * 2;
+            const uint16_t* t = reinterpret_cast<const uint16_t*>(stages + ((size_t)s * ROWS + r_local) * tstride + (src & 15));
+            for (int i = l; i < ne; i += 8) {
+                const float w = h2f(t[i]);
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    if (m < mt) {
+                        const float pr = h2f(xs[m * K + e0 + i]) * w;
+                        acc[m] = pr + acc[m];
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (warp == 0 && !abort_flag && kt + MM_STAGES < nkt) issue(kt + MM_STAGES);
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (abort_flag) {
+        drain_stages(bars, nkt, tid);
+        return;
+    }
+    // lanes summed left to right (simd_ops.h:75-78), then the scalar tail (ops.cpp:224-228).
+    const int base = lane & ~7;
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __shfl_sync(0xffffffffu, acc[m], base + j);
+        if (l == 0 && r_local < nrows && m < mt) {
+            float d = v[0] + v[1];
+            d = d + v[2];
+            d = d + v[3];
+            d = d + v[4];
+            d = d + v[5];
+            d = d + v[6];
+            d = d + v[7];
+            const uint16_t* wr = reinterpret_cast<const uint16_t*>(W + (long)(row0 + r_local) * w_stride);
+            for (int k = K8; k < K; ++k) {
+                const float pr = h2f(xs[m * K + k]) * h2f(wr[k]);
+                d = d + pr;
+            }
+            Y[(long)(m0 + m) * y_stride + row0 + r_local] = d;
+        }
+    }
+}
+
+}  // namespace gtn
