@@ -110,9 +110,42 @@ static cudaError_t launch_mm_f16(const uint8_t* X, long xs, int M, const uint8_t
 #undef GTN_MMF
 }
 
+template <int WDT>
+static cudaError_t launch_plain(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int row0, int nrows,
+                                int K, float* Y, long ldy, cudaStream_t st) {
+    return launch_pdl(k_mm_rows_plain<WDT>, dim3(nrows, M), dim3(32), 0, st, W, ws, row0, K, X, xs, Y, ldy);
+}
+
+static cudaError_t matmul_tma(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K,
+                              float* Y, long ldy, cudaStream_t st);
+
 cudaError_t matmul_f32(const uint8_t* X, long xs, int xdt, int M, const uint8_t* W, long ws, int wdt, int N, int K,
-                       float* Y, long ldy, cudaStream_t st) {
+                       float* Y, long ldy, cudaStream_t st, bool padded) {
     (void)xdt;
+    auto plain = [&](int row0, int nrows) -> cudaError_t {
+        if (wdt == GTN_Q8) return launch_plain<GTN_Q8>(X, xs, M, W, ws, row0, nrows, K, Y, ldy, st);
+        if (wdt == GTN_Q4) return launch_plain<GTN_Q4>(X, xs, M, W, ws, row0, nrows, K, Y, ldy, st);
+        return launch_plain<GTN_F16>(X, xs, M, W, ws, row0, nrows, K, Y, ldy, st);
+    };
+    if (!padded) {
+        if (((uintptr_t)W & 15) != 0) return plain(0, N);
+        // bytes the TMA tiles cover in the last row: whole blocks (Q) or the first K/8*8 halves (fp16)
+        const long covered = wdt == GTN_F16 ? (long)(K / 8) * 16 : row_bytes(wdt, K);
+        const uintptr_t end = (uintptr_t)W + (uintptr_t)(N - 1) * ws + covered;
+        if ((end & 15) != 0 || (ws & 15) != 0) {
+            // every row but the last reads at most into the following row; the last row goes plain
+            if (N > 1) {
+                const cudaError_t e = matmul_tma(X, xs, M, W, ws, wdt, N - 1, K, Y, ldy, st);
+                if (e != cudaSuccess) return e;
+            }
+            return plain(N - 1, 1);
+        }
+    }
+    return matmul_tma(X, xs, M, W, ws, wdt, N, K, Y, ldy, st);
+}
+
+static cudaError_t matmul_tma(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K,
+                              float* Y, long ldy, cudaStream_t st) {
     const int mt = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
     if (wdt == GTN_F16) {
         int nw = 4;
@@ -290,13 +323,13 @@ int gtn_matmul_2d(const gtn_tensor* x, const gtn_tensor* w, gtn_tensor* out, int
     if (out->dtype == GTN_F32) {
         float* Y = (float*)((uint8_t*)out->data + (long)start_pos * os);
         return cuda_status(matmul_f32(X, bstride(x, 0), x->dtype, M, (const uint8_t*)w->data, bstride(w, 0),
-                                      w->dtype, N, K, Y, out->ndim == 1 ? 0 : N, st),
+                                      w->dtype, N, K, Y, out->ndim == 1 ? 0 : N, st, false),
                            "matmul_2d");
     }
     float* Y = nullptr;
     GTN_CHECK(cuda_status(cudaMallocAsync((void**)&Y, sizeof(float) * (size_t)M * N, st), "matmul_2d scratch"));
     cudaError_t e = matmul_f32(X, bstride(x, 0), x->dtype, M, (const uint8_t*)w->data, bstride(w, 0), w->dtype, N,
-                               K, Y, N, st);
+                               K, Y, N, st, false);
     if (e == cudaSuccess)
         e = launch_pdl(k_write_rows, dim3(((N + GTN_QBLK - 1) / GTN_QBLK + 3) / 4, M), dim3(128), 0, st,
                        (const float*)Y, (long)N, (uint8_t*)out->data, os, (int)out->dtype, N, start_pos);

@@ -46,8 +46,11 @@ unsigned int take_device_error();
 
 // fp32 matmul core used by both layers: Y[M, N] (row stride ldy floats) = X[M, K] . W[N, K]^T.
 // xdt/wdt: (Q8, Q8), (Q8, Q4) or (F16, F16). Returns a cudaError_t.
+// `padded`: W is 16-byte aligned and its allocation extends at least 16 bytes past the last row
+// (the engine's arena guarantees it). Otherwise rows whose TMA tiles could leave the buffer are
+// computed by the plain-load kernel, so no byte outside W is ever read.
 cudaError_t matmul_f32(const uint8_t* X, long x_stride, int xdt, int M, const uint8_t* W, long w_stride, int wdt,
-                       int N, int K, float* Y, long ldy, cudaStream_t st);
+                       int N, int K, float* Y, long ldy, cudaStream_t st, bool padded = true);
 
 // Host table of (cos, sin) for positions [0, npos) and j < rd/2, as rotary_emb_impl computes them
 // (ops.cpp:791-812): theta = m * powf(10000, -((2j)/rd)), then cosf / sinf.

@@ -326,4 +326,73 @@ __global__ void __launch_bounds__(NW * 32) k_mm_f16(const uint8_t* __restrict__ 
     }
 }
 
+// Plain-load variant for rows whose TMA tiles could reach outside the caller's weight buffer (an
+// unaligned base, or a last row that does not end on a 16-byte boundary). One warp per
+// (row, activation row): lanes 0..3 (Q8/Q4) or 0..7 (fp16) run the reference's lane chains with
+// the same arithmetic as k_mm_q / k_mm_f16. grid (rows, M); block 32.
+template <int WDT>
+__global__ void k_mm_rows_plain(const uint8_t* __restrict__ W, long w_stride, int row0, int K,
+                                const uint8_t* __restrict__ X, long x_stride, float* __restrict__ Y, long y_stride) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int row = row0 + blockIdx.x, m = blockIdx.y, l = threadIdx.x;
+    const uint8_t* wr = W + (long)row * w_stride;
+    const uint8_t* xr = X + (long)m * x_stride;
+    float acc = 0.0f;
+    if (WDT == GTN_F16) {
+        const int K8 = (K / 8) * 8;
+        if (l < 8) {
+            for (int i = l; i < K8; i += 8) {
+                const uint16_t wv = (uint16_t)(wr[2 * i] | (wr[2 * i + 1] << 8));
+                const uint16_t xv = (uint16_t)(xr[2 * i] | (xr[2 * i + 1] << 8));
+                const float pr = h2f(xv) * h2f(wv);
+                acc = pr + acc;
+            }
+        }
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __shfl_sync(0xffffffffu, acc, j);
+        if (l == 0) {
+            float d = v[0] + v[1];
+            for (int j = 2; j < 8; ++j) d = d + v[j];
+            for (int k = K8; k < K; ++k) {
+                const uint16_t wv = (uint16_t)(wr[2 * k] | (wr[2 * k + 1] << 8));
+                const uint16_t xv = (uint16_t)(xr[2 * k] | (xr[2 * k + 1] << 8));
+                const float pr = h2f(xv) * h2f(wv);
+                d = d + pr;
+            }
+            Y[(long)m * y_stride + row] = d;
+        }
+        return;
+    }
+    constexpr int BB = WDT == GTN_Q8 ? GTN_Q8_BYTES : GTN_Q4_BYTES;
+    if (l < 4) {
+        for (int b = 0; b < K / GTN_QBLK; ++b) {
+            const uint8_t* xb = xr + (long)b * GTN_Q8_BYTES;
+            const uint8_t* wb = wr + (long)b * BB;
+            const int8_t* xq = reinterpret_cast<const int8_t*>(xb + 2);
+            int L = 0;
+            for (int c = 0; c < GTN_QBLK; c += 8) {
+                for (int e = c + 2 * l; e < c + 2 * l + 2; ++e) {
+                    int wv;
+                    if (WDT == GTN_Q8) {
+                        wv = (int)(int8_t)wb[2 + e];
+                    } else {
+                        const uint8_t p = wb[2 + (e & 15)];
+                        wv = (e < 16 ? (p >> 4) : (p & 15)) - 7;
+                    }
+                    L += (int)xq[e] * wv;
+                }
+            }
+            const float da = h2f((uint16_t)(xb[0] | (xb[1] << 8)));
+            const float dw = h2f((uint16_t)(wb[0] | (wb[1] << 8)));
+            const float sc = da * dw;
+            const float pr = (float)L * sc;
+            acc = acc + pr;
+        }
+    }
+    const float t01 = acc + __shfl_xor_sync(0xffffffffu, acc, 1);
+    const float t = t01 + __shfl_xor_sync(0xffffffffu, t01, 2);
+    if (l == 0) Y[(long)m * y_stride + row] = t;
+}
+
 }  // namespace gtn

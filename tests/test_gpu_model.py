@@ -1,0 +1,91 @@
+"""Model-level GPU parity: the engine (gtn_model_*) against the oracle's model wiring on small
+custom architectures of each family (bit-exact logits and greedy tokens), and against the
+reference's own greedy tokens on full-size TinyLlama (committed golden tokens; the live compiled
+reference too where it is present)."""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import gten_b200 as G
+from gten_b200 import gtenfile
+from helpers import F16, Q4, Q8
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def cpu_pack(orc):
+    def pack(w, dt):
+        return orc.pack_q8(w.numpy()) if dt == Q8 else orc.pack_q4(w.numpy())
+    return pack
+
+
+CUSTOM = {
+    "llama": [1000, 256, 2, 4, 2, 512, 0],
+    "zephyr": [777, 192, 2, 3, 3, 320, 1],
+    "minicpm": [900, 128, 3, 2, 2, 288, 2],
+}
+
+
+@pytest.mark.parametrize("name", list(CUSTOM))
+@pytest.mark.parametrize("wdt", [Q8, Q4, F16])
+def test_custom_model_matches_oracle(orc, gpu, name, wdt):
+    from oracle.oracle import OracleModel
+    dims = CUSTOM[name]
+    img = gtenfile.synthetic_image(6, wdt, 99, cpu_pack(orc), dims=dims, std=0.05, gain_std=0.1)
+    n_prompt, n_gen = 21, 12
+    max_ctx = 2 * (n_prompt + n_gen)  # keeps the reference's qk rows apart (fp16 needs 2x)
+    prompt = np.random.default_rng(5).integers(0, dims[0], n_prompt).astype(np.int32)
+    om = OracleModel(orc, 6, wdt, max_ctx, img, dims=dims)
+    m = G.Model(G.CUSTOM, wdt, max_ctx, dims=dims)
+    m.load(img)
+    # prefill logits, then one decode step
+    assert np.array_equal(m.logits(prompt, 0), om.logits(prompt, 0))
+    p2 = np.concatenate([prompt, [7]]).astype(np.int32)
+    assert np.array_equal(m.logits(p2, n_prompt), om.logits(p2, n_prompt))
+    # greedy decode from scratch
+    om2 = OracleModel(orc, 6, wdt, max_ctx, img, dims=dims)
+    assert np.array_equal(m.generate(prompt, n_gen), om2.greedy(prompt, n_gen))
+    m.close()
+
+
+def test_load_rejects_bad_images(orc, gpu):
+    dims = CUSTOM["llama"]
+    img = gtenfile.synthetic_image(6, Q8, 1, cpu_pack(orc), dims=dims)
+    m = G.Model(G.CUSTOM, Q8, 16, dims=dims)
+    bad = img.copy()
+    bad[0] ^= 1
+    with pytest.raises(G.GtenError, match="status 4"):
+        m.load(bad)
+    with pytest.raises(G.GtenError, match="status 4"):
+        m.load(img[: img.size // 2])
+    with pytest.raises(G.GtenError, match="status 1"):
+        m.generate(np.array([1, 2, 3], np.int32), 2)  # not loaded yet
+    m.load(img)
+    with pytest.raises(G.GtenError, match="status 1"):
+        m.generate(np.array([dims[0]], np.int32), 1)  # token id out of range
+    m.close()
+
+
+GOLDEN = os.path.join(HERE, "golden", "greedy_tokens.json")
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("wdt", [Q8, Q4])
+def test_tinyllama_greedy_matches_reference(orc, gpu, wdt):
+    """Full-size TinyLlama, seeded N(0, 0.02) weights, 64-token prompt, 64 greedy tokens: the ids
+    must equal the reference CPU build's (tests/golden/greedy_tokens.json, made by
+    tests/golden/make_golden.py with the compiled reference)."""
+    with open(GOLDEN) as f:
+        gold = json.load(f)
+    case = gold[f"tinyllama_w{wdt}"]
+    img = gtenfile.synthetic_image(0, wdt, case["seed"], gtenfile.cuda_packer())
+    prompt = np.array(case["prompt"], np.int32)
+    m = G.Model(G.TINYLLAMA, wdt, case["n_ctx"])
+    m.load(img)
+    got = m.generate(prompt, len(case["tokens"]))
+    assert got.tolist() == case["tokens"]
+    m.close()

@@ -1,0 +1,214 @@
+"""GPU parity of every gten op (C-ABI, sm_100a kernels) against the CPU oracle, bit for bit.
+
+Each case builds seeded inputs in the reference formats, runs the op through
+lib/libgten_b200.so and compares the output bytes with the oracle's restatement of the
+reference (oracle/gten_oracle.c), which is itself pinned to the compiled reference."""
+import numpy as np
+import pytest
+import torch
+
+import gten_b200 as G
+from helpers import F16, F32, I32, Q4, Q8, act_rows, fp16_vec, from_dev, row_bytes, to_dev, weights
+
+pytestmark = pytest.mark.gpu
+
+
+def dev_out(nbytes, device, fill=None):
+    t = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+    if fill is not None:
+        t.copy_(to_dev(fill, device))
+    return t
+
+
+@pytest.mark.parametrize("wdt", [Q8, Q4, F16])
+@pytest.mark.parametrize("M,K,N", [(1, 2048, 256), (1, 2048, 2048), (1, 5632, 2048), (3, 256, 96), (16, 2048, 64),
+                                   (9, 5760, 40), (64, 2304, 72), (1, 2048, 32003)])
+@pytest.mark.parametrize("odt_kind", ["act", "f32"])
+def test_matmul_2d(orc, gpu, wdt, M, K, N, odt_kind):
+    rng = np.random.default_rng(M * 1000 + K + N + wdt)
+    xdt = F16 if wdt == F16 else Q8
+    odt = xdt if odt_kind == "act" else F32
+    x = act_rows(orc, rng, xdt, M, K)
+    w = weights(orc, rng, wdt, N, K)
+    for sp in sorted({0, M - 1}):
+        want = orc.matmul_2d(x, xdt, M, K, w, wdt, N, odt, start_pos=sp)
+        out = dev_out(row_bytes(odt, N) * M, gpu)
+        G.matmul_2d(G.GT(to_dev(x, gpu), xdt, (M, K)), G.GT(to_dev(w, gpu), wdt, (N, K)),
+                    G.GT(out, odt, (M, N)), start_pos=sp)
+        got = from_dev(out)
+        rb = row_bytes(odt, N)
+        assert np.array_equal(got[sp * rb:], want[sp * rb:]), f"start_pos={sp}"
+
+
+@pytest.mark.parametrize("wdt", [Q8, Q4, F16])
+def test_matmul_1d_logits(orc, gpu, wdt):
+    """EmbeddingLinear's stride-0 fp32 output (modules.cpp:111-122): last row only."""
+    rng = np.random.default_rng(7 + wdt)
+    xdt = F16 if wdt == F16 else Q8
+    M, K, N = 5, 2048, 1000
+    x = act_rows(orc, rng, xdt, M, K)
+    w = weights(orc, rng, wdt, N, K)
+    want = orc.matmul_2d(x, xdt, M, K, w, wdt, N, F32, start_pos=M - 1, out_1d=True)
+    out = dev_out(4 * N, gpu)
+    G.matmul_2d(G.GT(to_dev(x, gpu), xdt, (M, K)), G.GT(to_dev(w, gpu), wdt, (N, K)), G.GT(out, F32, (N,)),
+                start_pos=M - 1)
+    assert np.array_equal(from_dev(out), want)
+
+
+@pytest.mark.parametrize("dt", [Q8, F16])
+@pytest.mark.parametrize("n,sp,H,KVH", [(1, 0, 4, 4), (9, 0, 8, 2), (40, 39, 8, 2), (70, 69, 32, 4), (33, 0, 4, 1),
+                                        (300, 299, 32, 4), (257, 250, 36, 36), (1536, 1535, 16, 4)])
+def test_qkv_attn(orc, gpu, dt, n, sp, H, KVH):
+    rng = np.random.default_rng(n * 7 + H + dt)
+    q = act_rows(orc, rng, dt, n, H * 64)
+    k = act_rows(orc, rng, dt, n, KVH * 64)
+    v = act_rows(orc, rng, dt, n, KVH * 64)
+    want = orc.qkv_attn(q, k, v, dt, n, H, H * 64, KVH * 64, sp)
+    out = dev_out(row_bytes(dt, H * 64) * n, gpu)
+    G.qkv_attn(G.GT(to_dev(q, gpu), dt, (n, H * 64)), G.GT(to_dev(k, gpu), dt, (n, KVH * 64)),
+               G.GT(to_dev(v, gpu), dt, (n, KVH * 64)), None, G.GT(out, dt, (n, H * 64)), max_ctx=n, start_pos=sp)
+    rb = row_bytes(dt, H * 64)
+    assert np.array_equal(from_dev(out)[sp * rb:], want[sp * rb:])
+
+
+@pytest.mark.parametrize("dt", [Q8, F16])
+@pytest.mark.parametrize("D", [2048, 2304, 96])
+def test_norms(orc, gpu, dt, D):
+    rng = np.random.default_rng(D + dt)
+    M = 5
+    x = act_rows(orc, rng, dt, M, D)
+    w = fp16_vec(rng, D)
+    b = fp16_vec(rng, D, 0.0, 0.1)
+    rb = row_bytes(dt, D)
+    xin = G.GT(to_dev(x, gpu), dt, (M, D))
+    out = dev_out(rb * M, gpu)
+    G.rms_norm(xin, G.GT(to_dev(w, gpu), F16, (D,)), G.GT(out, dt, (M, D)), start_pos=1)
+    assert np.array_equal(from_dev(out)[rb:], orc.rms_norm(x, dt, M, D, w, 1)[rb:])
+    out = dev_out(rb * M, gpu)
+    G.layer_norm(xin, G.GT(to_dev(w, gpu), F16, (D,)), G.GT(to_dev(b, gpu), F16, (D,)), G.GT(out, dt, (M, D)),
+                 start_pos=1)
+    assert np.array_equal(from_dev(out)[rb:], orc.layer_norm(x, dt, M, D, w, b, 1)[rb:])
+
+
+@pytest.mark.parametrize("dt", [Q8, F16])
+def test_rms_norm_3d(orc, gpu, dt):
+    rng = np.random.default_rng(3 + dt)
+    M, Hh, dh = 4, 20, 64
+    x = act_rows(orc, rng, dt, M, Hh * dh)
+    w = fp16_vec(rng, dh)
+    out = dev_out(row_bytes(dt, Hh * dh) * M, gpu)
+    G.rms_norm(G.GT(to_dev(x, gpu), dt, (M, Hh, dh)), G.GT(to_dev(w, gpu), F16, (dh,)), G.GT(out, dt, (M, Hh * dh)))
+    assert np.array_equal(from_dev(out), orc.rms_norm_3d(x, dt, M, Hh, dh, w, 0))
+
+
+@pytest.mark.parametrize("dt", [Q8, F16])
+@pytest.mark.parametrize("pct", [1.0, 0.25])
+@pytest.mark.parametrize("M,sp", [(5, 2), (1, 0), (700, 690)])
+def test_rotary_emb(orc, gpu, dt, pct, M, sp):
+    rng = np.random.default_rng(M + int(pct * 4) + dt)
+    D = 2048
+    x = act_rows(orc, rng, dt, M, D)
+    want = orc.rotary_emb(x, dt, M, D, 64, pct, sp)
+    buf = to_dev(x, gpu)
+    G.rotary_emb(G.GT(buf, dt, (M, D)), G.GT(buf, dt, (M, D)), 64, pct, start_pos=sp)
+    rb = row_bytes(dt, D)
+    assert np.array_equal(from_dev(buf)[sp * rb:], want[sp * rb:])
+
+
+@pytest.mark.parametrize("dt", [Q8, F16])
+@pytest.mark.parametrize("D", [5632, 5760, 2048, 70])
+def test_elementwise(orc, gpu, dt, D):
+    rng = np.random.default_rng(D + 11 * dt)
+    M = 3
+    rb = row_bytes(dt, D)
+    x = act_rows(orc, rng, dt, M, D, 3.0)
+    y = act_rows(orc, rng, dt, M, D)
+    bias = fp16_vec(rng, D, 0.0, 0.5)
+
+    def run(fn, *args, out=None):
+        return from_dev(out)
+
+    # silu (out of place)
+    out = dev_out(rb * M, gpu)
+    G.silu(G.GT(to_dev(x, gpu), dt, (M, D)), G.GT(out, dt, (M, D)), start_pos=1)
+    assert np.array_equal(from_dev(out)[rb:], orc.silu(x, dt, M, D, 1)[rb:])
+    # silu_inplace
+    buf = to_dev(x, gpu)
+    G.silu_inplace(G.GT(buf, dt, (M, D)))
+    assert np.array_equal(from_dev(buf), orc.silu(x, dt, M, D, 0))
+    # multiply / add
+    out = dev_out(rb * M, gpu)
+    G.multiply(G.GT(to_dev(x, gpu), dt, (M, D)), G.GT(to_dev(y, gpu), dt, (M, D)), G.GT(out, dt, (M, D)))
+    assert np.array_equal(from_dev(out), orc.multiply(x, y, dt, M, D))
+    buf = to_dev(x, gpu)
+    G.multiply_inplace(G.GT(buf, dt, (M, D)), G.GT(to_dev(y, gpu), dt, (M, D)))
+    assert np.array_equal(from_dev(buf), orc.multiply(x, y, dt, M, D))
+    out = dev_out(rb * M, gpu)
+    G.add(G.GT(to_dev(x, gpu), dt, (M, D)), G.GT(to_dev(y, gpu), dt, (M, D)), G.GT(out, dt, (M, D)))
+    assert np.array_equal(from_dev(out), orc.add(x, y, dt, M, D))
+    # scale (minicpm's three constants) and bias
+    for s in (12.0, float(np.float32(1.4) / np.sqrt(40.0)), 1.0 / 9):
+        buf = to_dev(x, gpu)
+        G.scale(G.GT(buf, dt, (M, D)), s, start_pos=2)
+        assert np.array_equal(from_dev(buf), orc.scale(x, dt, M, D, s, 2))
+    buf = to_dev(x, gpu)
+    G.bias_add_inplace(G.GT(buf, dt, (M, D)), G.GT(to_dev(bias, gpu), F16, (D,)))
+    assert np.array_equal(from_dev(buf), orc.bias_add_inplace(x, dt, M, D, bias))
+
+
+@pytest.mark.parametrize("wdt", [Q8, Q4, F16])
+def test_token_embed(orc, gpu, wdt):
+    rng = np.random.default_rng(21 + wdt)
+    V, D = 300, 2304
+    w = weights(orc, rng, wdt, V, D)
+    toks = rng.integers(0, V, 9).astype(np.int32)
+    odt = F16 if wdt == F16 else Q8
+    out = dev_out(row_bytes(odt, D) * toks.size, gpu)
+    G.token_embed(G.GT(to_dev(w, gpu), wdt, (V, D)), G.GT(torch.from_numpy(toks).to(gpu), I32, (toks.size,)),
+                  G.GT(out, odt, (toks.size, D)), start_pos=2)
+    rb = row_bytes(odt, D)
+    assert np.array_equal(from_dev(out)[2 * rb:], orc.token_embed(w, wdt, V, D, toks, odt, 2)[2 * rb:])
+
+
+@pytest.mark.parametrize("rows,cols", [(37, 2048), (1, 32), (256, 5760)])
+def test_pack_and_quantize(orc, gpu, rows, cols):
+    rng = np.random.default_rng(rows + cols)
+    w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    w[0, :32] = 0.0                      # an all-zero block (delta 0)
+    w[-1, 32:64] = np.float32(0.5) * (np.arange(32) % 3 - 1)  # exact .5 ties after scaling
+    wd = torch.from_numpy(w).to(gpu)
+    for dt, packer, ref in ((Q8, G.pack_q8, orc.pack_q8), (Q4, G.pack_q4, orc.pack_q4)):
+        out = torch.zeros(rows * row_bytes(dt, cols), dtype=torch.uint8, device=gpu)
+        packer(wd, out)
+        assert np.array_equal(from_dev(out), ref(w))
+    # activation quantizer with a partial last block
+    x = (rng.standard_normal((rows, cols + 7)) * 3).astype(np.float32)
+    out = torch.zeros(rows * row_bytes(Q8, cols + 7), dtype=torch.uint8, device=gpu)
+    G.quantize_q8_rows(torch.from_numpy(x).to(gpu), out)
+    want = np.concatenate([orc.q8_quantize_row(x[i]) for i in range(rows)])
+    got = from_dev(out)
+    rb = row_bytes(Q8, cols + 7)
+    valid = np.ones(rb, bool)
+    valid[rb - 32 + 7:] = False  # bytes past the partial block's 7 values are unspecified
+    for i in range(rows):
+        assert np.array_equal(got[i * rb:(i + 1) * rb][valid], want[i * rb:(i + 1) * rb][valid])
+
+
+@pytest.mark.parametrize("n", [1, 32003, 100352, 122753])
+def test_argmax(orc, gpu, n):
+    rng = np.random.default_rng(n)
+    x = rng.standard_normal(n).astype(np.float32)
+    if n > 10:
+        x[[3, n // 2, n - 1]] = x.max() + 1.0  # ties: the first index wins (sampler.cpp:189-195)
+    out = torch.zeros(1, dtype=torch.int32, device=gpu)
+    G.argmax(torch.from_numpy(x).to(gpu), out)
+    assert int(out.item()) == orc.argmax(x)
+
+
+def test_errors_are_status_codes(gpu):
+    """Shape/dtype violations return GTN_ERR_ARG (the reference asserts and exits)."""
+    x = torch.zeros(64, dtype=torch.uint8, device=gpu)
+    with pytest.raises(G.GtenError, match="status 1"):
+        G.matmul_2d(G.GT(x, Q8, (1, 32)), G.GT(x, Q8, (1, 64)), G.GT(x, F32, (1, 1)))
+    with pytest.raises(G.GtenError, match="status 1"):
+        G.add(G.GT(x, Q8, (1, 32)), G.GT(x, F16, (1, 32)), G.GT(x, Q8, (1, 32)))
