@@ -53,6 +53,9 @@ typedef struct gtn_tensor {
 /* Human-readable text of the last error on the calling thread ("" if none). */
 const char* gtn_last_error(void);
 
+/* Number of CUDA kernels this library has launched in the process (a diagnostic counter). */
+unsigned long long gtn_kernel_launches(void);
+
 /* ---- gten::ops (src/gten/ops.h) ----------------------------------------------------------- */
 
 /* ops.h:16 matmul_2d(x, w, out, start_pos): out[r,:] = x[r,:] . w^T for r in [start_pos, n_ctx),
@@ -156,6 +159,17 @@ int gtn_model_logits(gtn_model* m, const int32_t* tokens, int n_tokens, int star
  * prompt (host int32), then n_gen greedy steps; out_tokens (host) receives the n_gen ids.
  * Synchronous. */
 int gtn_model_generate(gtn_model* m, const int32_t* prompt, int n_prompt, int n_gen, int32_t* out_tokens);
+
+/* The same greedy loop with device-resident int32 prompt / output arrays, enqueued on the model's
+ * stream without host synchronization (the ids never leave HBM). Token ids are range-checked on
+ * the device; gtn_model_check reports violations. */
+int gtn_model_generate_device(gtn_model* m, const int32_t* prompt, int n_prompt, int n_gen, int32_t* out_tokens);
+
+/* The cudaStream_t the model enqueues its work on. */
+void* gtn_model_stream(gtn_model* m);
+
+/* Waits for the model's stream and returns GTN_ERR_DEVICE if a kernel flagged an error. */
+int gtn_model_check(gtn_model* m);
 
 #ifdef __cplusplus
 }

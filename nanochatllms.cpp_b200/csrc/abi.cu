@@ -1,5 +1,6 @@
 // Op-level C ABI (include/gten_b200.h): gten::ops, the packer / quantizer and the argmax.
 // Argument checks mirror the reference's GTEN_ASSERTs (src/gten/ops.cpp) but return GTN_ERR_ARG.
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <mutex>
@@ -26,6 +27,9 @@ static int cuda_status(cudaError_t e, const char* what) {
     if (e == cudaSuccess) return GTN_OK;
     return fail(e == cudaErrorMemoryAllocation ? GTN_ERR_OOM : GTN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
+
+static std::atomic<unsigned long long> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 __device__ unsigned int g_dev_err;
 
@@ -195,6 +199,16 @@ static int check_tensor(const gtn_tensor* t, const char* name) {
     if (t->ndim < 1 || t->ndim > 3) return fail(GTN_ERR_ARG, "%s has %d dims", name, t->ndim);
     for (int i = 0; i < t->ndim; ++i)
         if (t->shape[i] <= 0) return fail(GTN_ERR_ARG, "%s dim %d is %d", name, i, t->shape[i]);
+    // Quantized rows of a partial last block: the reference allocates ceil(n/32) blocks per row
+    // (tensor.cpp:43-45) but steps rows by floor(n/32) blocks (tensor.h:196-200), so rows beyond
+    // the first overlap. Only single-row use is well defined.
+    if ((t->dtype == GTN_Q8 || t->dtype == GTN_Q4) && t->ndim >= 2 && t->shape[t->ndim - 1] % GTN_QBLK != 0) {
+        long rows = 1;
+        for (int i = 0; i < t->ndim - 1; ++i) rows *= t->shape[i];
+        if (rows > 1)
+            return fail(GTN_ERR_ARG, "%s: quantized rows of %d elements (not a multiple of 32) overlap", name,
+                        t->shape[t->ndim - 1]);
+    }
     return GTN_OK;
 }
 
@@ -295,6 +309,8 @@ static int rowop(const gtn_tensor* a, const gtn_tensor* b, gtn_tensor* out, floa
 extern "C" {
 
 const char* gtn_last_error(void) { return g_last_error.c_str(); }
+
+unsigned long long gtn_kernel_launches(void) { return g_launches.load(); }
 
 // ops.cpp:617-636
 int gtn_matmul_2d(const gtn_tensor* x, const gtn_tensor* w, gtn_tensor* out, int start_pos, void* stream) {
@@ -457,7 +473,7 @@ int gtn_token_embed(const gtn_tensor* weight, const gtn_tensor* tokens, gtn_tens
     cudaError_t e = launch_pdl(k_embed, dim3((nb + 3) / 4, n_ctx - start_pos), dim3(128), 0, S(stream),
                                (const uint8_t*)weight->data, bstride(weight, 0), (int)weight->dtype,
                                (const int32_t*)tokens->data, (uint8_t*)out->data, bstride(out, 0), (int)out->dtype, n,
-                               start_pos);
+                               start_pos, weight->shape[0], device_error_word());
     return cuda_status(e, "token_embed");
 }
 
@@ -465,6 +481,7 @@ int gtn_pack_q8(const float* w, int64_t rows, int64_t cols, void* out, void* str
     GTN_REQUIRE(w && out && rows > 0 && cols > 0 && cols % GTN_QBLK == 0, "pack_q8: arguments");
     GTN_REQUIRE(((uintptr_t)w & 15) == 0, "pack_q8: w must be 16-byte aligned");
     const long nb = rows * (cols / GTN_QBLK);
+    count_launch();
     k_pack<false><<<(unsigned)((nb + 255) / 256), 256, 0, S(stream)>>>(w, nb, (uint8_t*)out);
     return launched("pack_q8");
 }
@@ -473,6 +490,7 @@ int gtn_pack_q4(const float* w, int64_t rows, int64_t cols, void* out, void* str
     GTN_REQUIRE(w && out && rows > 0 && cols > 0 && cols % GTN_QBLK == 0, "pack_q4: arguments");
     GTN_REQUIRE(((uintptr_t)w & 15) == 0, "pack_q4: w must be 16-byte aligned");
     const long nb = rows * (cols / GTN_QBLK);
+    count_launch();
     k_pack<true><<<(unsigned)((nb + 255) / 256), 256, 0, S(stream)>>>(w, nb, (uint8_t*)out);
     return launched("pack_q4");
 }

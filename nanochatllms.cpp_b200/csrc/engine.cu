@@ -52,6 +52,7 @@ struct gtn_model {
     float* logits = nullptr;
     int32_t* tok = nullptr;
     int32_t* next = nullptr;
+    int32_t* gen = nullptr;
     float2* rope = nullptr;
     cudaStream_t st = nullptr;
     std::vector<void*> allocs;
@@ -190,6 +191,7 @@ int gtn_model_create(int kind, int wdtype, int max_ctx, int max_batch, const int
     rc |= dalloc(m.get(), &m->logits, sizeof(float) * (size_t)m->n_vocab * max_batch);
     rc |= dalloc(m.get(), &m->tok, sizeof(int32_t) * (size_t)max_ctx * max_batch);
     rc |= dalloc(m.get(), &m->next, sizeof(int32_t) * (size_t)max_batch);
+    rc |= dalloc(m.get(), &m->gen, sizeof(int32_t) * (size_t)max_ctx * max_batch);
     for (int l = 0; l < m->nl && rc == GTN_OK; ++l) {
         const long kvb = (long)max_batch * max_ctx * row_bytes(adt, m->L[l].nkv * m->dh);
         rc |= dalloc(m.get(), &m->L[l].kc, kvb);
@@ -402,7 +404,7 @@ static int forward(gtn_model* m, int seq, int n, int sp) {
     } while (0)
     const int32_t* toks = m->tok + (long)seq * m->max_ctx + sp;
     GK(launch_pdl(k_embed, dim3(((d + 31) / 32 + 3) / 4, M), dim3(128), 0, st, m->emb, m->emb_rs, m->wdt, toks, m->x,
-                  rd_, adt, d, 0));
+                  rd_, adt, d, 0, m->n_vocab, device_error_word()));
     if (m->family == 2) GK(rows_op(ROP_SCALE, m->x, rd_, nullptr, 0, m->x, rd_, adt, d, M, 12.0f, nullptr, st));
     for (int l = 0; l < m->nl; ++l) {
         Layer& Ly = m->L[l];
@@ -475,7 +477,24 @@ static int forward(gtn_model* m, int seq, int n, int sp) {
 
 static int check_dev_err() {
     const unsigned int v = take_device_error();
-    if (v) return fail(GTN_ERR_DEVICE, "device-side bounded wait expired (code %u)", v);
+    if (v)
+        return fail(GTN_ERR_DEVICE, "device-side error code %u (1: a bounded wait expired, 2: token id out of range)",
+                    v);
+    return GTN_OK;
+}
+
+// Greedy loop on the device (sampler.cpp:19-53 without the EOS stop): the prompt is already in
+// m->tok; each step's argmax becomes the next input token and is appended to `out` (device).
+static int generate_dev(gtn_model* m, int n_prompt, int n_gen, int32_t* out) {
+    int n = n_prompt;
+    for (int i = 0; i < n_gen; ++i) {
+        const int rc = forward(m, 0, n, i == 0 ? 0 : n - 1);
+        if (rc != GTN_OK) return rc;
+        if (i + 1 < n_gen)
+            ECHK(cudaMemcpyAsync(m->tok + n, m->next, sizeof(int32_t), cudaMemcpyDeviceToDevice, m->st), "next");
+        ECHK(cudaMemcpyAsync(out + i, m->next, sizeof(int32_t), cudaMemcpyDeviceToDevice, m->st), "out");
+        ++n;
+    }
     return GTN_OK;
 }
 
@@ -504,17 +523,27 @@ int gtn_model_generate(gtn_model* m, const int32_t* prompt, int n_prompt, int n_
     for (int i = 0; i < n_prompt; ++i)
         if (prompt[i] < 0 || prompt[i] >= m->n_vocab) return fail(GTN_ERR_ARG, "model_generate: token id %d", prompt[i]);
     ECHK(cudaMemcpyAsync(m->tok, prompt, sizeof(int32_t) * n_prompt, cudaMemcpyHostToDevice, m->st), "prompt");
-    int n = n_prompt;
-    for (int i = 0; i < n_gen; ++i) {
-        const int rc = forward(m, 0, n, i == 0 ? 0 : n - 1);
-        if (rc != GTN_OK) return rc;
-        // the sampled id becomes the next input token on the device (sampler.cpp:206)
-        if (i + 1 < n_gen)
-            ECHK(cudaMemcpyAsync(m->tok + n, m->next, sizeof(int32_t), cudaMemcpyDeviceToDevice, m->st), "next");
-        ECHK(cudaMemcpyAsync(out_tokens + i, m->next, sizeof(int32_t), cudaMemcpyDeviceToHost, m->st), "out");
-        ++n;
-    }
+    // generated ids collect on the device and come back in one copy
+    const int rc = generate_dev(m, n_prompt, n_gen, m->gen);
+    if (rc != GTN_OK) return rc;
+    ECHK(cudaMemcpyAsync(out_tokens, m->gen, sizeof(int32_t) * n_gen, cudaMemcpyDeviceToHost, m->st), "out");
     ECHK(cudaStreamSynchronize(m->st), "model_generate");
+    return check_dev_err();
+}
+
+int gtn_model_generate_device(gtn_model* m, const int32_t* prompt, int n_prompt, int n_gen, int32_t* out_tokens) {
+    if (!m || !m->loaded || !prompt || !out_tokens || n_prompt <= 0 || n_gen <= 0)
+        return fail(GTN_ERR_ARG, "model_generate_device: arguments");
+    if (n_prompt + n_gen - 1 > m->max_ctx) return fail(GTN_ERR_ARG, "model_generate_device: exceeds max_ctx");
+    ECHK(cudaMemcpyAsync(m->tok, prompt, sizeof(int32_t) * n_prompt, cudaMemcpyDeviceToDevice, m->st), "prompt");
+    return generate_dev(m, n_prompt, n_gen, out_tokens);
+}
+
+void* gtn_model_stream(gtn_model* m) { return m ? (void*)m->st : nullptr; }
+
+int gtn_model_check(gtn_model* m) {
+    if (!m) return fail(GTN_ERR_ARG, "model_check: NULL");
+    ECHK(cudaStreamSynchronize(m->st), "model_check");
     return check_dev_err();
 }
 

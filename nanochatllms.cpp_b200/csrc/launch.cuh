@@ -15,6 +15,9 @@ namespace gtn {
 void set_error(const std::string& msg);
 int fail(int code, const char* fmt, ...);
 
+// Number of kernels this library has launched in the process (gtn_kernel_launches).
+void count_launch();
+
 // Launches `kern` with programmatic dependent launch enabled (the kernel may start while the
 // previous kernel in the stream finishes; it calls griddepcontrol.wait before reading its inputs).
 template <typename... KArgs, typename... Args>
@@ -30,6 +33,7 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    count_launch();
     return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 

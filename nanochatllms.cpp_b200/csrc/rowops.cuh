@@ -154,13 +154,21 @@ static __global__ void k_rope(const uint8_t* in, long is, uint8_t* out, long os,
 }
 
 // token_embed / copy_row (ops.cpp:526-576). grid: (ceil(nblocks/4), rows); block 128.
+// Token ids come from device memory, so each is range-checked here: an id outside [0, n_vocab)
+// sets GTN_DEVERR_TOKEN in *err and row 0 is read instead (never out of bounds).
+#define GTN_DEVERR_TOKEN 2u
 static __global__ void k_embed(const uint8_t* w, long ws, int wdt, const int32_t* tokens, uint8_t* out, long os,
-                               int odt, int n, int row0) {
+                               int odt, int n, int row0, int n_vocab, unsigned int* err) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int row = row0 + blockIdx.y;
     const int blk = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (blk * GTN_QBLK >= n) return;
-    const uint8_t* src = w + (long)tokens[row] * ws;
+    int tok = tokens[row];
+    if (tok < 0 || tok >= n_vocab) {
+        if (blk == 0 && lane == 0 && err) atomicOr(err, GTN_DEVERR_TOKEN);
+        tok = 0;
+    }
+    const uint8_t* src = w + (long)tok * ws;
     uint8_t* dst = out + (long)row * os;
     if (wdt == GTN_Q4) {
         const int i = blk * GTN_QBLK + lane;
@@ -195,20 +203,27 @@ static __global__ void k_pack(const float* w, long nblocks, uint8_t* out) {
     const float delta = absmax / (Q4 ? 7.0f : 127.0f);
     const float inv = delta != 0.0f ? 1.0f / delta : 0.0f;
     const uint16_t d = f2h(delta);
+    // Blocks are 34 or 18 bytes, so every block starts on a 2-byte boundary: store 16-bit words.
     if (Q4) {
-        uint8_t* o = out + b * GTN_Q4_BYTES;
-        o[0] = (uint8_t)(d & 255); o[1] = (uint8_t)(d >> 8);
+        uint16_t* o = reinterpret_cast<uint16_t*>(out + b * GTN_Q4_BYTES);
+        o[0] = d;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int t0 = (int)(rintf(x[j] * inv) + 7.0f);
-            const int t1 = (int)(rintf(x[j + 16] * inv) + 7.0f);
-            o[2 + j] = (uint8_t)((t0 << 4) | (t1 & 15));
+        for (int j = 0; j < 16; j += 2) {
+            const int a0 = (int)(rintf(x[j] * inv) + 7.0f), a1 = (int)(rintf(x[j + 16] * inv) + 7.0f);
+            const int b0 = (int)(rintf(x[j + 1] * inv) + 7.0f), b1 = (int)(rintf(x[j + 17] * inv) + 7.0f);
+            const unsigned lo = (unsigned)((a0 << 4) | (a1 & 15)) & 255u;
+            const unsigned hi = (unsigned)((b0 << 4) | (b1 & 15)) & 255u;
+            o[1 + j / 2] = (uint16_t)(lo | (hi << 8));
         }
     } else {
-        uint8_t* o = out + b * GTN_Q8_BYTES;
-        o[0] = (uint8_t)(d & 255); o[1] = (uint8_t)(d >> 8);
+        uint16_t* o = reinterpret_cast<uint16_t*>(out + b * GTN_Q8_BYTES);
+        o[0] = d;
 #pragma unroll
-        for (int j = 0; j < GTN_QBLK; ++j) o[2 + j] = (uint8_t)(int8_t)(int)rintf(x[j] * inv);
+        for (int j = 0; j < GTN_QBLK; j += 2) {
+            const unsigned lo = (unsigned)(int)rintf(x[j] * inv) & 255u;
+            const unsigned hi = (unsigned)(int)rintf(x[j + 1] * inv) & 255u;
+            o[1 + j / 2] = (uint16_t)(lo | (hi << 8));
+        }
     }
 }
 

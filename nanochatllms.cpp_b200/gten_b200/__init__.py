@@ -49,17 +49,27 @@ def lib() -> C.CDLL:
             raise GtenError(f"{LIB_PATH} is missing: build it with nanochatllms.cpp_b200/build.py")
         L = C.CDLL(LIB_PATH)
         L.gtn_last_error.restype = C.c_char_p
+        L.gtn_kernel_launches.restype = C.c_ulonglong
         L.gtn_model_create.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_void_p)]
         L.gtn_model_free.argtypes = [C.c_void_p]
         L.gtn_model_n_vocab.argtypes = [C.c_void_p]
         L.gtn_model_load.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t]
         L.gtn_model_logits.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
         L.gtn_model_generate.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.gtn_model_generate_device.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.gtn_model_stream.argtypes = [C.c_void_p]
+        L.gtn_model_stream.restype = C.c_void_p
+        L.gtn_model_check.argtypes = [C.c_void_p]
         for name in ("gtn_pack_q8", "gtn_pack_q4", "gtn_quantize_q8_rows"):
             getattr(L, name).argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p]
         L.gtn_argmax.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
         _lib = L
     return _lib
+
+
+def kernel_launches() -> int:
+    """Kernels launched by the library so far in this process."""
+    return int(lib().gtn_kernel_launches())
 
 
 def _check(rc: int, what: str) -> None:
@@ -241,6 +251,18 @@ class Model:
         out = np.zeros(n_gen, np.int32)
         _check(lib().gtn_model_generate(self._h, p.ctypes.data, p.size, n_gen, out.ctypes.data), "model_generate")
         return out
+
+    def generate_device(self, prompt_dev, n_gen: int, out_dev) -> None:
+        """Greedy decode with device int32 tensors; asynchronous on ``self.stream_ptr``."""
+        _check(lib().gtn_model_generate_device(self._h, _ptr(prompt_dev), prompt_dev.numel(), n_gen, _ptr(out_dev)),
+               "model_generate_device")
+
+    @property
+    def stream_ptr(self) -> int:
+        return lib().gtn_model_stream(self._h) or 0
+
+    def check(self) -> None:
+        _check(lib().gtn_model_check(self._h), "model_check")
 
     def close(self):
         if self._h:

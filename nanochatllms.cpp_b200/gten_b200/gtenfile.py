@@ -134,6 +134,36 @@ def synthetic_image(kind: int, wdtype: int, seed: int, pack: Callable, dims=None
     return np.frombuffer(b"".join(parts), np.uint8)
 
 
+def synthetic_image_device(kind: int, wdtype: int, seed: int, dims=None, std: float = 0.02,
+                           device: str = "cuda") -> np.ndarray:
+    """Like synthetic_image, but the N(0, std) matrices are drawn by a CUDA generator (much faster
+    for multi-GB checkpoints; the values differ from the CPU-seeded ones) and packed by the
+    library's CUDA packer."""
+    import torch
+
+    from . import pack_q4, pack_q8
+
+    a = arch(kind, dims)
+    parts = [struct.pack("<q", MAGIC)]
+    gen = torch.Generator(device=device)
+    for idx, (name, k, shape) in enumerate(records(a)):
+        if k == "w":
+            gen.manual_seed(seed + idx)
+            w = torch.randn(shape, generator=gen, dtype=torch.float32, device=device) * std
+            if wdtype == F16:
+                payload = w.to(torch.float16).cpu().numpy().tobytes()
+            else:
+                out = torch.empty(shape[0] * row_bytes(wdtype, shape[1]), dtype=torch.uint8, device=device)
+                (pack_q8 if wdtype == Q8 else pack_q4)(w, out)
+                payload = out.cpu().numpy().tobytes()
+            del w
+        else:
+            payload = np.full(shape, 1.0 if k == "g" else 0.0, np.float16).tobytes()
+        parts.append(_header(name, len(payload)))
+        parts.append(payload)
+    return np.frombuffer(b"".join(parts), np.uint8)
+
+
 def cuda_packer(device: str = "cuda"):
     """A packer running the library's CUDA kernels (gtn_pack_q8 / gtn_pack_q4)."""
     import torch

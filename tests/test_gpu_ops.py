@@ -22,7 +22,7 @@ def dev_out(nbytes, device, fill=None):
 
 @pytest.mark.parametrize("wdt", [Q8, Q4, F16])
 @pytest.mark.parametrize("M,K,N", [(1, 2048, 256), (1, 2048, 2048), (1, 5632, 2048), (3, 256, 96), (16, 2048, 64),
-                                   (9, 5760, 40), (64, 2304, 72), (1, 2048, 32003)])
+                                   (9, 5760, 64), (64, 2304, 96), (1, 2048, 32003), (1, 2048, 40)])
 @pytest.mark.parametrize("odt_kind", ["act", "f32"])
 def test_matmul_2d(orc, gpu, wdt, M, K, N, odt_kind):
     rng = np.random.default_rng(M * 1000 + K + N + wdt)
@@ -119,19 +119,17 @@ def test_rotary_emb(orc, gpu, dt, pct, M, sp):
 @pytest.mark.parametrize("D", [5632, 5760, 2048, 70])
 def test_elementwise(orc, gpu, dt, D):
     rng = np.random.default_rng(D + 11 * dt)
-    M = 3
+    M = 3 if (D % 32 == 0 or dt == F16) else 1
     rb = row_bytes(dt, D)
     x = act_rows(orc, rng, dt, M, D, 3.0)
     y = act_rows(orc, rng, dt, M, D)
     bias = fp16_vec(rng, D, 0.0, 0.5)
 
-    def run(fn, *args, out=None):
-        return from_dev(out)
-
     # silu (out of place)
     out = dev_out(rb * M, gpu)
-    G.silu(G.GT(to_dev(x, gpu), dt, (M, D)), G.GT(out, dt, (M, D)), start_pos=1)
-    assert np.array_equal(from_dev(out)[rb:], orc.silu(x, dt, M, D, 1)[rb:])
+    sp = min(1, M - 1)
+    G.silu(G.GT(to_dev(x, gpu), dt, (M, D)), G.GT(out, dt, (M, D)), start_pos=sp)
+    assert np.array_equal(from_dev(out)[sp * rb:], orc.silu(x, dt, M, D, sp)[sp * rb:])
     # silu_inplace
     buf = to_dev(x, gpu)
     G.silu_inplace(G.GT(buf, dt, (M, D)))
@@ -149,8 +147,8 @@ def test_elementwise(orc, gpu, dt, D):
     # scale (minicpm's three constants) and bias
     for s in (12.0, float(np.float32(1.4) / np.sqrt(40.0)), 1.0 / 9):
         buf = to_dev(x, gpu)
-        G.scale(G.GT(buf, dt, (M, D)), s, start_pos=2)
-        assert np.array_equal(from_dev(buf), orc.scale(x, dt, M, D, s, 2))
+        G.scale(G.GT(buf, dt, (M, D)), s, start_pos=M - 1)
+        assert np.array_equal(from_dev(buf), orc.scale(x, dt, M, D, s, M - 1))
     buf = to_dev(x, gpu)
     G.bias_add_inplace(G.GT(buf, dt, (M, D)), G.GT(to_dev(bias, gpu), F16, (D,)))
     assert np.array_equal(from_dev(buf), orc.bias_add_inplace(x, dt, M, D, bias))
@@ -175,7 +173,8 @@ def test_pack_and_quantize(orc, gpu, rows, cols):
     rng = np.random.default_rng(rows + cols)
     w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
     w[0, :32] = 0.0                      # an all-zero block (delta 0)
-    w[-1, 32:64] = np.float32(0.5) * (np.arange(32) % 3 - 1)  # exact .5 ties after scaling
+    if cols >= 64:
+        w[-1, 32:64] = np.float32(0.5) * (np.arange(32) % 3 - 1)  # block with absmax 0.5 and zeros
     wd = torch.from_numpy(w).to(gpu)
     for dt, packer, ref in ((Q8, G.pack_q8, orc.pack_q8), (Q4, G.pack_q4, orc.pack_q4)):
         out = torch.zeros(rows * row_bytes(dt, cols), dtype=torch.uint8, device=gpu)
@@ -212,3 +211,6 @@ def test_errors_are_status_codes(gpu):
         G.matmul_2d(G.GT(x, Q8, (1, 32)), G.GT(x, Q8, (1, 64)), G.GT(x, F32, (1, 1)))
     with pytest.raises(G.GtenError, match="status 1"):
         G.add(G.GT(x, Q8, (1, 32)), G.GT(x, F16, (1, 32)), G.GT(x, Q8, (1, 32)))
+    # multi-row quantized tensors need whole blocks per row (see check_tensor in abi.cu)
+    with pytest.raises(G.GtenError, match="overlap"):
+        G.silu_inplace(G.GT(x, Q8, (2, 40)))
