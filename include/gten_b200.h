@@ -65,6 +65,16 @@ unsigned long long gtn_kernel_launches(void);
  * (cudaMallocAsync / cudaFreeAsync on `stream`). */
 int gtn_matmul_2d(const gtn_tensor* x, const gtn_tensor* w, gtn_tensor* out, int start_pos, void* stream);
 
+/* No counterpart in the reference. gtn_matmul_2d for callers that may not allocate device memory
+ * (a host that owns a fixed memory budget, code running inside an allocator or memory-pool
+ * callback, paths that cannot risk an allocation's implicit synchronization): same arguments and
+ * results, but a Q8 / fp16 `out` is staged in a fixed 8 MiB array inside the library instead of
+ * cudaMallocAsync scratch, so (n_ctx - start_pos) * n_out may not exceed 2,097,152 (GTN_ERR_ARG
+ * otherwise; fp32 outputs need no staging and have no limit). The array's device address is
+ * looked up on the first call made on each device — make that call before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race on it. */
+int gtn_matmul_2d_noalloc(const gtn_tensor* x, const gtn_tensor* w, gtn_tensor* out, int start_pos, void* stream);
+
 /* ops.h:22 qkv_attn(q, k, v, qk, qkv, max_ctx, start_pos): causal attention with GQA, the
  * probability rows stored in the activation dtype as the reference does (ops.cpp:1017-1220).
  * `qk` is accepted for signature parity and may be NULL: the probabilities stay on chip. */
