@@ -170,6 +170,13 @@ int gtn_model_logits(gtn_model* m, const int32_t* tokens, int n_tokens, int star
  * Synchronous. */
 int gtn_model_generate(gtn_model* m, const int32_t* prompt, int n_prompt, int n_gen, int32_t* out_tokens);
 
+/* greedy_sample for `batch` independent sequences (the reference has no batching: each sequence
+ * gives exactly the ids it would give alone). prompts: host [batch][n_prompt]; out_tokens: host
+ * [batch][n_gen]. batch <= max_batch; Q8/Q4 models of the TinyLlama, Zephyr and MiniCPM families.
+ * Synchronous. */
+int gtn_model_generate_batch(gtn_model* m, const int32_t* prompts, int batch, int n_prompt, int n_gen,
+                             int32_t* out_tokens);
+
 /* The same greedy loop with device-resident int32 prompt / output arrays, enqueued on the model's
  * stream without host synchronization (the ids never leave HBM). Token ids are range-checked on
  * the device; gtn_model_check reports violations. */

@@ -17,6 +17,7 @@
 #include <memory>
 #include <vector>
 
+#include "fused.cuh"
 #include "launch.cuh"
 
 namespace gtn {
@@ -56,6 +57,17 @@ struct gtn_model {
     float2* rope = nullptr;
     cudaStream_t st = nullptr;
     std::vector<void*> allocs;
+    // fused decode step (Q8/Q4 weights, families 0-2): per-sequence device positions, residual
+    // rows (x after attention input, h after attention), stacked projection outputs
+    bool fused = false;
+    int* pos = nullptr;
+    uint8_t *rx = nullptr, *rh = nullptr, *datt = nullptr;
+    float *yqkv = nullptr, *yo = nullptr, *ygu = nullptr, *yd = nullptr;
+    long ldqkv = 0, ldgu = 0;
+    cudaGraphExec_t graph = nullptr;
+    int graph_B = 0;
+    long graph_kernels = 0;
+    int* pos_host = nullptr;  // pinned staging for position uploads
 };
 
 namespace gtn {
@@ -189,13 +201,29 @@ int gtn_model_create(int kind, int wdtype, int max_ctx, int max_batch, const int
     const long ywidth = std::max<long>(m->max_q + 2L * m->max_kv, 2L * m->max_ffn);
     rc |= dalloc(m.get(), &m->y, sizeof(float) * R * ywidth);
     rc |= dalloc(m.get(), &m->logits, sizeof(float) * (size_t)m->n_vocab * max_batch);
-    rc |= dalloc(m.get(), &m->tok, sizeof(int32_t) * (size_t)max_ctx * max_batch);
+    // token ids per sequence: max_ctx + 1 slots (the last generated id is recorded, never fed back)
+    rc |= dalloc(m.get(), &m->tok, sizeof(int32_t) * (size_t)(max_ctx + 1) * max_batch);
     rc |= dalloc(m.get(), &m->next, sizeof(int32_t) * (size_t)max_batch);
-    rc |= dalloc(m.get(), &m->gen, sizeof(int32_t) * (size_t)max_ctx * max_batch);
+    rc |= dalloc(m.get(), &m->gen, sizeof(int32_t) * (size_t)(max_ctx + 1) * max_batch);
     for (int l = 0; l < m->nl && rc == GTN_OK; ++l) {
         const long kvb = (long)max_batch * max_ctx * row_bytes(adt, m->L[l].nkv * m->dh);
         rc |= dalloc(m.get(), &m->L[l].kc, kvb);
         rc |= dalloc(m.get(), &m->L[l].vc, kvb);
+    }
+    m->fused = (m->wdt == GTN_Q8 || m->wdt == GTN_Q4) && m->family <= 2 && m->dh == 64;
+    if (rc == GTN_OK && m->fused) {
+        const long B = max_batch;
+        m->ldqkv = m->max_q + 2L * m->max_kv;
+        m->ldgu = 2L * m->max_ffn;
+        rc |= dalloc(m.get(), &m->pos, sizeof(int) * B);
+        rc |= dalloc(m.get(), &m->rx, B * row_bytes(adt, m->d));
+        rc |= dalloc(m.get(), &m->rh, B * row_bytes(adt, m->d));
+        rc |= dalloc(m.get(), &m->datt, B * row_bytes(adt, m->max_q));
+        rc |= dalloc(m.get(), &m->yqkv, sizeof(float) * B * m->ldqkv);
+        rc |= dalloc(m.get(), &m->yo, sizeof(float) * B * m->d);
+        rc |= dalloc(m.get(), &m->ygu, sizeof(float) * B * m->ldgu);
+        rc |= dalloc(m.get(), &m->yd, sizeof(float) * B * m->d);
+        if (rc == GTN_OK && cudaMallocHost((void**)&m->pos_host, sizeof(int) * B) != cudaSuccess) rc = GTN_ERR_OOM;
     }
     if (rc == GTN_OK && m->rd > 0) {
         auto tab = rope_table_host(max_ctx, m->rd);
@@ -216,6 +244,8 @@ int gtn_model_create(int kind, int wdtype, int max_ctx, int max_batch, const int
 void gtn_model_free(gtn_model* m) {
     if (!m) return;
     if (m->st) cudaStreamSynchronize(m->st);
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    if (m->pos_host) cudaFreeHost(m->pos_host);
     free_all(m);
     if (m->arena) cudaFree(m->arena);
     if (m->st) cudaStreamDestroy(m->st);
@@ -402,7 +432,7 @@ static int forward(gtn_model* m, int seq, int n, int sp) {
         e = (expr);                                         \
         if (e != cudaSuccess) return cuda_st(e, #expr);     \
     } while (0)
-    const int32_t* toks = m->tok + (long)seq * m->max_ctx + sp;
+    const int32_t* toks = m->tok + (long)seq * (m->max_ctx + 1) + sp;
     GK(launch_pdl(k_embed, dim3(((d + 31) / 32 + 3) / 4, M), dim3(128), 0, st, m->emb, m->emb_rs, m->wdt, toks, m->x,
                   rd_, adt, d, 0, m->n_vocab, device_error_word()));
     if (m->family == 2) GK(rows_op(ROP_SCALE, m->x, rd_, nullptr, 0, m->x, rd_, adt, d, M, 12.0f, nullptr, st));
@@ -483,9 +513,193 @@ static int check_dev_err() {
     return GTN_OK;
 }
 
+// ---- fused decode step ---------------------------------------------------------------------
+// With `dry` set, only the shared-memory attributes of the kernels are configured (so that the
+// step can then be captured into a CUDA graph with no non-stream calls inside the capture).
+static long g_step_kernels = 0;
+
+template <int WDT, int NW, int MT, int PRO>
+static cudaError_t fg_launch(const FArgs& a, cudaStream_t st, bool dry) {
+    const size_t smem = fgemv_smem<WDT>(NW, MT, a.K, a.adt, PRO);
+    if (dry) return ensure_smem(k_fgemv<WDT, NW, MT, PRO>, smem);
+    ++g_step_kernels;
+    const dim3 grid((a.N + NW * 8 - 1) / (NW * 8), (a.B + MT - 1) / MT);
+    return launch_pdl(k_fgemv<WDT, NW, MT, PRO>, grid, dim3(NW * 32), smem, st, a);
+}
+
+template <int WDT, int PRO>
+static cudaError_t fg_mt(const FArgs& a, cudaStream_t st, bool dry) {
+    const bool big = a.N > 4096;
+    if (a.B <= 1) return big ? fg_launch<WDT, 4, 1, PRO>(a, st, dry) : fg_launch<WDT, 1, 1, PRO>(a, st, dry);
+    if (a.B <= 2) return big ? fg_launch<WDT, 4, 2, PRO>(a, st, dry) : fg_launch<WDT, 1, 2, PRO>(a, st, dry);
+    if (a.B <= 4) return big ? fg_launch<WDT, 4, 4, PRO>(a, st, dry) : fg_launch<WDT, 1, 4, PRO>(a, st, dry);
+    return big ? fg_launch<WDT, 4, 8, PRO>(a, st, dry) : fg_launch<WDT, 1, 8, PRO>(a, st, dry);
+}
+
+static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) {
+    if (m->wdt == GTN_Q8) {
+        if (pro == PRO_COPY) return fg_mt<GTN_Q8, PRO_COPY>(a, m->st, dry);
+        if (pro == PRO_RESNORM) return fg_mt<GTN_Q8, PRO_RESNORM>(a, m->st, dry);
+        return fg_mt<GTN_Q8, PRO_SWIGLU>(a, m->st, dry);
+    }
+    if (pro == PRO_COPY) return fg_mt<GTN_Q4, PRO_COPY>(a, m->st, dry);
+    if (pro == PRO_RESNORM) return fg_mt<GTN_Q4, PRO_RESNORM>(a, m->st, dry);
+    return fg_mt<GTN_Q4, PRO_SWIGLU>(a, m->st, dry);
+}
+
+// One greedy decode step for sequences 0..B-1 at positions m->pos[b] (their input tokens are at
+// m->tok[b*max_ctx + pos[b]]): the reference's block sequence (tinyllama.cpp:99-104 and the
+// siblings) as five kernels per layer, then the lm_head GEMV and the greedy pick.
+static int decode_step(gtn_model* m, int B, bool dry) {
+    cudaStream_t st = m->st;
+    const int adt = m->adt, d = m->d, dh = m->dh;
+    const float depth = (float)(1.4f / std::sqrt(40.0));  // minicpm.cpp:57
+    const bool cpm = m->family == 2;
+    unsigned int* err = device_error_word();
+    cudaError_t e = cudaSuccess;
+#define SK(expr)                                              \
+    do {                                                      \
+        e = (expr);                                           \
+        if (e != cudaSuccess) return cuda_st(e, #expr);       \
+    } while (0)
+    FArgs base{};
+    base.B = B;
+    base.pos = m->pos;
+    base.adt = adt;
+    base.err = err;
+    for (int l = 0; l < m->nl; ++l) {
+        Layer& Ly = m->L[l];
+        const int qd = Ly.nh * dh, kvd = Ly.nkv * dh, nqkv = qd + 2 * kvd;
+        const long rkv = row_bytes(adt, kvd);
+        FArgs q = base;
+        q.K = d;
+        if (l == 0) {
+            q.emb = m->emb; q.emb_s = m->emb_rs; q.emb_dt = m->wdt; q.tok = m->tok; q.tok_s = m->max_ctx + 1;
+            q.n_vocab = m->n_vocab; q.scale_emb = cpm; q.es = 12.0f;
+        } else {
+            q.xres = m->rh; q.xres_s = row_bytes(adt, d); q.yadd = m->yd; q.yadd_s = d;
+            q.scale_y = cpm; q.ys = depth;
+        }
+        q.xout = m->rx; q.xout_s = row_bytes(adt, d);
+        q.nw = Ly.n1w; q.nb = Ly.n1b; q.layer = m->family == 1;
+        q.W = Ly.wqkv; q.ws = Ly.rs_d; q.N = nqkv; q.Y = m->yqkv; q.ldy = m->ldqkv;
+        SK(fgemv(m, q, PRO_RESNORM, dry));
+
+        AArgs at{};
+        at.adt = adt; at.q_heads = Ly.nh; at.kv_heads = Ly.nkv; at.d = dh; at.pos = m->pos;
+        at.y = m->yqkv; at.ys = m->ldqkv; at.bq = Ly.bq; at.bk = Ly.bk; at.bv = Ly.bv;
+        at.cs = m->rope; at.half = m->rd / 2; at.kc = Ly.kc; at.vc = Ly.vc; at.kvs = rkv;
+        at.seq_stride = (long)m->max_ctx * rkv; at.out = m->datt; at.os = row_bytes(adt, m->max_q); at.err = err;
+        const size_t asm_ = fattn_smem(m->max_ctx, adt, dh);
+        if (dry) {
+            SK(ensure_smem(k_fattn, asm_));
+        } else {
+            ++g_step_kernels;
+            SK(launch_pdl(k_fattn, dim3(Ly.nh, B), dim3(ATT_THREADS), asm_, st, at));
+        }
+
+        FArgs o = base;
+        o.K = qd; o.xin = m->datt; o.xin_s = row_bytes(adt, m->max_q);
+        o.W = Ly.wo; o.ws = Ly.rs_q; o.N = d; o.Y = m->yo; o.ldy = d;
+        SK(fgemv(m, o, PRO_COPY, dry));
+
+        FArgs gu = base;
+        gu.K = d; gu.xres = m->rx; gu.xres_s = row_bytes(adt, d); gu.yadd = m->yo; gu.yadd_s = d;
+        gu.scale_y = cpm; gu.ys = depth; gu.xout = m->rh; gu.xout_s = row_bytes(adt, d);
+        gu.nw = Ly.n2w; gu.nb = Ly.n2b; gu.layer = m->family == 1;
+        gu.W = Ly.wgu; gu.ws = Ly.rs_d; gu.N = 2 * Ly.nffn; gu.Y = m->ygu; gu.ldy = m->ldgu;
+        SK(fgemv(m, gu, PRO_RESNORM, dry));
+
+        FArgs dn = base;
+        dn.K = Ly.nffn; dn.gu = m->ygu; dn.gu_s = m->ldgu;
+        dn.W = Ly.wd; dn.ws = Ly.rs_f; dn.N = d; dn.Y = m->yd; dn.ldy = d;
+        SK(fgemv(m, dn, PRO_SWIGLU, dry));
+    }
+    FArgs hd = base;
+    hd.K = d; hd.xres = m->rh; hd.xres_s = row_bytes(adt, d); hd.yadd = m->yd; hd.yadd_s = d;
+    hd.scale_y = cpm; hd.ys = depth;
+    hd.nw = m->nfw; hd.nb = m->nfb; hd.layer = m->family == 1; hd.post = cpm; hd.ps = 1.0f / 9;
+    hd.W = m->lm_head; hd.ws = m->emb_rs; hd.N = m->n_vocab; hd.Y = m->logits; hd.ldy = m->n_vocab;
+    SK(fgemv(m, hd, PRO_RESNORM, dry));
+    if (!dry) {
+        ++g_step_kernels;
+        SK(launch_pdl(k_fargmax, dim3(B), dim3(1024), 0, st, (const float*)m->logits, (long)m->n_vocab, m->n_vocab,
+                      m->tok, m->gen, (long)m->max_ctx + 1, m->pos, m->max_ctx + 1, err));
+    }
+#undef SK
+    return GTN_OK;
+}
+
+// Captures decode_step(B) into a CUDA graph (once per B) and launches it.
+static int run_step(gtn_model* m, int B) {
+    if (!m->graph || m->graph_B != B) {
+        if (m->graph) {
+            cudaGraphExecDestroy(m->graph);
+            m->graph = nullptr;
+        }
+        int rc = decode_step(m, B, true);
+        if (rc != GTN_OK) return rc;
+        cudaGraph_t g = nullptr;
+        ECHK(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal), "graph capture");
+        g_step_kernels = 0;
+        rc = decode_step(m, B, false);
+        const cudaError_t ec = cudaStreamEndCapture(m->st, &g);
+        if (rc != GTN_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        ECHK(ec, "graph capture end");
+        const cudaError_t ei = cudaGraphInstantiate(&m->graph, g, 0);
+        cudaGraphDestroy(g);
+        ECHK(ei, "graph instantiate");
+        m->graph_B = B;
+        m->graph_kernels = g_step_kernels;
+    }
+    ECHK(cudaGraphLaunch(m->graph, m->st), "graph launch");
+    for (long i = 0; i < m->graph_kernels; ++i) count_launch();
+    return GTN_OK;
+}
+
+// Sets pos[b] = p for b < B (from pinned host memory, ordered on the model's stream).
+static int set_positions(gtn_model* m, int B, int p) {
+    ECHK(cudaStreamSynchronize(m->st), "positions");
+    for (int b = 0; b < B; ++b) m->pos_host[b] = p;
+    ECHK(cudaMemcpyAsync(m->pos, m->pos_host, sizeof(int) * B, cudaMemcpyHostToDevice, m->st), "positions");
+    return GTN_OK;
+}
+
+// Greedy generation for sequences 0..B-1 whose n_prompt prompt tokens are already in m->tok
+// (row b at b*max_ctx): per-sequence prefill with the op-by-op path (it fills the KV cache and
+// the last row's logits), the greedy pick, then n_gen-1 fused decode steps replayed from a CUDA
+// graph. The generated ids land in m->gen[b*max_ctx + n_prompt + i].
+static int generate_fused(gtn_model* m, int B, int n_prompt, int n_gen) {
+    for (int b = 0; b < B; ++b) {
+        const int rc = forward(m, b, n_prompt, 0);
+        if (rc != GTN_OK) return rc;
+    }
+    int rc = set_positions(m, B, n_prompt - 1);
+    if (rc != GTN_OK) return rc;
+    count_launch();
+    ECHK(launch_pdl(k_fargmax, dim3(B), dim3(1024), 0, m->st, (const float*)m->logits, (long)m->n_vocab, m->n_vocab,
+                    m->tok, m->gen, (long)m->max_ctx + 1, m->pos, m->max_ctx + 1, device_error_word()),
+         "first token");
+    for (int i = 1; i < n_gen; ++i) {
+        rc = run_step(m, B);
+        if (rc != GTN_OK) return rc;
+    }
+    return GTN_OK;
+}
+
 // Greedy loop on the device (sampler.cpp:19-53 without the EOS stop): the prompt is already in
 // m->tok; each step's argmax becomes the next input token and is appended to `out` (device).
 static int generate_dev(gtn_model* m, int n_prompt, int n_gen, int32_t* out) {
+    if (m->fused) {
+        const int rc = generate_fused(m, 1, n_prompt, n_gen);
+        if (rc != GTN_OK) return rc;
+        ECHK(cudaMemcpyAsync(out, m->gen + n_prompt, sizeof(int32_t) * n_gen, cudaMemcpyDeviceToDevice, m->st),
+             "out");
+        return GTN_OK;
+    }
     int n = n_prompt;
     for (int i = 0; i < n_gen; ++i) {
         const int rc = forward(m, 0, n, i == 0 ? 0 : n - 1);
@@ -524,10 +738,40 @@ int gtn_model_generate(gtn_model* m, const int32_t* prompt, int n_prompt, int n_
         if (prompt[i] < 0 || prompt[i] >= m->n_vocab) return fail(GTN_ERR_ARG, "model_generate: token id %d", prompt[i]);
     ECHK(cudaMemcpyAsync(m->tok, prompt, sizeof(int32_t) * n_prompt, cudaMemcpyHostToDevice, m->st), "prompt");
     // generated ids collect on the device and come back in one copy
-    const int rc = generate_dev(m, n_prompt, n_gen, m->gen);
-    if (rc != GTN_OK) return rc;
-    ECHK(cudaMemcpyAsync(out_tokens, m->gen, sizeof(int32_t) * n_gen, cudaMemcpyDeviceToHost, m->st), "out");
+    if (m->fused) {
+        const int rc = generate_fused(m, 1, n_prompt, n_gen);
+        if (rc != GTN_OK) return rc;
+        ECHK(cudaMemcpyAsync(out_tokens, m->gen + n_prompt, sizeof(int32_t) * n_gen, cudaMemcpyDeviceToHost, m->st),
+             "out");
+    } else {
+        int32_t* tmp = m->gen + 0;
+        const int rc = generate_dev(m, n_prompt, n_gen, tmp);
+        if (rc != GTN_OK) return rc;
+        ECHK(cudaMemcpyAsync(out_tokens, tmp, sizeof(int32_t) * n_gen, cudaMemcpyDeviceToHost, m->st), "out");
+    }
     ECHK(cudaStreamSynchronize(m->st), "model_generate");
+    return check_dev_err();
+}
+
+int gtn_model_generate_batch(gtn_model* m, const int32_t* prompts, int batch, int n_prompt, int n_gen,
+                             int32_t* out_tokens) {
+    if (!m || !m->loaded || !prompts || !out_tokens || batch <= 0 || n_prompt <= 0 || n_gen <= 0)
+        return fail(GTN_ERR_ARG, "model_generate_batch: arguments");
+    if (batch > m->max_batch) return fail(GTN_ERR_ARG, "model_generate_batch: batch %d > max_batch %d", batch, m->max_batch);
+    if (n_prompt + n_gen - 1 > m->max_ctx) return fail(GTN_ERR_ARG, "model_generate_batch: exceeds max_ctx");
+    if (!m->fused) return fail(GTN_ERR_ARG, "model_generate_batch: needs Q8/Q4 weights of the TinyLlama, Zephyr or MiniCPM family");
+    for (long i = 0; i < (long)batch * n_prompt; ++i)
+        if (prompts[i] < 0 || prompts[i] >= m->n_vocab) return fail(GTN_ERR_ARG, "model_generate_batch: token id %d", prompts[i]);
+    const long ts = m->max_ctx + 1;
+    ECHK(cudaMemcpy2DAsync(m->tok, sizeof(int32_t) * ts, prompts, sizeof(int32_t) * n_prompt, sizeof(int32_t) * n_prompt,
+                           batch, cudaMemcpyHostToDevice, m->st),
+         "prompts");
+    const int rc = generate_fused(m, batch, n_prompt, n_gen);
+    if (rc != GTN_OK) return rc;
+    ECHK(cudaMemcpy2DAsync(out_tokens, sizeof(int32_t) * n_gen, m->gen + n_prompt, sizeof(int32_t) * ts,
+                           sizeof(int32_t) * n_gen, batch, cudaMemcpyDeviceToHost, m->st),
+         "out");
+    ECHK(cudaStreamSynchronize(m->st), "model_generate_batch");
     return check_dev_err();
 }
 

@@ -1,0 +1,566 @@
+// Fused decode-step kernels (batch of B sequences, one new token each, device-side positions).
+//
+// The reference runs each decode step as ~20 ops per layer, requantizing every intermediate row
+// (modules.cpp, tinyllama.cpp:35-40/88-97, zephyr.cpp:24-41, minicpm.cpp:42-69). Here one layer is
+// five kernels, and every requantization point of the reference is kept inside them:
+//   k_fgemv<RESNORM>  residual update  x = q(x_prev + q(y_prev))  [MiniCPM: q(q(y)*s)]
+//                     then RMSNorm / LayerNorm -> q(.)  (the GEMV's activation), then the
+//                     stacked q/k/v GEMV (fp32 out). Layer 0 takes the embedding row instead.
+//   k_fattn           q(y_q) [+bias -> q] -> RoPE -> q; same for k; q(y_v) [+bias -> q]; writes the
+//                     new K/V cache rows; causal attention over pos+1 keys -> q(att)
+//   k_fgemv<COPY>     o-projection GEMV over q(att)
+//   k_fgemv<RESNORM>  h = q(x + q(y_o)), norm -> q(.), gate/up GEMV
+//   k_fgemv<SWIGLU>   q(silu(q(y_g))) * q(y_u) -> q(.), down GEMV
+// and after the last layer k_fgemv<RESNORM> (final norm [MiniCPM: q(q(.)/9)], lm_head) and
+// k_fargmax (greedy pick, appends the token, advances the position).
+// Every CTA of a GEMV recomputes its prologue (the activation vector is small); block 0 writes the
+// new residual row for the later kernels. All global writes happen after griddepcontrol.wait, and
+// weights (read-only) are prefetched with TMA before it, so a kernel's weight stream overlaps the
+// previous kernel under programmatic dependent launch.
+#pragma once
+#include "attention.cuh"
+#include "matmul.cuh"
+#include "rowops.cuh"
+
+namespace gtn {
+
+// Value of element blk*32+lane after a round trip through dtype adt (write_row_from_float +
+// read_row_to_float, ops.cpp:41-123); optionally stores the bytes into `row` (nullptr: no store).
+__device__ __forceinline__ float requant(float v, int lane, int nv, int adt, uint8_t* row, int blk) {
+    if (adt == GTN_Q8) {
+        uint16_t dh;
+        const int8_t q = warp_quant_block(v, lane, nv, &dh);
+        if (row) {
+            uint8_t* b = row + (long)blk * GTN_Q8_BYTES;
+            if (lane == 0) *reinterpret_cast<uint16_t*>(b) = dh;
+            if (lane < nv) b[2 + lane] = (uint8_t)q;
+        }
+        return (float)q * h2f(dh);
+    }
+    if (adt == GTN_F16) {
+        const uint16_t hv = f2h(v);
+        if (row && lane < nv) reinterpret_cast<uint16_t*>(row)[blk * GTN_QBLK + lane] = hv;
+        return h2f(hv);
+    }
+    if (row && lane < nv) reinterpret_cast<float*>(row)[blk * GTN_QBLK + lane] = v;
+    return v;
+}
+
+enum { PRO_COPY = 0, PRO_RESNORM = 1, PRO_SWIGLU = 2 };
+
+struct FArgs {
+    int B;              // sequences in this launch (rows of the activation)
+    const int* pos;     // [B] absolute position of each sequence's new token
+    int adt;            // activation dtype (Q8 / F16)
+    int K;              // activation width (GEMV input)
+    // PRO_COPY: activation rows in global memory
+    const uint8_t* xin; long xin_s;
+    // PRO_RESNORM
+    const uint8_t* xres; long xres_s;        // residual rows (adt)
+    const float* yadd; long yadd_s;          // fp32 rows requantized and added to the residual (or null)
+    int scale_y; float ys;                   // MiniCPM depth scale of the branch output
+    uint8_t* xout; long xout_s;              // new residual rows, written by block 0 (or null)
+    const uint8_t* emb; long emb_s; int emb_dt; const int32_t* tok; long tok_s; int n_vocab;
+    int scale_emb; float es;                 // MiniCPM embedding scale (x12)
+    const uint16_t* nw; const uint16_t* nb; int layer;  // norm gain / bias, LayerNorm if layer
+    int post; float ps;                      // MiniCPM pre-lm_head scale (1/9)
+    // PRO_SWIGLU: fp32 rows [gate | up], ffn columns each
+    const float* gu; long gu_s;
+    // GEMV
+    const uint8_t* W; long ws; int N;
+    float* Y; long ldy;
+    unsigned int* err;
+};
+
+// Shared memory plan of k_fgemv: [mbarriers 128][weight stages][xq rows][prep][fp32 row buffer]
+template <int WDT>
+__host__ __device__ inline size_t fgemv_smem(int nw, int mt, int K, int adt, int pro) {
+    const int nb = K / GTN_QBLK;
+    size_t s = 128 + (size_t)MM_STAGES * nw * 8 * mm_q_tile_stride<WDT>();
+    s += ((size_t)mt * row_bytes(adt, K) + 15) / 16 * 16;
+    s += (size_t)mt * nb * 4 * sizeof(LanePrep);
+    if (pro == PRO_RESNORM) s += (size_t)mt * K * sizeof(float);
+    return s;
+}
+
+// Builds the MT activation rows of this launch in shared memory (xq), per the prologue kind.
+template <int PRO, int MT>
+__device__ __forceinline__ void fgemv_prologue(const FArgs& a, uint8_t* xq, float* sval, int m0, int mt) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
+    const int K = a.K, nbk = (K + GTN_QBLK - 1) / GTN_QBLK;
+    const long xrb = row_bytes(a.adt, K);
+    if (PRO == PRO_COPY) {
+        for (int m = 0; m < mt; ++m) {
+            const uint8_t* src = a.xin + (long)(m0 + m) * a.xin_s;
+            uint8_t* dst = xq + (long)m * xrb;
+            if ((((uintptr_t)src) & 3) == 0 && (xrb & 3) == 0) {
+                for (int i = tid; i < xrb / 4; i += blockDim.x)
+                    reinterpret_cast<uint32_t*>(dst)[i] = reinterpret_cast<const uint32_t*>(src)[i];
+            } else {
+                for (int i = tid; i < xrb; i += blockDim.x) dst[i] = src[i];
+            }
+        }
+        return;
+    }
+    if (PRO == PRO_SWIGLU) {
+        // ops.cpp:733-772 then 918-970: silu on the requantized gate, requantized, times the
+        // requantized up projection, requantized (tinyllama.cpp:88-97).
+        for (int m = 0; m < mt; ++m) {
+            const float* g = a.gu + (long)(m0 + m) * a.gu_s;
+            const float* u = g + K;
+            for (int blk = warp; blk < nbk; blk += nwarps) {
+                const int i = blk * GTN_QBLK + lane, nv = min(GTN_QBLK, K - blk * GTN_QBLK);
+                const float gv = requant(i < K ? g[i] : 0.0f, lane, nv, a.adt, nullptr, blk);
+                const float den = 1.0f + exp_cr(-gv);
+                const float sv = requant(gv / den, lane, nv, a.adt, nullptr, blk);
+                const float uv = requant(i < K ? u[i] : 0.0f, lane, nv, a.adt, nullptr, blk);
+                requant(sv * uv, lane, nv, a.adt, xq + (long)m * xrb, blk);
+            }
+        }
+        return;
+    }
+    // PRO_RESNORM: residual update, then the norm's sequential sums (one thread per row).
+    for (int m = 0; m < mt; ++m) {
+        float* sv = sval + (long)m * K;
+        uint8_t* xo = (a.xout && blockIdx.x == 0) ? a.xout + (long)(m0 + m) * a.xout_s : nullptr;
+        const uint8_t* xr = a.xres ? a.xres + (long)(m0 + m) * a.xres_s : nullptr;
+        const uint8_t* er = nullptr;
+        if (a.emb) {
+            int t = a.tok[(long)(m0 + m) * a.tok_s + a.pos[m0 + m]];
+            if (t < 0 || t >= a.n_vocab) {
+                if (tid == 0 && blockIdx.x == 0 && a.err) atomicOr(a.err, GTN_DEVERR_TOKEN);
+                t = 0;
+            }
+            er = a.emb + (long)t * a.emb_s;
+        }
+        for (int blk = warp; blk < nbk; blk += nwarps) {
+            const int i = blk * GTN_QBLK + lane, nv = min(GTN_QBLK, K - blk * GTN_QBLK);
+            float r;
+            if (er) {
+                // token_embed (ops.cpp:526-545): Q8 / fp16 rows copied, Q4 rows requantized to Q8
+                const float e = i < K ? load_elem(er, a.emb_dt, i) : 0.0f;
+                if (a.emb_dt == a.adt) {
+                    r = e;
+                    if (xo && i < K) {
+                        if (a.adt == GTN_Q8) {
+                            const uint8_t* sb = er + (long)blk * GTN_Q8_BYTES;
+                            uint8_t* db = xo + (long)blk * GTN_Q8_BYTES;
+                            if (lane < 2) db[lane] = sb[lane];
+                            db[2 + lane] = sb[2 + lane];
+                        } else {
+                            reinterpret_cast<uint16_t*>(xo)[i] = reinterpret_cast<const uint16_t*>(er)[i];
+                        }
+                    }
+                    if (a.scale_emb) r = requant(r * a.es, lane, nv, a.adt, xo, blk);  // minicpm.cpp:96
+                } else {
+                    r = requant(e, lane, nv, a.adt, a.scale_emb ? nullptr : xo, blk);
+                    if (a.scale_emb) r = requant(r * a.es, lane, nv, a.adt, xo, blk);
+                }
+            } else {
+                const float xv = i < K ? load_elem(xr, a.adt, i) : 0.0f;
+                if (a.yadd) {
+                    const float* y = a.yadd + (long)(m0 + m) * a.yadd_s;
+                    float o = requant(i < K ? y[i] : 0.0f, lane, nv, a.adt, nullptr, blk);
+                    if (a.scale_y) o = requant(o * a.ys, lane, nv, a.adt, nullptr, blk);  // minicpm.cpp:57-58
+                    r = requant(xv + o, lane, nv, a.adt, xo, blk);                        // ops::add
+                } else {
+                    r = xv;
+                }
+            }
+            if (i < K) sv[i] = r;
+        }
+    }
+    __syncthreads();
+    __shared__ float stat[MT][2];
+    if (tid < mt) {
+        const float* v = sval + (long)tid * K;
+        if (a.layer) {
+            float sum = 0.0f;
+            for (int i = 0; i < K; ++i) sum = sum + v[i];
+            const float mean = sum / (float)K;
+            float ss = 0.0f;
+            for (int i = 0; i < K; ++i) {
+                const float d = v[i] - mean;
+                const float d2 = d * d;
+                ss = ss + d2;
+            }
+            stat[tid][0] = mean;
+            stat[tid][1] = sqrtf(ss / (float)K);
+        } else {
+            float sq = 0.0f;
+#pragma unroll 16
+            for (int i = 0; i < K; ++i) {
+                const float p = v[i] * v[i];
+                sq = sq + p;
+            }
+            stat[tid][0] = 0.0f;
+            stat[tid][1] = sqrtf(sq / (float)K);
+        }
+    }
+    __syncthreads();
+    for (int m = 0; m < mt; ++m) {
+        const float* v = sval + (long)m * K;
+        const float mean = stat[m][0], sd = stat[m][1];
+        for (int blk = warp; blk < nbk; blk += nwarps) {
+            const int i = blk * GTN_QBLK + lane, nv = min(GTN_QBLK, K - blk * GTN_QBLK);
+            float y = 0.0f;
+            if (i < K) {
+                if (a.layer) {
+                    const float dd = v[i] - mean;
+                    const float t = dd / (sd + 1e-05f);
+                    const float u = t * h2f(a.nw[i]);
+                    y = u + h2f(a.nb[i]);
+                } else {
+                    const float t = v[i] / (sd + 1e-6f);
+                    y = t * h2f(a.nw[i]);
+                }
+            }
+            if (a.post) {
+                const float nq = requant(y, lane, nv, a.adt, nullptr, blk);
+                requant(nq * a.ps, lane, nv, a.adt, xq + (long)m * xrb, blk);
+            } else {
+                requant(y, lane, nv, a.adt, xq + (long)m * xrb, blk);
+            }
+        }
+    }
+}
+
+// Fused GEMV: prologue (activation rows into shared memory) + the exact Q8/Q4 GEMV of k_mm_q.
+// grid.x = ceil(N / (8*NW)); rows of the launch: B <= MT.
+template <int WDT, int NW, int MT, int PRO>
+__global__ void __launch_bounds__(NW * 32) k_fgemv(const FArgs a) {
+    using C = MMCfg<WDT>;
+    constexpr int ROWS = NW * 8;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int abort_flag;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+    const int tstride = mm_q_tile_stride<WDT>();
+    uint8_t* stages = smem + 128;
+    const int K = a.K, nb = K / GTN_QBLK;
+    uint8_t* xq = stages + (size_t)MM_STAGES * ROWS * tstride;
+    const size_t xq_bytes = ((size_t)MT * row_bytes(a.adt, K) + 15) / 16 * 16;
+    LanePrep* prep = reinterpret_cast<LanePrep*>(xq + xq_bytes);
+    float* sval = reinterpret_cast<float*>(prep + (size_t)MT * nb * 4);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int r_local = warp * 8 + (lane >> 2), l = lane & 3;
+    const int row0 = blockIdx.x * ROWS;
+    const int nrows = min(ROWS, a.N - row0);
+    const int m0 = blockIdx.y * MT;
+    const int mt = min(MT, a.B - m0);
+    const int nkt = (nb + C::KT_BLOCKS - 1) / C::KT_BLOCKS;
+    const uint8_t* W = a.W;
+    const long w_stride = a.ws;
+
+    auto issue = [&](int kt) {
+        const int s = kt % MM_STAGES;
+        const int b0 = kt * C::KT_BLOCKS;
+        const int nbt = min(C::KT_BLOCKS, nb - b0);
+        uint32_t total = 0;
+        for (int r = 0; r < nrows; ++r) {
+            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + r) * w_stride +
+                                  (uintptr_t)b0 * C::BLK_BYTES;
+            total += ((uint32_t)(src & 15) + nbt * C::BLK_BYTES + 15) & ~15u;
+        }
+        if (lane == 0) mbar_arrive_expect_tx(&bars[s], total);
+        __syncwarp();
+        for (int r = lane; r < nrows; r += 32) {
+            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + r) * w_stride +
+                                  (uintptr_t)b0 * C::BLK_BYTES;
+            const uint32_t off = (uint32_t)(src & 15);
+            bulk_g2s(stages + ((size_t)s * ROWS + r) * tstride, reinterpret_cast<const void*>(src - off),
+                     (off + nbt * C::BLK_BYTES + 15) & ~15u, &bars[s]);
+        }
+    };
+
+    if (tid == 0) {
+        for (int s = 0; s < MM_STAGES; ++s) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+    if (warp == 0)
+        for (int kt = 0; kt < min(MM_STAGES, nkt); ++kt) issue(kt);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    fgemv_prologue<PRO, MT>(a, xq, sval, m0, mt);
+    __syncthreads();
+    build_prep_q8(xq, row_bytes(GTN_Q8, K), 0, mt, nb, prep);
+    __syncthreads();
+
+    float acc[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+    for (int kt = 0; kt < nkt; ++kt) {
+        const int s = kt % MM_STAGES;
+        if (!abort_flag && !mbar_wait_bounded(&bars[s], (kt / MM_STAGES) & 1, a.err)) abort_flag = 1;
+        const int b0 = kt * C::KT_BLOCKS;
+        const int nbt = min(C::KT_BLOCKS, nb - b0);
+        if (!abort_flag && r_local < nrows) {
+            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + r_local) * w_stride +
+                                  (uintptr_t)b0 * C::BLK_BYTES;
+            const uint8_t* t = stages + ((size_t)s * ROWS + r_local) * tstride + (src & 15);
+#pragma unroll 4
+            for (int b = 0; b < nbt; ++b) {
+                const uint8_t* p = t + b * C::BLK_BYTES;
+                const float dw = h2f(ld_u16(p));
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    if (m < mt) {
+                        const LanePrep av = prep[((size_t)m * nb + b0 + b) * 4 + l];
+                        const int L = WDT == GTN_Q8 ? q8_block_lane_dot(p, l, av) : q4_block_lane_dot(p, l, av);
+                        const float sc = av.da * dw;
+                        const float pr = (float)L * sc;
+                        acc[m] = acc[m] + pr;
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (warp == 0 && !abort_flag && kt + MM_STAGES < nkt) issue(kt + MM_STAGES);
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (abort_flag) {
+        drain_stages(bars, nkt, tid);
+        return;
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        const float t01 = acc[m] + __shfl_xor_sync(0xffffffffu, acc[m], 1);
+        const float t = t01 + __shfl_xor_sync(0xffffffffu, t01, 2);
+        if (l == 0 && r_local < nrows && m < mt) a.Y[(long)(m0 + m) * a.ldy + row0 + r_local] = t;
+    }
+}
+
+// ---- attention with the q/k/v epilogue of the stacked projection ----------------------------
+struct AArgs {
+    int adt, q_heads, kv_heads, d;          // d = head size (64)
+    const int* pos;                          // [B]
+    const float* y; long ys;                 // stacked q|k|v fp32 rows
+    const uint16_t *bq, *bk, *bv;            // Zephyr biases (or null)
+    const float2* cs; int half;              // RoPE table [pos][half] (cos, sin), half = rd/2
+    uint8_t* kc; uint8_t* vc; long kvs;      // cache rows of this layer (row stride kvs bytes)
+    long seq_stride;                         // bytes between sequences in the cache
+    uint8_t* out; long os;                   // attention output rows (adt)
+    unsigned int* err;
+};
+
+// One Linear output head (d values starting at column c0 of row y) through the reference's
+// epilogue: requant (Linear) [-> + bias -> requant (bias_add_inplace)] [-> RoPE -> requant].
+// Warp-cooperative; writes the resulting head bytes to `dst` (row_bytes(adt, d)).
+__device__ __forceinline__ void head_epilogue(const AArgs& a, const float* yrow, int c0, const uint16_t* bias,
+                                              bool rope, int p, uint8_t* dst, float* tmp) {
+    const int lane = threadIdx.x & 31;
+    const int nbh = a.d / GTN_QBLK;
+    for (int k = 0; k < nbh; ++k) {
+        const int i = k * GTN_QBLK + lane;
+        float v = requant(yrow[c0 + i], lane, GTN_QBLK, a.adt, nullptr, 0);
+        if (bias) v = requant(v + h2f(bias[i]), lane, GTN_QBLK, a.adt, nullptr, 0);  // bias: this head's slice
+        tmp[i] = v;
+    }
+    __syncwarp();
+    for (int k = 0; k < nbh; ++k) {
+        const int i = k * GTN_QBLK + lane;
+        float y = tmp[i];
+        if (rope) {
+            const float2* c = a.cs + (long)p * a.half;
+            if (i < a.half) {
+                const float2 t = c[i];
+                const float p0 = tmp[i] * t.x, p1 = tmp[i + a.half] * t.y;
+                y = p0 - p1;
+            } else if (i < 2 * a.half) {
+                const float2 t = c[i - a.half];
+                const float p2 = tmp[i - a.half] * t.y, p3 = tmp[i] * t.x;
+                y = p2 + p3;
+            }
+            requant(y, lane, GTN_QBLK, a.adt, dst, k);
+        } else {
+            requant(y, lane, GTN_QBLK, a.adt, dst, k);
+        }
+    }
+    __syncwarp();
+}
+
+// grid (q_heads, B); block ATT_THREADS. Decode attention of sequence b at position p = pos[b]
+// (keys 0..p), preceded by the q/k/v epilogue; the q-head 0 of each kv group writes the new K/V
+// cache rows. Key p is taken from this CTA's own epilogue values.
+static __global__ void __launch_bounds__(ATT_THREADS) k_fattn(const AArgs a) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    __shared__ __align__(16) uint8_t qh[256 * 2], kh[256 * 2], vh[256 * 2];
+    __shared__ float tmp[3][256];
+    __shared__ float red[ATT_THREADS / 32];
+    __shared__ float s_stat[2];
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int group = a.q_heads / a.kv_heads, g = h / group;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int d = a.d;
+    const long hb = row_bytes(a.adt, d);
+    const int p = a.pos[b], n = p + 1;
+    const float* yrow = a.y + (long)b * a.ys;
+    const int qd = a.q_heads * d, kvd = a.kv_heads * d;
+    const bool rope = a.half > 0;
+    if (warp == 0) head_epilogue(a, yrow, h * d, a.bq ? a.bq + h * d : nullptr, rope, p, qh, tmp[0]);
+    if (warp == 1) head_epilogue(a, yrow, qd + g * d, a.bk ? a.bk + g * d : nullptr, rope, p, kh, tmp[1]);
+    if (warp == 2) head_epilogue(a, yrow, qd + kvd + g * d, a.bv ? a.bv + g * d : nullptr, false, p, vh, tmp[2]);
+    __syncthreads();
+    uint8_t* kc = a.kc + (long)b * a.seq_stride;
+    uint8_t* vc = a.vc + (long)b * a.seq_stride;
+    if (h % group == 0) {
+        for (int i = tid; i < hb; i += ATT_THREADS) {
+            kc[(long)p * a.kvs + (long)g * hb + i] = kh[i];
+            vc[(long)p * a.kvs + (long)g * hb + i] = vh[i];
+        }
+    }
+    float* pr = reinterpret_cast<float*>(sm);
+    uint8_t* vt = sm + ((n * 4 + 15) / 16) * 16;
+    float* part = reinterpret_cast<float*>(vt + (long)ATT_VTILE * hb);
+    const float scale = 1.0f / sqrtf((float)d);
+    float mx = -INFINITY;
+    for (int j = tid; j < n; j += ATT_THREADS) {
+        const uint8_t* kr = j == p ? kh : kc + (long)j * a.kvs + (long)g * hb;
+        const float dd = head_dot(qh, kr, a.adt, d);
+        const float sc = dd * scale;
+        pr[j] = sc;
+        mx = fmaxf(mx, sc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        float m = red[0];
+        for (int w = 1; w < ATT_THREADS / 32; ++w) m = fmaxf(m, red[w]);
+        s_stat[0] = m;
+    }
+    __syncthreads();
+    const float m = s_stat[0];
+    for (int j = tid; j < n; j += ATT_THREADS) pr[j] = exp_cr(pr[j] - m);
+    __syncthreads();
+    if (tid == 0) {
+        float sum = 0.0f;
+#pragma unroll 8
+        for (int j = 0; j < n; ++j) sum = sum + pr[j];
+        s_stat[1] = sum;
+    }
+    __syncthreads();
+    const float sum = s_stat[1];
+    for (int blk = warp; blk * GTN_QBLK < n; blk += ATT_THREADS / 32) {
+        const int j = blk * GTN_QBLK + lane;
+        const float pj = j < n ? pr[j] / sum : 0.0f;
+        const float back = requant(pj, lane, min(GTN_QBLK, n - blk * GTN_QBLK), a.adt, nullptr, 0);
+        __syncwarp();
+        if (j < n) pr[j] = back;
+    }
+    __syncthreads();
+    const int n8 = (n / 8) * 8;
+    const int npairs = d * 8;
+    const int per = (npairs + ATT_THREADS - 1) / ATT_THREADS;
+    float acc[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc[u] = 0.0f;
+    for (int t0 = 0; t0 < n; t0 += ATT_VTILE) {
+        const int nt = min(ATT_VTILE, n - t0);
+        if ((hb & 3) == 0 && (a.kvs & 3) == 0) {
+            const int wpr = (int)(hb / 4);
+            for (int i = tid; i < nt * wpr; i += ATT_THREADS) {
+                const int jj = i / wpr, ww = i % wpr;
+                const int j = t0 + jj;
+                const uint32_t* src = j == p ? reinterpret_cast<const uint32_t*>(vh)
+                                             : reinterpret_cast<const uint32_t*>(vc + (long)j * a.kvs + (long)g * hb);
+                reinterpret_cast<uint32_t*>(vt + (long)jj * hb)[ww] = src[ww];
+            }
+        } else {
+            for (int i = tid; i < nt * hb; i += ATT_THREADS) {
+                const int jj = i / hb, bb = i % hb;
+                const int j = t0 + jj;
+                vt[i] = j == p ? vh[bb] : vc[(long)j * a.kvs + (long)g * hb + bb];
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int pi = tid + u * ATT_THREADS;
+            if (u < per && pi < npairs) {
+                const int c = pi >> 3, l = pi & 7;
+                float acu = acc[u];
+                for (int jj = l; jj < nt && t0 + jj < n8; jj += 8) {
+                    const float vv = load_elem(vt + (long)jj * hb, a.adt, c);
+                    const float pp = pr[t0 + jj] * vv;
+                    acu = pp + acu;
+                }
+                acc[u] = acu;
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        const int pi = tid + u * ATT_THREADS;
+        if (u < per && pi < npairs) part[(pi & 7) * d + (pi >> 3)] = acc[u];
+    }
+    __syncthreads();
+    asm volatile("griddepcontrol.launch_dependents;");
+    uint8_t* dst = a.out + (long)b * a.os + (long)h * hb;
+    for (int blk = warp; blk * GTN_QBLK < d; blk += ATT_THREADS / 32) {
+        const int c = blk * GTN_QBLK + lane;
+        float y = 0.0f;
+        if (c < d) {
+            y = part[c] + part[d + c];
+            for (int l = 2; l < 8; ++l) y = y + part[l * d + c];
+            for (int j = n8; j < n; ++j) {
+                const uint8_t* vr = j == p ? vh : vc + (long)j * a.kvs + (long)g * hb;
+                const float vv = load_elem(vr, a.adt, c);
+                const float pp = pr[j] * vv;
+                y = y + pp;
+            }
+        }
+        store_row_elem(dst, a.adt, blk, lane, d, y);
+    }
+}
+
+inline size_t fattn_smem(int n, int adt, int d) {
+    return (size_t)((n * 4 + 15) / 16) * 16 + (size_t)ATT_VTILE * row_bytes(adt, d) + (size_t)8 * d * 4 + 16;
+}
+
+// Greedy pick per sequence (sampler.cpp:30-41) + the decode loop's bookkeeping: the id becomes the
+// input token of the next position and is recorded; the position advances. grid B; block 1024.
+static __global__ void k_fargmax(const float* logits, long ls, int n, int32_t* tok, int32_t* gen, long tok_s,
+                                 int* pos, int max_ctx, unsigned int* err) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    __shared__ float bv[1024];
+    __shared__ int bi[1024];
+    const int b = blockIdx.x;
+    const float* xr = logits + (long)b * ls;
+    const int t = threadIdx.x, nt = blockDim.x;
+    const int per = (n + nt - 1) / nt;
+    float best = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int j = t * per; j < min(n, (t + 1) * per); ++j) {
+        const float v = xr[j];
+        if (v > best) { best = v; idx = j; }
+    }
+    bv[t] = best;
+    bi[t] = idx;
+    __syncthreads();
+    for (int s = nt / 2; s > 0; s >>= 1) {
+        if (t < s) {
+            const float v2 = bv[t + s];
+            const int i2 = bi[t + s];
+            if (v2 > bv[t] || (v2 == bv[t] && i2 < bi[t])) { bv[t] = v2; bi[t] = i2; }
+        }
+        __syncthreads();
+    }
+    if (t == 0) {
+        const int id = bi[0] == 0x7fffffff ? 0 : bi[0];
+        const int p = pos[b];
+        if (p + 1 < max_ctx) {
+            tok[(long)b * tok_s + p + 1] = id;
+            gen[(long)b * tok_s + p + 1] = id;
+            pos[b] = p + 1;
+        } else if (err) {
+            atomicOr(err, 4u);
+        }
+    }
+}
+
+}  // namespace gtn

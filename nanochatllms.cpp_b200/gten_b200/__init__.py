@@ -57,6 +57,7 @@ def lib() -> C.CDLL:
         L.gtn_model_logits.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
         L.gtn_model_generate.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
         L.gtn_model_generate_device.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.gtn_model_generate_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
         L.gtn_model_stream.argtypes = [C.c_void_p]
         L.gtn_model_stream.restype = C.c_void_p
         L.gtn_model_check.argtypes = [C.c_void_p]
@@ -250,6 +251,15 @@ class Model:
         p = np.ascontiguousarray(prompt, np.int32)
         out = np.zeros(n_gen, np.int32)
         _check(lib().gtn_model_generate(self._h, p.ctypes.data, p.size, n_gen, out.ctypes.data), "model_generate")
+        return out
+
+    def generate_batch(self, prompts, n_gen: int):
+        """prompts: [batch, n_prompt] int32 (host); returns [batch, n_gen] greedy ids."""
+        import numpy as np
+        p = np.ascontiguousarray(prompts, np.int32)
+        out = np.zeros((p.shape[0], n_gen), np.int32)
+        _check(lib().gtn_model_generate_batch(self._h, p.ctypes.data, p.shape[0], p.shape[1], n_gen, out.ctypes.data),
+               "model_generate_batch")
         return out
 
     def generate_device(self, prompt_dev, n_gen: int, out_dev) -> None:

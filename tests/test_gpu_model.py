@@ -52,6 +52,27 @@ def test_custom_model_matches_oracle(orc, gpu, name, wdt):
     m.close()
 
 
+@pytest.mark.parametrize("name", list(CUSTOM))
+@pytest.mark.parametrize("wdt", [Q8, Q4])
+@pytest.mark.parametrize("batch", [3, 11])
+def test_batched_generation_matches_single_sequences(orc, gpu, name, wdt, batch):
+    """The reference has no batching: each sequence of a batch must produce exactly the ids the
+    oracle gives for it alone (batch 11 exercises a second 8-row tile of the fused GEMVs)."""
+    from oracle.oracle import OracleModel
+    dims = CUSTOM[name]
+    img = gtenfile.synthetic_image(6, wdt, 77, cpu_pack(orc), dims=dims, std=0.05, gain_std=0.1)
+    n_prompt, n_gen = 13, 9
+    max_ctx = 2 * (n_prompt + n_gen)
+    prompts = np.random.default_rng(batch).integers(0, dims[0], (batch, n_prompt)).astype(np.int32)
+    m = G.Model(G.CUSTOM, wdt, max_ctx, max_batch=batch, dims=dims)
+    m.load(img)
+    got = m.generate_batch(prompts, n_gen)
+    for b in range(batch):
+        om = OracleModel(orc, 6, wdt, max_ctx, img, dims=dims)
+        assert np.array_equal(got[b], om.greedy(prompts[b], n_gen)), f"sequence {b}"
+    m.close()
+
+
 def test_load_rejects_bad_images(orc, gpu):
     dims = CUSTOM["llama"]
     img = gtenfile.synthetic_image(6, Q8, 1, cpu_pack(orc), dims=dims)
