@@ -3,6 +3,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
+#include <map>
 #include <mutex>
 
 #include "launch.cuh"
@@ -30,6 +31,18 @@ static int cuda_status(cudaError_t e, const char* what) {
 
 static std::atomic<unsigned long long> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+bool smem_attr_needed(const void* kern, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, size_t> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    size_t& cur = done[{kern, dev}];
+    if (cur >= smem) return false;
+    cur = smem;
+    return true;
+}
 
 __device__ unsigned int g_dev_err;
 

@@ -61,7 +61,8 @@ struct gtn_model {
     // rows (x after attention input, h after attention), stacked projection outputs
     bool fused = false;
     int* pos = nullptr;
-    uint8_t *rx = nullptr, *rh = nullptr, *datt = nullptr;
+    uint8_t *rx = nullptr, *rh = nullptr, *datt = nullptr, *act = nullptr;
+    long act_s = 0;
     float *yqkv = nullptr, *yo = nullptr, *ygu = nullptr, *yd = nullptr;
     long ldqkv = 0, ldgu = 0;
     cudaGraphExec_t graph = nullptr;
@@ -219,6 +220,8 @@ int gtn_model_create(int kind, int wdtype, int max_ctx, int max_batch, const int
         rc |= dalloc(m.get(), &m->rx, B * row_bytes(adt, m->d));
         rc |= dalloc(m.get(), &m->rh, B * row_bytes(adt, m->d));
         rc |= dalloc(m.get(), &m->datt, B * row_bytes(adt, m->max_q));
+        m->act_s = (std::max(row_bytes(adt, m->d), row_bytes(adt, m->max_ffn)) + 15) / 16 * 16;
+        rc |= dalloc(m.get(), &m->act, B * m->act_s);
         rc |= dalloc(m.get(), &m->yqkv, sizeof(float) * B * m->ldqkv);
         rc |= dalloc(m.get(), &m->yo, sizeof(float) * B * m->d);
         rc |= dalloc(m.get(), &m->ygu, sizeof(float) * B * m->ldgu);
@@ -536,15 +539,34 @@ static cudaError_t fg_mt(const FArgs& a, cudaStream_t st, bool dry) {
     return big ? fg_launch<WDT, 4, 8, PRO>(a, st, dry) : fg_launch<WDT, 1, 8, PRO>(a, st, dry);
 }
 
+// A GEMV whose activation needs a prologue (residual + norm, or SwiGLU) runs it once in k_prep
+// (one CTA per sequence) into m->act; the GEMV then copies that row.
 static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) {
-    if (m->wdt == GTN_Q8) {
-        if (pro == PRO_COPY) return fg_mt<GTN_Q8, PRO_COPY>(a, m->st, dry);
-        if (pro == PRO_RESNORM) return fg_mt<GTN_Q8, PRO_RESNORM>(a, m->st, dry);
-        return fg_mt<GTN_Q8, PRO_SWIGLU>(a, m->st, dry);
+    FArgs g = a;
+    if (pro != PRO_COPY) {
+        const size_t smem = pro == PRO_RESNORM ? sizeof(float) * (size_t)a.K : 0;
+        cudaError_t e;
+        if (pro == PRO_RESNORM) {
+            if (dry) {
+                e = ensure_smem(k_prep<PRO_RESNORM>, smem);
+            } else {
+                ++g_step_kernels;
+                e = launch_pdl(k_prep<PRO_RESNORM>, dim3(1, a.B), dim3(1024), smem, m->st, a, m->act, m->act_s);
+            }
+        } else {
+            if (dry) {
+                e = ensure_smem(k_prep<PRO_SWIGLU>, smem);
+            } else {
+                ++g_step_kernels;
+                e = launch_pdl(k_prep<PRO_SWIGLU>, dim3(1, a.B), dim3(1024), smem, m->st, a, m->act, m->act_s);
+            }
+        }
+        if (e != cudaSuccess) return e;
+        g.xin = m->act;
+        g.xin_s = m->act_s;
     }
-    if (pro == PRO_COPY) return fg_mt<GTN_Q4, PRO_COPY>(a, m->st, dry);
-    if (pro == PRO_RESNORM) return fg_mt<GTN_Q4, PRO_RESNORM>(a, m->st, dry);
-    return fg_mt<GTN_Q4, PRO_SWIGLU>(a, m->st, dry);
+    if (m->wdt == GTN_Q8) return fg_mt<GTN_Q8, PRO_COPY>(g, m->st, dry);
+    return fg_mt<GTN_Q4, PRO_COPY>(g, m->st, dry);
 }
 
 // One greedy decode step for sequences 0..B-1 at positions m->pos[b] (their input tokens are at

@@ -172,7 +172,15 @@ __device__ __forceinline__ void fgemv_prologue(const FArgs& a, uint8_t* xq, floa
     }
     __syncthreads();
     __shared__ float stat[MT][2];
-    if (tid < mt) {
+    if (mt == 1 && !a.layer) {
+        // one row: the exact parallel form of the sequential sum of squares (seqsum.cuh)
+        __shared__ SeqSumSmem ss;
+        const float sq = seq_sum_squares(sval, K, ss);
+        if (tid == 0) {
+            stat[0][0] = 0.0f;
+            stat[0][1] = sqrtf(sq / (float)K);
+        }
+    } else if (tid < mt) {
         const float* v = sval + (long)tid * K;
         if (a.layer) {
             float sum = 0.0f;
@@ -329,6 +337,18 @@ __global__ void __launch_bounds__(NW * 32) k_fgemv(const FArgs a) {
         const float t = t01 + __shfl_xor_sync(0xffffffffu, t01, 2);
         if (l == 0 && r_local < nrows && m < mt) a.Y[(long)(m0 + m) * a.ldy + row0 + r_local] = t;
     }
+}
+
+// Computes the activation rows of one GEMV once (residual update + norm, or the SwiGLU chain) and
+// writes them to `act` (row stride act_s bytes); grid (1, B), block 1024, dynamic smem K floats
+// for RESNORM. It lets the following GEMV launch at once, so its weight prefetch overlaps this.
+template <int PRO>
+static __global__ void __launch_bounds__(1024) k_prep(const FArgs a, uint8_t* act, long act_s) {
+    extern __shared__ float sval[];
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int m = blockIdx.y;
+    fgemv_prologue<PRO, 1>(a, act + (long)m * act_s, sval, m, 1);
 }
 
 // ---- attention with the q/k/v epilogue of the stacked projection ----------------------------

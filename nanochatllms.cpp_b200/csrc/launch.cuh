@@ -37,9 +37,14 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
     return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
+// True when `kern` on the current device has not yet been allowed `smem` bytes of dynamic shared
+// memory (records the new maximum).
+bool smem_attr_needed(const void* kern, size_t smem);
+
 template <typename K>
 inline cudaError_t ensure_smem(K kern, size_t smem) {
     if (smem <= 48 * 1024) return cudaSuccess;
+    if (!smem_attr_needed(reinterpret_cast<const void*>(kern), smem)) return cudaSuccess;
     return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
 

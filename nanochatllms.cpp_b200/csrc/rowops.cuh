@@ -7,6 +7,7 @@
 // which is write_row_from_float / q8_quantize_row (ops.cpp:87-123, quants.cpp:140-158).
 #pragma once
 #include "common.cuh"
+#include "seqsum.cuh"
 
 namespace gtn {
 
@@ -74,7 +75,15 @@ static __global__ void k_norm(const uint8_t* x, long xs, long hs, uint8_t* out, 
     const uint8_t* src = x + (long)row * xs + (long)h * hs;
     for (int i = threadIdx.x; i < n; i += blockDim.x) v[i] = load_elem(src, dt, i);
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (!LAYER) {
+        // the sequential sum of squares, computed exactly in parallel (seqsum.cuh)
+        __shared__ SeqSumSmem ss;
+        const float sq = seq_sum_squares(v, n, ss);
+        if (threadIdx.x == 0) {
+            stat[0] = 0.0f;
+            stat[1] = sqrtf(sq / (float)n);
+        }
+    } else if (threadIdx.x == 0) {
         if (LAYER) {
             float sum = 0.0f;
             for (int i = 0; i < n; ++i) sum = sum + v[i];

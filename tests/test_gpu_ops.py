@@ -90,6 +90,36 @@ def test_norms(orc, gpu, dt, D):
     assert np.array_equal(from_dev(out)[rb:], orc.layer_norm(x, dt, M, D, w, b, 1)[rb:])
 
 
+@pytest.mark.parametrize("D", [2048, 2304, 64, 1000])
+def test_rms_norm_sequential_sum_adversarial(orc, gpu, D):
+    """The RMSNorm sum of squares is computed by an exact parallel emulation of the reference's
+    sequential fp32 loop (seqsum.cuh): rows built to stress binade crossings, ties, zeros and
+    extreme ranges must still match the serial loop bit for bit."""
+    rng = np.random.default_rng(D)
+    rows = [
+        rng.standard_normal(D),
+        np.ones(D),
+        np.full(D, 3.0),
+        2.0 ** rng.integers(-20, 20, D),
+        np.concatenate([np.zeros(D // 2), rng.standard_normal(D - D // 2)]),
+        np.zeros(D),
+        np.where(rng.random(D) < 0.01, 1e6, 1e-3) * rng.standard_normal(D),
+        1.0 + 2.0 ** -12 * rng.integers(0, 8, D),          # short mantissas: rounding ties
+        np.sqrt(np.arange(1, D + 1, dtype=np.float64)),   # squares near integers
+        rng.standard_normal(D) * 1e-20,                    # subnormal squares
+        np.linspace(1e-3, 1e3, D),
+    ]
+    x = np.stack(rows).astype(np.float32)
+    M = x.shape[0]
+    w = fp16_vec(rng, D)
+    out = torch.zeros(M * D * 4, dtype=torch.uint8, device=gpu)
+    G.rms_norm(G.GT(to_dev(x, gpu), F32, (M, D)), G.GT(to_dev(w, gpu), F16, (D,)), G.GT(out, F32, (M, D)))
+    want = orc.rms_norm(x.view(np.uint8).ravel().copy(), F32, M, D, w, 0)
+    got = from_dev(out)
+    for r in range(M):
+        assert np.array_equal(got[r * D * 4:(r + 1) * D * 4], want[r * D * 4:(r + 1) * D * 4]), f"row {r}"
+
+
 @pytest.mark.parametrize("dt", [Q8, F16])
 def test_rms_norm_3d(orc, gpu, dt):
     rng = np.random.default_rng(3 + dt)
