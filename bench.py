@@ -342,7 +342,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--wdtype", type=int, default=3, choices=[1, 3, 4], help="1 fp16, 3 q8, 4 q4")
+    ap.add_argument("--gemv-only", action="store_true",
+                    help="only the exact GEMV sweep on TinyLlama's shapes (M=1), e.g. for profiling")
     args = ap.parse_args()
+    if args.gemv_only:
+        import torch
+
+        import gten_b200 as G
+        hbm, _ = peaks()
+        _, sweep = gemv_roofline(G, torch, args.wdtype, torch.device("cuda", 0), hbm)
+        print(json.dumps({"gemv_sweep": sweep, "wdtype": WDT_NAMES[args.wdtype]}), flush=True)
+        return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -553,13 +553,12 @@ static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) 
                 ++g_step_kernels;
                 e = launch_pdl(k_prep<PRO_RESNORM>, dim3(1, a.B), dim3(1024), smem, m->st, a, m->act, m->act_s);
             }
+        } else if (!dry) {
+            ++g_step_kernels;
+            const int nbk = (a.K + GTN_QBLK - 1) / GTN_QBLK;
+            e = launch_pdl(k_prep_swiglu, dim3((nbk + 31) / 32, a.B), dim3(1024), 0, m->st, a, m->act, m->act_s);
         } else {
-            if (dry) {
-                e = ensure_smem(k_prep<PRO_SWIGLU>, smem);
-            } else {
-                ++g_step_kernels;
-                e = launch_pdl(k_prep<PRO_SWIGLU>, dim3(1, a.B), dim3(1024), smem, m->st, a, m->act, m->act_s);
-            }
+            e = cudaSuccess;
         }
         if (e != cudaSuccess) return e;
         g.xin = m->act;

@@ -351,6 +351,24 @@ static __global__ void __launch_bounds__(1024) k_prep(const FArgs a, uint8_t* ac
     fgemv_prologue<PRO, 1>(a, act + (long)m * act_s, sval, m, 1);
 }
 
+// The SwiGLU activation is block-local, so it is spread over many CTAs: grid (ceil(blocks/32), B),
+// block 1024 (one warp per 32-element block).
+static __global__ void __launch_bounds__(1024) k_prep_swiglu(const FArgs a, uint8_t* act, long act_s) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int K = a.K, nbk = (K + GTN_QBLK - 1) / GTN_QBLK;
+    const int blk = blockIdx.x * 32 + (threadIdx.x >> 5), lane = threadIdx.x & 31, m = blockIdx.y;
+    if (blk >= nbk) return;
+    const float* g = a.gu + (long)m * a.gu_s;
+    const float* u = g + K;
+    const int i = blk * GTN_QBLK + lane, nv = min(GTN_QBLK, K - blk * GTN_QBLK);
+    const float gv = requant(i < K ? g[i] : 0.0f, lane, nv, a.adt, nullptr, blk);
+    const float den = 1.0f + exp_cr(-gv);
+    const float sv = requant(gv / den, lane, nv, a.adt, nullptr, blk);
+    const float uv = requant(i < K ? u[i] : 0.0f, lane, nv, a.adt, nullptr, blk);
+    requant(sv * uv, lane, nv, a.adt, act + (long)m * act_s, blk);
+}
+
 // ---- attention with the q/k/v epilogue of the stacked projection ----------------------------
 struct AArgs {
     int adt, q_heads, kv_heads, d;          // d = head size (64)
@@ -552,10 +570,9 @@ static __global__ void k_fargmax(const float* logits, long ls, int n, int32_t* t
     const int b = blockIdx.x;
     const float* xr = logits + (long)b * ls;
     const int t = threadIdx.x, nt = blockDim.x;
-    const int per = (n + nt - 1) / nt;
     float best = -INFINITY;
     int idx = 0x7fffffff;
-    for (int j = t * per; j < min(n, (t + 1) * per); ++j) {
+    for (int j = t; j < n; j += nt) {  // coalesced; each thread keeps its first maximum
         const float v = xr[j];
         if (v > best) { best = v; idx = j; }
     }

@@ -268,10 +268,9 @@ static __global__ void k_argmax(const float* x, int n, int32_t* out, long out_st
     __shared__ int bi[1024];
     const float* xr = x + (long)blockIdx.x * x_stride;
     const int t = threadIdx.x, nt = blockDim.x;
-    const int per = (n + nt - 1) / nt;
     float best = -INFINITY;
     int idx = 0x7fffffff;
-    for (int j = t * per; j < min(n, (t + 1) * per); ++j) {
+    for (int j = t; j < n; j += nt) {  // coalesced; each thread keeps its first maximum
         const float v = xr[j];
         if (v > best) { best = v; idx = j; }
     }

@@ -30,6 +30,7 @@ struct SeqSumSmem {
     double scan[SEQSUM_THREADS_MAX / 32];
     int total[SEQSUM_EXP_SLOTS];
     int head[SEQSUM_EXP_SLOTS];
+    int lo, hi;  // range of slots that received a head
     int bad;
     float result;
 };
@@ -61,7 +62,11 @@ __device__ __forceinline__ float seq_sum_squares(const float* v, int n, SeqSumSm
         s.total[i] = 0;
         s.head[i] = -1;
     }
-    if (tid == 0) s.bad = 0;
+    if (tid == 0) {
+        s.bad = 0;
+        s.lo = SEQSUM_EXP_SLOTS;
+        s.hi = -1;
+    }
     // (2) exclusive prefix of the per-thread chunk sums, in double
     double local = 0.0;
     for (int i = i0; i < i1; ++i) {
@@ -101,7 +106,12 @@ __device__ __forceinline__ float seq_sum_squares(const float* v, int n, SeqSumSm
             cur_tot = 0;
             cur_e = e;
             const int slot = e + SEQSUM_EXP_OFF;
-            if (slot < 0 || slot >= SEQSUM_EXP_SLOTS || atomicCAS(&s.head[slot], -1, i) != -1) s.bad = 1;
+            if (slot < 0 || slot >= SEQSUM_EXP_SLOTS || atomicCAS(&s.head[slot], -1, i) != -1) {
+                s.bad = 1;
+            } else {
+                atomicMin(&s.lo, slot);
+                atomicMax(&s.hi, slot);
+            }
         } else {
             if (e != cur_e) {
                 seqsum_flush(s, cur_e, cur_tot);
@@ -118,11 +128,15 @@ __device__ __forceinline__ float seq_sum_squares(const float* v, int n, SeqSumSm
     }
     seqsum_flush(s, cur_e, cur_tot);
     __syncthreads();
+    // a total outside [lo, hi] belongs to a binade without a head: a misprediction
+    for (int i = tid; i < SEQSUM_EXP_SLOTS; i += nt)
+        if ((i < s.lo || i > s.hi) && s.total[i] != 0) s.bad = 1;
+    __syncthreads();
     // (4) walk the binades in order, verifying every crossing
     if (tid == 0) {
         bool ok = !s.bad;
         float S = 0.0f;
-        for (int slot = 0; ok && slot < SEQSUM_EXP_SLOTS; ++slot) {
+        for (int slot = s.lo; ok && slot <= s.hi; ++slot) {
             const int h = s.head[slot];
             if (h < 0) {
                 if (s.total[slot] != 0) ok = false;
