@@ -344,7 +344,23 @@ def main():
     ap.add_argument("--wdtype", type=int, default=3, choices=[1, 3, 4], help="1 fp16, 3 q8, 4 q4")
     ap.add_argument("--gemv-only", action="store_true",
                     help="only the exact GEMV sweep on TinyLlama's shapes (M=1), e.g. for profiling")
+    ap.add_argument("--decode-only", type=int, default=0, metavar="T",
+                    help="only load the model and run one request of T generated tokens (for a launch list)")
     args = ap.parse_args()
+    if args.decode_only:
+        import numpy as np
+        import torch
+
+        import gten_b200 as G
+        from gten_b200 import gtenfile
+        m = G.Model(G.TINYLLAMA, args.wdtype, N_PROMPT + N_GEN)
+        m.load(gtenfile.synthetic_image_device(G.TINYLLAMA, args.wdtype, SEED))
+        prompt = np.random.default_rng(42).integers(0, 32000, N_PROMPT).astype(np.int32)
+        out = m.generate(prompt, args.decode_only)
+        m.check()
+        m.close()
+        print(json.dumps({"decode_only": args.decode_only, "first_ids": [int(x) for x in out[:8]]}), flush=True)
+        return
     if args.gemv_only:
         import torch
 

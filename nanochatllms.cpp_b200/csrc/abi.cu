@@ -161,8 +161,103 @@ cudaError_t matmul_f32(const uint8_t* X, long xs, int xdt, int M, const uint8_t*
     return matmul_tma(X, xs, M, W, ws, wdt, N, K, Y, ldy, st);
 }
 
+static int sm_count() {
+    static thread_local int dev_cached = -1, n = 148;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != dev_cached) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 148;
+        dev_cached = dev;
+    }
+    return n;
+}
+
+template <int WDT, int R, int MT>
+static cudaError_t launch_gv2(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y,
+                              long ldy, cudaStream_t st, bool dry) {
+    const size_t smem = gv2_smem<WDT>(R, MT, K);
+    const cudaError_t e = ensure_smem(k_gemv2<WDT, R, MT>, smem);
+    if (e != cudaSuccess || dry) return e;
+    const int ngroups = (N + R - 1) / R;
+    int occ = (int)((227 * 1024) / (smem + 2048));
+    occ = occ < 1 ? 1 : (occ > 4 ? 4 : occ);
+    const int gx = std::min(ngroups, sm_count() * occ);
+    return launch_pdl(k_gemv2<WDT, R, MT>, dim3(gx, (M + MT - 1) / MT), dim3(GV2_THREADS), smem, st, W, ws, N, K, X,
+                      xs, M, Y, ldy, device_error_word());
+}
+
+// Rows per group and batch tile for the two-phase GEMV, chosen by shared memory.
+template <int WDT>
+static cudaError_t gemv2(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y, long ldy,
+                         cudaStream_t st, bool dry) {
+    const size_t lim = GV2_SMEM_LIMIT;
+#define GV(R_, MT_) return launch_gv2<WDT, R_, MT_>(X, xs, M, W, ws, N, K, Y, ldy, st, dry)
+    const int mt = M <= 1 ? 1 : (M <= 2 ? 2 : 4);
+    if (mt == 1) {
+        if (gv2_smem<WDT>(16, 1, K) <= lim) GV(16, 1);
+        GV(8, 1);
+    }
+    if (mt == 2) {
+        if (gv2_smem<WDT>(16, 2, K) <= lim) GV(16, 2);
+        if (gv2_smem<WDT>(8, 2, K) <= lim) GV(8, 2);
+        GV(8, 1);
+    }
+    if (gv2_smem<WDT>(16, 4, K) <= lim) GV(16, 4);
+    if (gv2_smem<WDT>(8, 4, K) <= lim) GV(8, 4);
+    if (gv2_smem<WDT>(8, 2, K) <= lim) GV(8, 2);
+    GV(8, 1);
+#undef GV
+}
+
+bool gemv_q_fits(int M, int wdt, int K) {
+    return M >= 1 && M <= 4 && (wdt == GTN_Q8 || wdt == GTN_Q4) && gv2_smem<GTN_Q8>(8, 1, K) <= GV2_SMEM_LIMIT;
+}
+
+// k_gemv3 plan for one activation row: rows per stage R = RP * passes (RP = rows covered by one
+// pass of 256 threads), as many passes (up to 16 rows) as keep two CTAs per SM.
+template <int WDT>
+static bool gv3_plan(const uint8_t* W, long ws, int K, int* R, int* RP) {
+    const int nb = K / GTN_QBLK;
+    if (K % GTN_QBLK || nb % 4 || nb / 4 > GV3_THREADS || nb == 0) return false;
+    if ((reinterpret_cast<uintptr_t>(W) & 15) || (ws & 15)) return false;
+    const int rp = std::min(GV3_THREADS / (nb / 4), GV3_THREADS / 4);  // phase 2: 4 threads per row
+    for (int passes = std::max(1, 16 / rp); passes >= 1; --passes)
+        if (gv3_smem<WDT>(rp * passes, K) <= 110 * 1024) {
+            *R = rp * passes;
+            *RP = rp;
+            return true;
+        }
+    return false;
+}
+
+template <int WDT>
+static cudaError_t launch_gv3(const uint8_t* X, const uint8_t* W, long ws, int N, int K, float* Y, int R, int RP,
+                              cudaStream_t st, bool dry) {
+    const size_t smem = gv3_smem<WDT>(R, K);
+    const cudaError_t e = ensure_smem(k_gemv3<WDT>, smem);
+    if (e != cudaSuccess || dry) return e;
+    const int ngroups = (N + R - 1) / R;
+    int occ = (int)((227 * 1024) / (smem + 2048));
+    occ = occ < 1 ? 1 : (occ > 2 ? 2 : occ);
+    const int gx = std::min(ngroups, sm_count() * occ);
+    return launch_pdl(k_gemv3<WDT>, dim3(gx), dim3(GV3_THREADS), smem, st, W, ws, N, K, X, Y, R, RP,
+                      device_error_word());
+}
+
+cudaError_t gemv_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
+                   long ldy, cudaStream_t st, bool dry) {
+    int R = 0, RP = 0;
+    if (M == 1 && wdt == GTN_Q8 && gv3_plan<GTN_Q8>(W, ws, K, &R, &RP))
+        return launch_gv3<GTN_Q8>(X, W, ws, N, K, Y, R, RP, st, dry);
+    if (M == 1 && wdt == GTN_Q4 && gv3_plan<GTN_Q4>(W, ws, K, &R, &RP))
+        return launch_gv3<GTN_Q4>(X, W, ws, N, K, Y, R, RP, st, dry);
+    if (wdt == GTN_Q8) return gemv2<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, st, dry);
+    return gemv2<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, st, dry);
+}
+
 static cudaError_t matmul_tma(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K,
                               float* Y, long ldy, cudaStream_t st) {
+    if (gemv_q_fits(M, wdt, K)) return gemv_q(X, xs, M, W, ws, wdt, N, K, Y, ldy, st, false);
     const int mt = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
     if (wdt == GTN_F16) {
         int nw = 4;
@@ -272,7 +367,7 @@ static int norm_common(const gtn_tensor* inp, const gtn_tensor* weight, const gt
         GTN_CHECK(check_tensor(bias, "bias"));
         GTN_REQUIRE(bias->ndim == 1 && bias->dtype == GTN_F16 && bias->shape[0] == n, "layer_norm: bias");
     }
-    const size_t smem = sizeof(float) * (size_t)n;
+    const size_t smem = 2 * sizeof(float) * (size_t)n;  // values + the exact sum's scratch
     cudaError_t e;
     if (layer) {
         e = ensure_smem(k_norm<true>, smem);

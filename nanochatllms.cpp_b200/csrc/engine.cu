@@ -407,7 +407,9 @@ static cudaError_t rows_op(int op, const uint8_t* a, long as, const uint8_t* b, 
 static cudaError_t norm_rows(const gtn_model* m, const uint8_t* x, uint8_t* out, const uint16_t* w, const uint16_t* b,
                              int M, cudaStream_t st) {
     const long rs = row_bytes(m->adt, m->d);
-    const size_t smem = sizeof(float) * m->d;
+    const size_t smem = 2 * sizeof(float) * m->d;  // values + the exact sum's scratch
+    const cudaError_t e = m->family == 1 ? ensure_smem(k_norm<true>, smem) : ensure_smem(k_norm<false>, smem);
+    if (e != cudaSuccess) return e;
     if (m->family == 1)
         return launch_pdl(k_norm<true>, dim3(1, M), dim3(256), smem, st, x, rs, 0L, out, rs, 0L, m->adt, m->d, 0, w, b);
     return launch_pdl(k_norm<false>, dim3(1, M), dim3(256), smem, st, x, rs, 0L, out, rs, 0L, m->adt, m->d, 0, w,
@@ -461,9 +463,9 @@ static int forward(gtn_model* m, int seq, int n, int sp) {
         const long hb = row_bytes(adt, dh);
         if (m->family == 3) {
             // openelm.cpp:44-52: QK RMSNorm over heads, then RoPE into the cache / query buffer.
-            GK(launch_pdl(k_norm<false>, dim3(Ly.nh, M), dim3(256), sizeof(float) * dh, st, (const uint8_t*)m->q, rq,
+            GK(launch_pdl(k_norm<false>, dim3(Ly.nh, M), dim3(256), 2 * sizeof(float) * dh, st, (const uint8_t*)m->q, rq,
                           hb, m->qn, rq, hb, adt, dh, 0, Ly.qnw, (const uint16_t*)nullptr));
-            GK(launch_pdl(k_norm<false>, dim3(Ly.nkv, M), dim3(256), sizeof(float) * dh, st,
+            GK(launch_pdl(k_norm<false>, dim3(Ly.nkv, M), dim3(256), 2 * sizeof(float) * dh, st,
                           (const uint8_t*)(kc + (long)sp * rkv), rkv, hb, m->kn, rkv, hb, adt, dh, 0, Ly.knw,
                           (const uint16_t*)nullptr));
             // the rope kernels index rows by absolute position; local buffers get bases shifted by -sp rows
@@ -544,7 +546,7 @@ static cudaError_t fg_mt(const FArgs& a, cudaStream_t st, bool dry) {
 static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) {
     FArgs g = a;
     if (pro != PRO_COPY) {
-        const size_t smem = pro == PRO_RESNORM ? sizeof(float) * (size_t)a.K : 0;
+        const size_t smem = pro == PRO_RESNORM ? 2 * sizeof(float) * (size_t)a.K : 0;  // values + sum scratch
         cudaError_t e;
         if (pro == PRO_RESNORM) {
             if (dry) {
@@ -563,6 +565,10 @@ static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) 
         if (e != cudaSuccess) return e;
         g.xin = m->act;
         g.xin_s = m->act_s;
+    }
+    if (gemv_q_fits(g.B, m->wdt, g.K)) {
+        if (!dry) ++g_step_kernels;
+        return gemv_q(g.xin, g.xin_s, g.B, g.W, g.ws, m->wdt, g.N, g.K, g.Y, g.ldy, m->st, dry);
     }
     if (m->wdt == GTN_Q8) return fg_mt<GTN_Q8, PRO_COPY>(g, m->st, dry);
     return fg_mt<GTN_Q4, PRO_COPY>(g, m->st, dry);

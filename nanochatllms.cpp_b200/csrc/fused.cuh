@@ -79,7 +79,7 @@ __host__ __device__ inline size_t fgemv_smem(int nw, int mt, int K, int adt, int
     size_t s = 128 + (size_t)MM_STAGES * nw * 8 * mm_q_tile_stride<WDT>();
     s += ((size_t)mt * row_bytes(adt, K) + 15) / 16 * 16;
     s += (size_t)mt * nb * 4 * sizeof(LanePrep);
-    if (pro == PRO_RESNORM) s += (size_t)mt * K * sizeof(float);
+    if (pro == PRO_RESNORM) s += (size_t)(mt + 1) * K * sizeof(float);  // values + the exact sum's scratch
     return s;
 }
 
@@ -175,7 +175,7 @@ __device__ __forceinline__ void fgemv_prologue(const FArgs& a, uint8_t* xq, floa
     if (mt == 1 && !a.layer) {
         // one row: the exact parallel form of the sequential sum of squares (seqsum.cuh)
         __shared__ SeqSumSmem ss;
-        const float sq = seq_sum_squares(sval, K, ss);
+        const float sq = seq_sum_squares(sval, K, ss, reinterpret_cast<int*>(sval + (size_t)mt * K));
         if (tid == 0) {
             stat[0][0] = 0.0f;
             stat[0][1] = sqrtf(sq / (float)K);
@@ -345,6 +345,13 @@ __global__ void __launch_bounds__(NW * 32) k_fgemv(const FArgs a) {
 template <int PRO>
 static __global__ void __launch_bounds__(1024) k_prep(const FArgs a, uint8_t* act, long act_s) {
     extern __shared__ float sval[];
+    if (PRO == PRO_RESNORM) {  // the norm weights do not depend on the previous kernel: warm L2 now
+        const int lines = (a.K * 2 + 127) / 128;
+        for (int i = threadIdx.x; i < lines; i += blockDim.x) {
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.nw) + 128L * i));
+            if (a.nb) asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.nb) + 128L * i));
+        }
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     const int m = blockIdx.y;

@@ -61,6 +61,14 @@ unsigned int take_device_error();
 cudaError_t matmul_f32(const uint8_t* X, long x_stride, int xdt, int M, const uint8_t* W, long w_stride, int wdt,
                        int N, int K, float* Y, long ldy, cudaStream_t st, bool padded = true);
 
+// Two-phase GEMV (k_gemv2) for M <= 4 activation rows of Q8 against Q8 or Q4 weights, with the
+// same `padded` precondition on W as matmul_f32. `dry` only configures shared memory (so that a
+// later launch can be captured into a CUDA graph). gemv_q_fits says whether a shape is supported.
+constexpr size_t GV2_SMEM_LIMIT = 200 * 1024;
+bool gemv_q_fits(int M, int wdt, int K);
+cudaError_t gemv_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
+                   long ldy, cudaStream_t st, bool dry);
+
 // Host table of (cos, sin) for positions [0, npos) and j < rd/2, as rotary_emb_impl computes them
 // (ops.cpp:791-812): theta = m * powf(10000, -((2j)/rd)), then cosf / sinf.
 std::vector<float2> rope_table_host(int npos, int rd);

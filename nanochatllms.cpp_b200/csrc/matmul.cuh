@@ -326,6 +326,312 @@ __global__ void __launch_bounds__(NW * 32) k_mm_f16(const uint8_t* __restrict__ 
     }
 }
 
+// ---- two-phase exact GEMV for small M --------------------------------------------------------
+// At M = 1 there are only N*4 lane chains, too few threads to cover latency when each walks K/32
+// dependent steps. Here a persistent CTA of 256 threads takes groups of R weight rows (whole rows,
+// TMA double-buffered): phase 1 computes every per-block lane product fl(float(L) * (da*dw)) in
+// parallel into shared memory, phase 2 runs the per-lane fp32 chains over the blocks in order
+// (acc = acc + p, exactly the reference's order), phase 3 forms (L0+L1)+(L2+L3).
+constexpr int GV2_THREADS = 256;
+
+template <int WDT>
+__host__ __device__ inline int gv2_rstride(int K) {
+    const long rb = (long)(K / GTN_QBLK) * MMCfg<WDT>::BLK_BYTES;
+    return (int)(((rb + 15) & ~15L) + 16);
+}
+template <int WDT>
+__host__ __device__ inline size_t gv2_smem(int R, int mt, int K) {
+    const int nb = K / GTN_QBLK;
+    return 128 + (size_t)2 * R * gv2_rstride<WDT>(K) + (size_t)mt * nb * 4 * sizeof(LanePrep) +
+           (size_t)mt * R * 4 * (nb + 1) * sizeof(float) + (size_t)mt * R * 4 * sizeof(float);
+}
+
+template <int WDT, int R, int MT>
+__global__ void __launch_bounds__(GV2_THREADS) k_gemv2(const uint8_t* __restrict__ W, long w_stride, int N, int K,
+                                                       const uint8_t* __restrict__ X, long x_stride, int M,
+                                                       float* __restrict__ Y, long y_stride, unsigned int* err) {
+    using C = MMCfg<WDT>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int abort_flag;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+    const int nb = K / GTN_QBLK;
+    const long rb = (long)nb * C::BLK_BYTES;
+    const int rstride = gv2_rstride<WDT>(K);
+    uint8_t* stage = smem + 128;
+    LanePrep* prep = reinterpret_cast<LanePrep*>(stage + (size_t)2 * R * rstride);
+    const int m0 = blockIdx.y * MT;
+    const int mt = min(MT, M - m0);
+    float* prod = reinterpret_cast<float*>(prep + (size_t)MT * nb * 4);
+    const int pstr = nb + 1;
+    float* res = prod + (size_t)MT * R * 4 * pstr;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ngroups = (N + R - 1) / R;
+
+    auto issue = [&](int g, int s) {  // warp 0
+        const int r0 = g * R, nr = min(R, N - r0);
+        uint32_t total = 0;
+        for (int r = 0; r < nr; ++r) {
+            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(r0 + r) * w_stride;
+            total += ((uint32_t)(src & 15) + (uint32_t)rb + 15) & ~15u;
+        }
+        if (lane == 0) mbar_arrive_expect_tx(&bars[s], total);
+        __syncwarp();
+        for (int r = lane; r < nr; r += 32) {
+            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(r0 + r) * w_stride;
+            const uint32_t off = (uint32_t)(src & 15);
+            bulk_g2s(stage + ((size_t)s * R + r) * rstride, reinterpret_cast<const void*>(src - off),
+                     (off + (uint32_t)rb + 15) & ~15u, &bars[s]);
+        }
+    };
+
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+    const int g0 = blockIdx.x;
+    int nissued[2] = {0, 0};  // meaningful in warp 0, which issues every copy
+    if (warp == 0) {
+        if (g0 < ngroups) issue(g0, 0), ++nissued[0];
+        if (g0 + (int)gridDim.x < ngroups) issue(g0 + gridDim.x, 1), ++nissued[1];
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    build_prep_q8(X, x_stride, m0, mt, nb, prep);
+    __syncthreads();
+    int it = 0;
+    for (int g = g0; g < ngroups; g += gridDim.x, ++it) {
+        const int s = it & 1;
+        const int r0 = g * R, nr = min(R, N - r0);
+        if (!abort_flag && !mbar_wait_bounded(&bars[s], (it >> 1) & 1, err)) abort_flag = 1;
+        __syncthreads();
+        if (!abort_flag) {
+            for (int item = tid; item < nr * nb; item += GV2_THREADS) {
+                const int r = item / nb, b = item - r * nb;
+                const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(r0 + r) * w_stride;
+                const uint8_t* p = stage + ((size_t)s * R + r) * rstride + (src & 15) + (size_t)b * C::BLK_BYTES;
+                const float dw = h2f(ld_u16(p));
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    if (m < mt) {
+#pragma unroll
+                        for (int l = 0; l < 4; ++l) {
+                            const LanePrep av = prep[((size_t)m * nb + b) * 4 + l];
+                            const int L = WDT == GTN_Q8 ? q8_block_lane_dot(p, l, av) : q4_block_lane_dot(p, l, av);
+                            const float sc = av.da * dw;
+                            prod[((size_t)(m * R + r) * 4 + l) * pstr + b] = (float)L * sc;
+                        }
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (warp == 0 && !abort_flag && g + 2 * (int)gridDim.x < ngroups) issue(g + 2 * gridDim.x, s), ++nissued[s];
+        if (!abort_flag) {
+            for (int c = tid; c < mt * nr * 4; c += GV2_THREADS) {
+                const int m = c / (nr * 4), rl = c - m * nr * 4;  // rl = r*4 + l
+                const float* pp = prod + ((size_t)(m * R) * 4 + rl) * pstr;
+                float acc = 0.0f;
+#pragma unroll 8
+                for (int b = 0; b < nb; ++b) acc = acc + pp[b];
+                res[c] = acc;
+            }
+        }
+        __syncthreads();
+        if (!abort_flag) {
+            for (int t = tid; t < mt * nr; t += GV2_THREADS) {
+                const int m = t / nr, r = t - m * nr;
+                const float* q = res + (size_t)t * 4;
+                const float y = (q[0] + q[1]) + (q[2] + q[3]);
+                Y[(long)(m0 + m) * y_stride + r0 + r] = y;
+            }
+        }
+        __syncthreads();
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (abort_flag && tid == 0) {
+        // bounded wait for the last copy issued into each stage (phase nissued-1)
+        for (int s = 0; s < 2; ++s) {
+            if (nissued[s] == 0) continue;
+            for (uint32_t i = 0; i < GTN_WAIT_LIMIT; ++i)
+                if (mbar_try_wait(&bars[s], (uint32_t)(nissued[s] - 1) & 1)) break;
+        }
+    }
+}
+
+// ---- single-row GEMV with the activation in registers (M = 1, 16-byte aligned weight rows) ------
+// Same arithmetic and order as k_gemv2. Thread (row slot rs, block group j) keeps the lane words of
+// activation blocks 4j..4j+3 in registers for the whole launch; weight rows arrive by TMA into a
+// double-buffered stage; phase 1 reads a thread's 4 weight blocks with 8-byte shared loads
+// (conflict-free: a half-warp covers 16 consecutive groups of one row), extracts the lane words
+// with byte permutes and writes the 16 products as four float4 (one per lane, blocks 4j..4j+3);
+// phase 2 runs the lane chains (acc = acc + p in block order) and the final (L0+L1)+(L2+L3).
+// Row stride of the products: a multiple of 4 floats, odd in float4 units (conflict-free float4
+// reads across 8 consecutive chains). grid: persistent over groups of R rows; block 256.
+constexpr int GV3_THREADS = 256;
+
+template <int WDT>
+__host__ __device__ inline int gv3_rstride(int K) {
+    return ((K / GTN_QBLK) * MMCfg<WDT>::BLK_BYTES + 15) & ~15;
+}
+__host__ __device__ inline int gv3_pstr(int nb) { return ((nb + 7) & ~7) + 4; }
+template <int WDT>
+__host__ __device__ inline size_t gv3_smem(int R, int K) {
+    return 128 + (size_t)2 * R * gv3_rstride<WDT>(K) + (size_t)R * 4 * gv3_pstr(K / GTN_QBLK) * sizeof(float);
+}
+
+// Little-endian u16 at even byte offset o of a register-resident byte array (o folds at compile
+// time once the loops are unrolled).
+__device__ __forceinline__ uint32_t gv3_u16(const uint32_t* w, int o) { return (w[o >> 2] >> ((o & 2) * 8)) & 0xffffu; }
+// (u16 at o1) | (u16 at o2) << 16
+__device__ __forceinline__ int gv3_pair(const uint32_t* w, int o1, int o2) {
+    const unsigned sel = (unsigned)(o1 & 2) | ((unsigned)((o1 & 2) + 1) << 4) | ((unsigned)(4 + (o2 & 2)) << 8) |
+                         ((unsigned)(5 + (o2 & 2)) << 12);
+    return (int)__byte_perm(w[o1 >> 2], w[o2 >> 2], sel);
+}
+
+template <int WDT>
+__global__ void __launch_bounds__(GV3_THREADS, 2) k_gemv3(const uint8_t* __restrict__ W, long w_stride, int N, int K,
+                                                         const uint8_t* __restrict__ X, float* __restrict__ Y, int R,
+                                                         int RP, unsigned int* err) {
+    using C = MMCfg<WDT>;
+    constexpr int GB = 4 * C::BLK_BYTES, GW = GB / 4;  // bytes / words of 4 weight blocks
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int abort_flag;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+    const int nb = K / GTN_QBLK, nbg = nb / 4;
+    const int rstride = gv3_rstride<WDT>(K);
+    const int pstr = gv3_pstr(nb);
+    uint8_t* stage = smem + 128;
+    float* prod = reinterpret_cast<float*>(stage + (size_t)2 * R * rstride);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int j = tid % nbg, rs = tid / nbg;
+    const bool p1 = rs < RP;
+    const int ngroups = (N + R - 1) / R;
+
+    auto issue = [&](int g, int s) {  // warp 0; W and w_stride are 16-byte aligned
+        const int r0 = g * R, nr = min(R, N - r0);
+        if (lane == 0) mbar_arrive_expect_tx(&bars[s], (uint32_t)rstride * (uint32_t)nr);
+        __syncwarp();
+        for (int r = lane; r < nr; r += 32)
+            bulk_g2s(stage + ((size_t)s * R + r) * rstride, W + (size_t)(r0 + r) * w_stride, (uint32_t)rstride,
+                     &bars[s]);
+    };
+
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+    const int g0 = blockIdx.x;
+    int nissued0 = 0, nissued1 = 0;  // meaningful in warp 0, which issues every copy
+    if (warp == 0) {
+        if (g0 < ngroups) issue(g0, 0), ++nissued0;
+        if (g0 + (int)gridDim.x < ngroups) issue(g0 + gridDim.x, 1), ++nissued1;
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // activation lane words of blocks 4j..4j+3 (same packing as build_prep_q8)
+    int a0[16], a1[16], asum[16];
+    float da[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint8_t* xb = X + (size_t)(4 * j + k) * GTN_Q8_BYTES;
+        da[k] = p1 ? h2f(ld_u16(xb)) : 0.0f;
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            int w0 = 0, w1 = 0;
+            if (p1) {
+                w0 = (int)ld_u16(xb + 2 + 2 * l) | ((int)ld_u16(xb + 10 + 2 * l) << 16);
+                w1 = (int)ld_u16(xb + 18 + 2 * l) | ((int)ld_u16(xb + 26 + 2 * l) << 16);
+            }
+            a0[k * 4 + l] = w0;
+            a1[k * 4 + l] = w1;
+            asum[k * 4 + l] = dp4a(w0, 0x01010101, dp4a(w1, 0x01010101, 0));
+        }
+    }
+    int it = 0;
+    for (int g = g0; g < ngroups; g += gridDim.x, ++it) {
+        const int s = it & 1;
+        const int r0 = g * R, nr = min(R, N - r0);
+        if (!abort_flag && !mbar_wait_bounded(&bars[s], (it >> 1) & 1, err)) abort_flag = 1;
+        __syncthreads();
+        if (abort_flag) break;
+        if (p1) {
+            for (int r = rs; r < nr; r += RP) {
+                const uint2* src = reinterpret_cast<const uint2*>(stage + ((size_t)s * R + r) * rstride + (size_t)j * GB);
+                uint32_t w[GW];
+#pragma unroll
+                for (int q = 0; q < GW / 2; ++q) {
+                    const uint2 t = src[q];
+                    w[2 * q] = t.x;
+                    w[2 * q + 1] = t.y;
+                }
+                float o[4][4];  // [lane][block]
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int ob = k * C::BLK_BYTES;
+                    const float sc = da[k] * h2f((uint16_t)gv3_u16(w, ob));
+#pragma unroll
+                    for (int l = 0; l < 4; ++l) {
+                        int L;
+                        if (WDT == GTN_Q8) {
+                            const int w0 = gv3_pair(w, ob + 2 + 2 * l, ob + 10 + 2 * l);
+                            const int w1 = gv3_pair(w, ob + 18 + 2 * l, ob + 26 + 2 * l);
+                            L = dp4a(w0, a0[k * 4 + l], dp4a(w1, a1[k * 4 + l], 0));
+                        } else {
+                            const int wb = gv3_pair(w, ob + 2 + 2 * l, ob + 10 + 2 * l);
+                            const int hi = (wb >> 4) & 0x0f0f0f0f, lo = wb & 0x0f0f0f0f;
+                            L = dp4a(hi, a0[k * 4 + l], dp4a(lo, a1[k * 4 + l], 0)) - 7 * asum[k * 4 + l];
+                        }
+                        o[l][k] = (float)L * sc;
+                    }
+                }
+#pragma unroll
+                for (int l = 0; l < 4; ++l)
+                    *reinterpret_cast<float4*>(prod + (size_t)(r * 4 + l) * pstr + 4 * j) =
+                        make_float4(o[l][0], o[l][1], o[l][2], o[l][3]);
+            }
+        }
+        __syncthreads();
+        if (warp == 0 && g + 2 * (int)gridDim.x < ngroups) {
+            issue(g + 2 * gridDim.x, s);
+            if (s == 0) ++nissued0;
+            else ++nissued1;
+        }
+        if (tid < ((R * 4 + 31) & ~31)) {  // whole warps: the combine shuffles need every lane
+            const int r = tid >> 2, l = tid & 3;
+            float acc = 0.0f;
+            if (r < nr) {
+                const float4* pp = reinterpret_cast<const float4*>(prod + (size_t)(r * 4 + l) * pstr);
+                for (int b4 = 0; b4 < nbg; ++b4) {
+                    const float4 v = pp[b4];
+                    acc = acc + v.x;
+                    acc = acc + v.y;
+                    acc = acc + v.z;
+                    acc = acc + v.w;
+                }
+            }
+            const float t01 = acc + __shfl_xor_sync(0xffffffffu, acc, 1);
+            const float t = t01 + __shfl_xor_sync(0xffffffffu, t01, 2);
+            if (l == 0 && r < nr) Y[r0 + r] = t;
+        }
+        __syncthreads();  // the products are rewritten by the next group
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (abort_flag && tid == 0) {
+        // bounded wait for the last copy issued into each stage (phase nissued-1)
+        const int ni[2] = {nissued0, nissued1};
+        for (int s = 0; s < 2; ++s) {
+            if (ni[s] == 0) continue;
+            for (uint32_t i = 0; i < GTN_WAIT_LIMIT; ++i)
+                if (mbar_try_wait(&bars[s], (uint32_t)(ni[s] - 1) & 1)) break;
+        }
+    }
+}
+
 // Plain-load variant for rows whose TMA tiles could reach outside the caller's weight buffer (an
 // unaligned base, or a last row that does not end on a 16-byte boundary). One warp per
 // (row, activation row): lanes 0..3 (Q8/Q4) or 0..7 (fp16) run the reference's lane chains with

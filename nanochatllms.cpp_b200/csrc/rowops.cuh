@@ -64,7 +64,7 @@ static __global__ void k_rowop(const uint8_t* a, long as, const uint8_t* b, long
 // order, as the reference computes them (one thread), the rest is element-parallel.
 //   rms_norm_vec_f32 ops.cpp:830-846: x / (sqrt(sum(x^2)/n) + 1e-6) * w
 //   vec_layer_norm_f32 ops.cpp:669-698: ((x - mean) / (sqrt(sum((x-mean)^2)/n) + 1e-5)) * w + b
-// grid: (heads, rows); block 256; dynamic smem n floats.
+// grid: (heads, rows); block 256; dynamic smem 2n floats (values + the exact sum's scratch).
 template <bool LAYER>
 static __global__ void k_norm(const uint8_t* x, long xs, long hs, uint8_t* out, long os, long ohs, int dt, int n,
                               int row0, const uint16_t* w, const uint16_t* bvec) {
@@ -78,7 +78,7 @@ static __global__ void k_norm(const uint8_t* x, long xs, long hs, uint8_t* out, 
     if (!LAYER) {
         // the sequential sum of squares, computed exactly in parallel (seqsum.cuh)
         __shared__ SeqSumSmem ss;
-        const float sq = seq_sum_squares(v, n, ss);
+        const float sq = seq_sum_squares(v, n, ss, reinterpret_cast<int*>(v + n));
         if (threadIdx.x == 0) {
             stat[0] = 0.0f;
             stat[1] = sqrtf(sq / (float)n);

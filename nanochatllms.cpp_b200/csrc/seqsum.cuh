@@ -5,163 +5,252 @@
 // non-negative terms the running sum S never decreases, so it moves through binades
 // [2^e, 2^(e+1)) in order, and while S stays inside one binade every add rounds to a multiple of
 // the same ulp u = 2^(e-23):
-//     fl(S + p) = S + u * inc(p),  inc(p) = floor(p/u) + (frac(p/u) > 1/2)
-// unless frac(p/u) == 1/2 exactly (a tie, decided by the parity of S/u). So a run of adds inside
-// one binade is an exact integer sum of per-term increments, which can be summed in any order.
+//     fl(S + p) = S + u * inc,  inc = floor(p/u) + (frac(p/u) > 1/2)
+// and when frac(p/u) == 1/2 exactly (a tie) round-half-even picks inc so that S/u + inc is even.
+// So a run of adds inside one binade is an integer sum of per-term increments; only the ties
+// depend on the running value, through its parity. For the ties j = 0, 1, ... of one binade let
+// d_j be the parity of (the binade's increments up to and including tie j's floor); tie j rounds
+// up iff (S_head/u + d_j + E_j) is odd, E_j being the round-ups before it. The parity of E_(j+1)
+// equals c_j = (S_head/u + d_j) mod 2, so tie 0 rounds up iff c_0 is odd and tie j >= 1 iff
+// d_j != d_(j-1): the binade's total round-ups are c_0 + sum_j (d_j xor d_(j-1)), which depends
+// on the running value only through the parity of S_head/u.
 //
-// Algorithm (one CTA): (1) terms p_i = fl(v_i * v_i); (2) a double-precision prefix scan predicts
-// the binade e_i of the running sum after term i; (3) the first term of each predicted binade
-// (its "head") is kept as a float, every other term adds inc(p_i) w.r.t. its binade's ulp to an
-// integer total per binade; (4) one thread walks the binades in order: S = fl(S + p_head) (an
-// exact IEEE add), checks that S really is in binade e, adds the binade's integer total and
-// checks the result is still below 2^(e+1). A failed check (a mispredicted crossing), a tie, or
-// a subnormal sum makes the CTA fall back to the plain sequential loop, so the result is always
-// bit-identical to the serial sum.
+// Algorithm (one CTA, every thread owns a contiguous chunk of terms):
+//  (1) terms p_i; the exponent of the largest fixes a fixed-point scale;
+//  (2) an exact int64 prefix scan of floor(p_i * 2^F) predicts the binade of the running sum after
+//      term i. Integer sums are associative, so every thread sees the same prediction at every
+//      index;
+//  (3) the first term of each predicted binade is its "head"; every other term gets its integer
+//      increment w.r.t. its binade's ulp (integer arithmetic on the float's bits); ties are listed;
+//  (4) an int64 prefix scan of the increments;
+//  (5) per binade (in parallel): the increments from its head to the next head, and the tie terms
+//      above; then one thread walks the binades in order: S = fl(S + p_head) (an exact IEEE add)
+//      must land in binade e, then S/u += increments + round-ups, which must stay below 2^24.
+// Any failed check (a mispredicted crossing, a term below the fixed-point resolution, a subnormal
+// binade, a non-finite term, more ties than the list holds) makes the CTA fall back to the plain
+// sequential loop, so the result is always bit-identical to the serial sum.
 #pragma once
 #include <cstdint>
 
 namespace gtn {
 
 constexpr int SEQSUM_THREADS_MAX = 1024;
-constexpr int SEQSUM_EXP_OFF = 150;     // slot = exponent + 150
-constexpr int SEQSUM_EXP_SLOTS = 320;
+constexpr int SEQSUM_SLOTS = 64;      // binades slot = floor(log2(Q)), Q = the fixed-point sum
+constexpr int SEQSUM_TIES_MAX = 128;
+constexpr int SEQSUM_FRAC_BITS = 25;  // the largest term becomes < 2^(24 + 25)
 
 struct SeqSumSmem {
-    double scan[SEQSUM_THREADS_MAX / 32];
-    int total[SEQSUM_EXP_SLOTS];
-    int head[SEQSUM_EXP_SLOTS];
-    int lo, hi;  // range of slots that received a head
+    long long wsum[SEQSUM_THREADS_MAX / 32];
+    long long cpre[SEQSUM_THREADS_MAX];  // per-thread exclusive prefix of the increments
+    long long tot[SEQSUM_SLOTS];         // per binade: increments from its head to the next head
+    int head[SEQSUM_SLOTS];
+    float phead[SEQSUM_SLOTS];
+    int d0[SEQSUM_SLOTS];                // parity of the first tie (or -1: no tie)
+    int x[SEQSUM_SLOTS];                 // sum of d_j xor d_(j-1) over the binade's ties
+    int tie[SEQSUM_TIES_MAX], tslot[SEQSUM_TIES_MAX];
+    int stie[SEQSUM_TIES_MAX], sslot[SEQSUM_TIES_MAX], sd[SEQSUM_TIES_MAX];
+    unsigned int mask[2];
+    int ntie;
     int bad;
+    unsigned int maxbits;
     float result;
 };
 
-// Binade exponent of a positive double (floor(log2(q))).
-__device__ __forceinline__ int binade_of(double q) {
-    int e;
-    frexp(q, &e);
-    return e - 1;
-}
-
-__device__ __forceinline__ void seqsum_flush(SeqSumSmem& s, int e, int tot) {
-    if (tot == 0) return;
-    const int slot = e + SEQSUM_EXP_OFF;
-    if (slot < 0 || slot >= SEQSUM_EXP_SLOTS) {
-        s.bad = 1;
-        return;
+// Exclusive prefix of x over the CTA (thread order), in int64; synchronizes the CTA.
+__device__ __forceinline__ long long seqsum_exscan64(long long x, long long* wsum) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    long long inc = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const long long t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
     }
-    atomicAdd(&s.total[slot], tot);
+    __syncthreads();  // wsum may still be read by a previous call
+    if (lane == 31) wsum[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        long long w = lane < nw ? wsum[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long t = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += t;
+        }
+        if (lane < nw) wsum[lane] = w;
+    }
+    __syncthreads();
+    return (warp > 0 ? wsum[warp - 1] : 0) + inc - x;
 }
 
-// Returns fl(...fl(fl(0 + p_0) + p_1)... + p_{n-1}) with p_i = fl(v[i] * v[i]), for v in shared
-// (or global) memory. All threads of the CTA must call it; it synchronizes the CTA.
-__device__ __forceinline__ float seq_sum_squares(const float* v, int n, SeqSumSmem& s) {
+// p = M * 2^(E - 23) for a finite non-negative float (M < 2^24; subnormals E = -126).
+__device__ __forceinline__ void seqsum_split(float p, unsigned int& M, int& E) {
+    const unsigned int b = __float_as_uint(p);
+    const unsigned int ef = b >> 23;
+    M = (b & 0x7fffffu) | (ef ? 0x800000u : 0u);
+    E = ef ? (int)ef - 127 : -126;
+}
+
+// Returns fl(...fl(fl(0 + p_0) + p_1)... + p_{n-1}) where p_i = term(i) >= 0 (a float computed
+// the same way on every call). `incs`: n ints of scratch (shared memory). All threads of the CTA
+// must call it (blockDim.x <= 1024, a multiple of 32, >= 64); it synchronizes the CTA.
+template <class Term>
+__device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, int* incs) {
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const int per = (n + nt - 1) / nt;
     const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
-    for (int i = tid; i < SEQSUM_EXP_SLOTS; i += nt) {
-        s.total[i] = 0;
-        s.head[i] = -1;
+    if (tid < SEQSUM_SLOTS) {
+        s.head[tid] = -1;
+        s.d0[tid] = -1;
+        s.x[tid] = 0;
     }
     if (tid == 0) {
-        s.bad = 0;
-        s.lo = SEQSUM_EXP_SLOTS;
-        s.hi = -1;
-    }
-    // (2) exclusive prefix of the per-thread chunk sums, in double
-    double local = 0.0;
-    for (int i = i0; i < i1; ++i) {
-        const float p = v[i] * v[i];
-        local += (double)p;
-    }
-    double incl = local;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const double t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t;
-    }
-    if (lane == 31) s.scan[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-        const int nw = nt >> 5;
-        double w = lane < nw ? s.scan[lane] : 0.0;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const double t = __shfl_up_sync(0xffffffffu, w, o);
-            if (lane >= o) w += t;
-        }
-        if (lane < nw) s.scan[lane] = w;
+        s.bad = n > (1 << 14);  // keeps the fixed-point sum below 2^63
+        s.ntie = 0;
+        s.maxbits = 0u;
     }
     __syncthreads();
-    double q = (warp > 0 ? s.scan[warp - 1] : 0.0) + (incl - local);  // terms before i0
-    // (3) heads and per-binade integer totals (run-length accumulated per thread)
-    int e_prev = q > 0.0 ? binade_of(q) : -1000;
-    int cur_e = -1000, cur_tot = 0;
+    // (1) largest term (non-negative floats order like their bit patterns)
+    unsigned int mb = 0u;
+    for (int i = i0; i < i1; ++i) mb = max(mb, __float_as_uint(term(i)));
+    mb = __reduce_max_sync(0xffffffffu, mb);
+    if (lane == 0) atomicMax(&s.maxbits, mb);
+    __syncthreads();
+    const unsigned int maxbits = s.maxbits;
+    if (maxbits == 0u) return 0.0f;                   // every term is +0: the sum is exactly 0
+    if (maxbits >= 0x7f800000u) s.bad = 1;            // inf / nan / a negative term
+    const int emax = maxbits >= 0x800000u ? (int)(maxbits >> 23) - 127 : -126;
+    // t_i = floor(p_i * 2^eoff), eoff = 23 + SEQSUM_FRAC_BITS - emax, i.e. with p = M * 2^(E-23):
+    // t_i = M << (E - emax + SEQSUM_FRAC_BITS), truncated when the shift is negative.
+    auto fixed = [&](float p) -> long long {
+        unsigned int M;
+        int E;
+        seqsum_split(p, M, E);
+        const int sh = E - emax + SEQSUM_FRAC_BITS;
+        if (sh >= 0) return (long long)M << sh;  // sh <= 25
+        return sh > -32 ? (long long)(M >> -sh) : 0LL;
+    };
+    // binade exponent of slot sl: Q = S * 2^(23 + FRAC - emax) => e = sl - (23 + FRAC - emax)
+    const int eoff = 23 + SEQSUM_FRAC_BITS - emax;
+    // (2) exact fixed-point prefix
+    long long loc = 0;
+    for (int i = i0; i < i1; ++i) loc += fixed(term(i));
+    long long Q = seqsum_exscan64(loc, s.wsum);
+    // (3) heads, increments, ties
+    int sl_prev = Q > 0 ? 63 - __clzll(Q) : -1;
+    long long itot = 0;
     for (int i = i0; i < i1; ++i) {
-        const float p = v[i] * v[i];
-        q += (double)p;
-        if (q <= 0.0) continue;  // leading zero terms: the sum stays exactly 0
-        const int e = binade_of(q);
-        if (e != e_prev) {
-            seqsum_flush(s, cur_e, cur_tot);
-            cur_tot = 0;
-            cur_e = e;
-            const int slot = e + SEQSUM_EXP_OFF;
-            if (slot < 0 || slot >= SEQSUM_EXP_SLOTS || atomicCAS(&s.head[slot], -1, i) != -1) {
-                s.bad = 1;
-            } else {
-                atomicMin(&s.lo, slot);
-                atomicMax(&s.hi, slot);
-            }
+        const float p = term(i);
+        const long long t = fixed(p);
+        Q += t;
+        int inc = 0;
+        if (Q == 0) {
+            if (p != 0.0f) s.bad = 1;  // a non-zero term below the fixed-point resolution
         } else {
-            if (e != cur_e) {
-                seqsum_flush(s, cur_e, cur_tot);
-                cur_tot = 0;
-                cur_e = e;
+            const int sl = 63 - __clzll(Q);  // < 63 since Q < 2^63
+            if (sl != sl_prev) {
+                s.head[sl] = i;
+            } else {
+                const int e = sl - eoff;
+                unsigned int M;
+                int E;
+                seqsum_split(p, M, E);
+                const int sh = e - E;  // p / u = M * 2^-sh
+                if (sh < 0 || e < -126) {
+                    s.bad = 1;
+                } else if (sh == 0) {
+                    inc = (int)M;
+                } else if (sh < 32) {
+                    inc = (int)(M >> sh);
+                    const unsigned int rem = M & ((1u << sh) - 1u), half = 1u << (sh - 1);
+                    if (rem > half) {
+                        ++inc;
+                    } else if (rem == half) {
+                        const int k = atomicAdd(&s.ntie, 1);
+                        if (k < SEQSUM_TIES_MAX) {
+                            s.tie[k] = i;
+                            s.tslot[k] = sl;
+                        } else {
+                            s.bad = 1;
+                        }
+                    }
+                }  // sh >= 32: p < u/2^8, the add does not change S
             }
-            const float x = p * ldexpf(1.0f, 23 - e);  // p/u, exact (power-of-two scaling)
-            const float fl = floorf(x);
-            const float fr = x - fl;
-            if (fr == 0.5f || x >= 16777216.0f || e < -126) s.bad = 1;
-            cur_tot += (int)fl + (fr > 0.5f ? 1 : 0);
+            sl_prev = sl;
         }
-        e_prev = e;
+        incs[i] = inc;
+        itot += inc;
     }
-    seqsum_flush(s, cur_e, cur_tot);
+    // (4) prefix of the increments: per-thread exclusive offsets in cpre
+    const long long ip = seqsum_exscan64(itot, s.wsum);
+    s.cpre[tid] = ip;
     __syncthreads();
-    // a total outside [lo, hi] belongs to a binade without a head: a misprediction
-    for (int i = tid; i < SEQSUM_EXP_SLOTS; i += nt)
-        if ((i < s.lo || i > s.hi) && s.total[i] != 0) s.bad = 1;
+    auto incl = [&](int i) -> long long {  // inclusive prefix of incs at i
+        const int owner = i / per;
+        long long r = s.cpre[owner];
+        for (int j = owner * per; j <= i; ++j) r += incs[j];
+        return r;
+    };
+    const int nties = min(s.ntie, SEQSUM_TIES_MAX);
+    // (5a) per binade: increments from the head to the next head; the ties in index order
+    if (tid < SEQSUM_SLOTS) {
+        const int h = s.head[tid];
+        const unsigned int bal = __ballot_sync(0xffffffffu, h >= 0);
+        if (lane == 0) s.mask[warp] = bal;
+        if (h >= 0) {
+            int hn = n;
+            for (int j = tid + 1; j < SEQSUM_SLOTS; ++j)
+                if (s.head[j] >= 0) {
+                    hn = s.head[j];
+                    break;
+                }
+            s.tot[tid] = incl(hn - 1) - incl(h);
+            s.phead[tid] = term(h);
+        }
+    }
+    for (int k = tid - SEQSUM_SLOTS; k >= 0 && k < nties; k += nt) {  // rank sort of the ties
+        const int i = s.tie[k];
+        int r = 0;
+        for (int j = 0; j < nties; ++j) r += s.tie[j] < i;
+        const int sl = s.tslot[k];
+        s.stie[r] = i;
+        s.sslot[r] = sl;
+        s.sd[r] = (int)((incl(i) - incl(s.head[sl])) & 1);
+    }
     __syncthreads();
-    // (4) walk the binades in order, verifying every crossing
+    for (int r = tid; r < nties; r += nt) {
+        const int sl = s.sslot[r];
+        if (r == 0 || s.sslot[r - 1] != sl) s.d0[sl] = s.sd[r];
+        else atomicAdd(&s.x[sl], s.sd[r] ^ s.sd[r - 1]);
+    }
+    __syncthreads();
+    // (5b) the walk over the binades that have a head
     if (tid == 0) {
         bool ok = !s.bad;
+        unsigned long long m = ((unsigned long long)s.mask[1] << 32) | s.mask[0];
         float S = 0.0f;
-        for (int slot = s.lo; ok && slot <= s.hi; ++slot) {
-            const int h = s.head[slot];
-            if (h < 0) {
-                if (s.total[slot] != 0) ok = false;
-                continue;
-            }
-            const int e = slot - SEQSUM_EXP_OFF;
-            const float ph = v[h] * v[h];
-            S = S + ph;
-            int es;
-            frexpf(S, &es);
-            if (es - 1 != e || e < -126) {
+        while (ok && m) {
+            const int sl = __ffsll((long long)m) - 1;
+            m &= m - 1;
+            const int e = sl - eoff;
+            S = S + s.phead[sl];
+            const unsigned int b = __float_as_uint(S);
+            if ((int)(b >> 23) - 127 != e || e < -126) {
                 ok = false;
                 break;
             }
-            const long k = (long)(S * ldexpf(1.0f, 23 - e)) + (long)s.total[slot];
-            if (k >= (1L << 24)) {
+            long long Sb = (long long)((b & 0x7fffffu) | 0x800000u);  // S / u
+            const int d0 = s.d0[sl];
+            if (d0 >= 0) Sb += ((Sb + d0) & 1) + s.x[sl];
+            Sb += s.tot[sl];
+            if (Sb >= (1LL << 24)) {
                 ok = false;
                 break;
             }
-            S = ldexpf((float)k, e - 23);
+            S = __uint_as_float(((unsigned int)(e + 127) << 23) | ((unsigned int)Sb & 0x7fffffu));
         }
         if (!ok) {  // fallback: the reference's loop as is
             S = 0.0f;
             for (int i = 0; i < n; ++i) {
-                const float p = v[i] * v[i];
+                const float p = term(i);
                 S = S + p;
             }
         }
@@ -169,6 +258,11 @@ __device__ __forceinline__ float seq_sum_squares(const float* v, int n, SeqSumSm
     }
     __syncthreads();
     return s.result;
+}
+
+// The sum of squares of v[0..n) (RMSNorm, ops.cpp:830-836: glibc powf(x, 2) == x*x exactly).
+__device__ __forceinline__ float seq_sum_squares(const float* v, int n, SeqSumSmem& s, int* incs) {
+    return seq_sum_exact([v](int i) { return v[i] * v[i]; }, n, s, incs);
 }
 
 }  // namespace gtn

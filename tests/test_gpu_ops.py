@@ -108,6 +108,11 @@ def test_rms_norm_sequential_sum_adversarial(orc, gpu, D):
         np.sqrt(np.arange(1, D + 1, dtype=np.float64)),   # squares near integers
         rng.standard_normal(D) * 1e-20,                    # subnormal squares
         np.linspace(1e-3, 1e3, D),
+        rng.integers(-127, 128, D) * 2.0 ** -7,            # int8 grid: many ties per binade
+        # Q8-dequantized values q * fp16(delta) per 32-block, as the residual stream holds them
+        rng.integers(-127, 128, D) * np.repeat(
+            rng.uniform(1e-3, 1e-1, (D + 31) // 32).astype(np.float16).astype(np.float64), 32)[:D],
+        np.concatenate([rng.standard_normal(D - 1) * 1e-30, [1.0]]),  # tiny terms, then a huge one
     ]
     x = np.stack(rows).astype(np.float32)
     M = x.shape[0]
