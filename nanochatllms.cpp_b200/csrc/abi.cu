@@ -487,8 +487,9 @@ int gtn_qkv_attn(const gtn_tensor* q, const gtn_tensor* k, const gtn_tensor* v, 
     if (e == cudaSuccess)
         e = launch_pdl(k_attn, dim3(qh, n_ctx - start_pos), dim3(ATT_THREADS), smem, S(stream),
                        (const uint8_t*)q->data, bstride(q, 0), (const uint8_t*)k->data, bstride(k, 0),
-                       (const uint8_t*)v->data, bstride(v, 0), (uint8_t*)qkv->data, bstride(qkv, 0), (int)q->dtype,
-                       n_ctx, start_pos, qh, kvh, d);
+                       row_bytes(k->dtype, d), (const uint8_t*)v->data, bstride(v, 0), row_bytes(v->dtype, d),
+                       (uint8_t*)qkv->data, bstride(qkv, 0), (int)q->dtype, n_ctx, start_pos, qh, kvh, d,
+                       device_error_word());
     return cuda_status(e, "qkv_attn");
 }
 

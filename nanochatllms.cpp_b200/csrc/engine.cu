@@ -49,6 +49,8 @@ struct gtn_model {
     int max_rows = 0, max_q = 0, max_kv = 0, max_ffn = 0;
     uint8_t *x = nullptr, *a = nullptr, *h = nullptr, *o = nullptr, *q = nullptr, *qn = nullptr, *att = nullptr;
     uint8_t *g = nullptr, *u = nullptr, *kn = nullptr;
+    uint8_t *kr = nullptr, *vr = nullptr;  // new K / V rows of a prefill, reference layout
+    long kv_rs = 0;                        // KV cache row stride (att_kv_rs: one padded head row)
     float* y = nullptr;
     float* logits = nullptr;
     int32_t* tok = nullptr;
@@ -197,6 +199,8 @@ int gtn_model_create(int kind, int wdtype, int max_ctx, int max_batch, const int
     rc |= dalloc(m.get(), &m->qn, R * row_bytes(adt, m->max_q));
     rc |= dalloc(m.get(), &m->att, R * row_bytes(adt, m->max_q));
     rc |= dalloc(m.get(), &m->kn, R * row_bytes(adt, m->max_kv));
+    rc |= dalloc(m.get(), &m->kr, R * row_bytes(adt, m->max_kv));
+    rc |= dalloc(m.get(), &m->vr, R * row_bytes(adt, m->max_kv));
     rc |= dalloc(m.get(), &m->g, R * row_bytes(adt, m->max_ffn));
     rc |= dalloc(m.get(), &m->u, R * row_bytes(adt, m->max_ffn));
     const long ywidth = std::max<long>(m->max_q + 2L * m->max_kv, 2L * m->max_ffn);
@@ -206,8 +210,12 @@ int gtn_model_create(int kind, int wdtype, int max_ctx, int max_batch, const int
     rc |= dalloc(m.get(), &m->tok, sizeof(int32_t) * (size_t)(max_ctx + 1) * max_batch);
     rc |= dalloc(m.get(), &m->next, sizeof(int32_t) * (size_t)max_batch);
     rc |= dalloc(m.get(), &m->gen, sizeof(int32_t) * (size_t)(max_ctx + 1) * max_batch);
+    // KV cache, head-major: [sequence][kv head][position][head row padded to 16 bytes, odd in
+    // 16-byte units], so that a run of positions of one head is one contiguous, 16-byte aligned
+    // range (one TMA bulk copy) whose rows load without bank conflicts
+    m->kv_rs = att_kv_rs(row_bytes(adt, m->dh));
     for (int l = 0; l < m->nl && rc == GTN_OK; ++l) {
-        const long kvb = (long)max_batch * max_ctx * row_bytes(adt, m->L[l].nkv * m->dh);
+        const long kvb = (long)max_batch * m->L[l].nkv * max_ctx * m->kv_rs;
         rc |= dalloc(m.get(), &m->L[l].kc, kvb);
         rc |= dalloc(m.get(), &m->L[l].vc, kvb);
     }
@@ -445,19 +453,22 @@ static int forward(gtn_model* m, int seq, int n, int sp) {
         Layer& Ly = m->L[l];
         const int qd = Ly.nh * dh, kvd = Ly.nkv * dh, nqkv = qd + 2 * kvd;
         const long rq = row_bytes(adt, qd), rkv = row_bytes(adt, kvd), rf = row_bytes(adt, Ly.nffn);
-        uint8_t* kc = Ly.kc + ((long)seq * m->max_ctx) * rkv;
-        uint8_t* vc = Ly.vc + ((long)seq * m->max_ctx) * rkv;
+        const long khs = (long)m->max_ctx * m->kv_rs;  // bytes between kv heads in the cache
+        uint8_t* kc = Ly.kc + (long)seq * Ly.nkv * khs;
+        uint8_t* vc = Ly.vc + (long)seq * Ly.nkv * khs;
+        // the new rows in reference layout, local row 0 = position sp (rope kernels index rows by
+        // absolute position, so they get bases shifted by -sp rows)
+        uint8_t* kr = m->kr;
+        uint8_t* vr = m->vr;
         GK(norm_rows(m, m->x, m->a, Ly.n1w, Ly.n1b, M, st));
         GK(matmul_f32(m->a, rd_, adt, M, Ly.wqkv, Ly.rs_d, m->wdt, nqkv, d, m->y, nqkv, st));
         GK(write_cols(m->y, nqkv, 0, qd, m->q, rq, adt, M, st));
-        GK(write_cols(m->y, nqkv, qd, kvd, kc + (long)sp * rkv, rkv, adt, M, st));
-        GK(write_cols(m->y, nqkv, qd + kvd, kvd, vc + (long)sp * rkv, rkv, adt, M, st));
+        GK(write_cols(m->y, nqkv, qd, kvd, kr, rkv, adt, M, st));
+        GK(write_cols(m->y, nqkv, qd + kvd, kvd, vr, rkv, adt, M, st));
         if (Ly.bq) {
             GK(rows_op(ROP_BIAS, m->q, rq, nullptr, 0, m->q, rq, adt, qd, M, 0.0f, Ly.bq, st));
-            GK(rows_op(ROP_BIAS, kc + (long)sp * rkv, rkv, nullptr, 0, kc + (long)sp * rkv, rkv, adt, kvd, M, 0.0f,
-                       Ly.bk, st));
-            GK(rows_op(ROP_BIAS, vc + (long)sp * rkv, rkv, nullptr, 0, vc + (long)sp * rkv, rkv, adt, kvd, M, 0.0f,
-                       Ly.bv, st));
+            GK(rows_op(ROP_BIAS, kr, rkv, nullptr, 0, kr, rkv, adt, kvd, M, 0.0f, Ly.bk, st));
+            GK(rows_op(ROP_BIAS, vr, rkv, nullptr, 0, vr, rkv, adt, kvd, M, 0.0f, Ly.bv, st));
         }
         const int half = m->rd / 2;
         const long hb = row_bytes(adt, dh);
@@ -466,24 +477,27 @@ static int forward(gtn_model* m, int seq, int n, int sp) {
             GK(launch_pdl(k_norm<false>, dim3(Ly.nh, M), dim3(256), 2 * sizeof(float) * dh, st, (const uint8_t*)m->q, rq,
                           hb, m->qn, rq, hb, adt, dh, 0, Ly.qnw, (const uint16_t*)nullptr));
             GK(launch_pdl(k_norm<false>, dim3(Ly.nkv, M), dim3(256), 2 * sizeof(float) * dh, st,
-                          (const uint8_t*)(kc + (long)sp * rkv), rkv, hb, m->kn, rkv, hb, adt, dh, 0, Ly.knw,
-                          (const uint16_t*)nullptr));
+                          (const uint8_t*)kr, rkv, hb, m->kn, rkv, hb, adt, dh, 0, Ly.knw, (const uint16_t*)nullptr));
             // the rope kernels index rows by absolute position; local buffers get bases shifted by -sp rows
             GK(launch_pdl(k_rope, dim3(Ly.nh, M), dim3(32), 0, st, (const uint8_t*)(m->qn - (long)sp * rq), rq,
                           m->q - (long)sp * rq, rq, adt, qd, dh, half, sp, (const float2*)m->rope, half));
             GK(launch_pdl(k_rope, dim3(Ly.nkv, M), dim3(32), 0, st, (const uint8_t*)(m->kn - (long)sp * rkv), rkv,
-                          kc, rkv, adt, kvd, dh, half, sp, (const float2*)m->rope, half));
+                          kr - (long)sp * rkv, rkv, adt, kvd, dh, half, sp, (const float2*)m->rope, half));
         } else if (half > 0) {
             GK(launch_pdl(k_rope, dim3(Ly.nh, M), dim3(32), 0, st, (const uint8_t*)(m->q - (long)sp * rq), rq,
                           m->q - (long)sp * rq, rq, adt, qd, dh, half, sp, (const float2*)m->rope, half));
-            GK(launch_pdl(k_rope, dim3(Ly.nkv, M), dim3(32), 0, st, (const uint8_t*)kc, rkv, kc, rkv, adt, kvd, dh,
-                          half, sp, (const float2*)m->rope, half));
+            GK(launch_pdl(k_rope, dim3(Ly.nkv, M), dim3(32), 0, st, (const uint8_t*)(kr - (long)sp * rkv), rkv,
+                          kr - (long)sp * rkv, rkv, adt, kvd, dh, half, sp, (const float2*)m->rope, half));
         }
+        GK(launch_pdl(k_kv_scatter, dim3(Ly.nkv, M), dim3(32), 0, st, (const uint8_t*)kr, rkv, kc, khs, m->kv_rs, sp,
+                      (int)hb));
+        GK(launch_pdl(k_kv_scatter, dim3(Ly.nkv, M), dim3(32), 0, st, (const uint8_t*)vr, rkv, vc, khs, m->kv_rs, sp,
+                      (int)hb));
         const size_t asmem = attn_smem(n, adt, dh);
         GK(ensure_smem(k_attn, asmem));
         GK(launch_pdl(k_attn, dim3(Ly.nh, M), dim3(ATT_THREADS), asmem, st, (const uint8_t*)(m->q - (long)sp * rq),
-                      rq, (const uint8_t*)kc, rkv, (const uint8_t*)vc, rkv, m->att - (long)sp * rq, rq, adt, n, sp,
-                      Ly.nh, Ly.nkv, dh));
+                      rq, (const uint8_t*)kc, m->kv_rs, khs, (const uint8_t*)vc, m->kv_rs, khs,
+                      m->att - (long)sp * rq, rq, adt, n, sp, Ly.nh, Ly.nkv, dh, device_error_word()));
         GK(matmul_f32(m->att, rq, adt, M, Ly.wo, Ly.rs_q, m->wdt, d, qd, m->y, d, st));
         GK(write_cols(m->y, d, 0, d, m->o, rd_, adt, M, st));
         if (m->family == 2) GK(rows_op(ROP_SCALE, m->o, rd_, nullptr, 0, m->o, rd_, adt, d, M, depth, nullptr, st));
@@ -615,8 +629,9 @@ static int decode_step(gtn_model* m, int B, bool dry) {
         AArgs at{};
         at.adt = adt; at.q_heads = Ly.nh; at.kv_heads = Ly.nkv; at.d = dh; at.pos = m->pos;
         at.y = m->yqkv; at.ys = m->ldqkv; at.bq = Ly.bq; at.bk = Ly.bk; at.bv = Ly.bv;
-        at.cs = m->rope; at.half = m->rd / 2; at.kc = Ly.kc; at.vc = Ly.vc; at.kvs = rkv;
-        at.seq_stride = (long)m->max_ctx * rkv; at.out = m->datt; at.os = row_bytes(adt, m->max_q); at.err = err;
+        at.cs = m->rope; at.half = m->rd / 2; at.kc = Ly.kc; at.vc = Ly.vc; at.kvs = m->kv_rs;
+        at.khs = (long)m->max_ctx * m->kv_rs; at.seq_stride = (long)Ly.nkv * at.khs;
+        at.out = m->datt; at.os = row_bytes(adt, m->max_q); at.err = err;
         const size_t asm_ = fattn_smem(m->max_ctx, adt, dh);
         if (dry) {
             SK(ensure_smem(k_fattn, asm_));

@@ -383,189 +383,83 @@ struct AArgs {
     const float* y; long ys;                 // stacked q|k|v fp32 rows
     const uint16_t *bq, *bk, *bv;            // Zephyr biases (or null)
     const float2* cs; int half;              // RoPE table [pos][half] (cos, sin), half = rd/2
-    uint8_t* kc; uint8_t* vc; long kvs;      // cache rows of this layer (row stride kvs bytes)
-    long seq_stride;                         // bytes between sequences in the cache
+    uint8_t* kc; uint8_t* vc; long kvs;      // cache of this layer: row stride kvs bytes
+    long khs;                                // bytes between kv heads
+    long seq_stride;                         // bytes between sequences
     uint8_t* out; long os;                   // attention output rows (adt)
     unsigned int* err;
 };
 
-// One Linear output head (d values starting at column c0 of row y) through the reference's
-// epilogue: requant (Linear) [-> + bias -> requant (bias_add_inplace)] [-> RoPE -> requant].
-// Warp-cooperative; writes the resulting head bytes to `dst` (row_bytes(adt, d)).
-__device__ __forceinline__ void head_epilogue(const AArgs& a, const float* yrow, int c0, const uint16_t* bias,
-                                              bool rope, int p, uint8_t* dst, float* tmp) {
-    const int lane = threadIdx.x & 31;
-    const int nbh = a.d / GTN_QBLK;
-    for (int k = 0; k < nbh; ++k) {
-        const int i = k * GTN_QBLK + lane;
-        float v = requant(yrow[c0 + i], lane, GTN_QBLK, a.adt, nullptr, 0);
-        if (bias) v = requant(v + h2f(bias[i]), lane, GTN_QBLK, a.adt, nullptr, 0);  // bias: this head's slice
-        tmp[i] = v;
-    }
-    __syncwarp();
-    for (int k = 0; k < nbh; ++k) {
-        const int i = k * GTN_QBLK + lane;
-        float y = tmp[i];
-        if (rope) {
-            const float2* c = a.cs + (long)p * a.half;
-            if (i < a.half) {
-                const float2 t = c[i];
-                const float p0 = tmp[i] * t.x, p1 = tmp[i + a.half] * t.y;
-                y = p0 - p1;
-            } else if (i < 2 * a.half) {
-                const float2 t = c[i - a.half];
-                const float p2 = tmp[i - a.half] * t.y, p3 = tmp[i] * t.x;
-                y = p2 + p3;
-            }
-            requant(y, lane, GTN_QBLK, a.adt, dst, k);
-        } else {
-            requant(y, lane, GTN_QBLK, a.adt, dst, k);
-        }
-    }
-    __syncwarp();
-}
-
 // grid (q_heads, B); block ATT_THREADS. Decode attention of sequence b at position p = pos[b]
-// (keys 0..p), preceded by the q/k/v epilogue; the q-head 0 of each kv group writes the new K/V
-// cache rows. Key p is taken from this CTA's own epilogue values.
+// (keys 0..p), preceded by the q/k/v epilogue of the stacked projection, one Linear output head
+// each: requant (Linear) [-> + bias -> requant (bias_add_inplace)] [-> RoPE -> requant]. The
+// epilogue runs one warp per (tensor, 32-block). The q-head 0 of each kv group writes the new K/V
+// cache rows; key p is taken from this CTA's own epilogue values. Then att_core / att_out.
 static __global__ void __launch_bounds__(ATT_THREADS) k_fattn(const AArgs a) {
     extern __shared__ __align__(16) uint8_t sm[];
-    __shared__ __align__(16) uint8_t qh[256 * 2], kh[256 * 2], vh[256 * 2];
-    __shared__ float tmp[3][256];
+    __shared__ __align__(16) uint8_t hrow[3][320];  // q, k, v head rows (adt), d <= 128
+    __shared__ float tmp[3][128];
     __shared__ float red[ATT_THREADS / 32];
     __shared__ float s_stat[2];
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ int abort_flag;
+    att_init_bars(bars, &abort_flag);
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int h = blockIdx.x, b = blockIdx.y;
     const int group = a.q_heads / a.kv_heads, g = h / group;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int d = a.d;
+    const int d = a.d, nbh = d / GTN_QBLK;
     const long hb = row_bytes(a.adt, d);
     const int p = a.pos[b], n = p + 1;
     const float* yrow = a.y + (long)b * a.ys;
     const int qd = a.q_heads * d, kvd = a.kv_heads * d;
     const bool rope = a.half > 0;
-    if (warp == 0) head_epilogue(a, yrow, h * d, a.bq ? a.bq + h * d : nullptr, rope, p, qh, tmp[0]);
-    if (warp == 1) head_epilogue(a, yrow, qd + g * d, a.bk ? a.bk + g * d : nullptr, rope, p, kh, tmp[1]);
-    if (warp == 2) head_epilogue(a, yrow, qd + kvd + g * d, a.bv ? a.bv + g * d : nullptr, false, p, vh, tmp[2]);
+    // (1) Linear requant [+ bias requant], one warp per (tensor t, block k)
+    for (int w = warp; w < 3 * nbh; w += ATT_THREADS / 32) {
+        const int t = w / nbh, k = w - t * nbh, i = k * GTN_QBLK + lane;
+        const int c0 = t == 0 ? h * d : (t == 1 ? qd + g * d : qd + kvd + g * d);
+        const uint16_t* bias = t == 0 ? a.bq : (t == 1 ? a.bk : a.bv);
+        float v = requant(yrow[c0 + i], lane, GTN_QBLK, a.adt, nullptr, 0);
+        if (bias) v = requant(v + h2f(bias[(t == 0 ? h : g) * d + i]), lane, GTN_QBLK, a.adt, nullptr, 0);
+        tmp[t][i] = v;
+    }
     __syncthreads();
-    uint8_t* kc = a.kc + (long)b * a.seq_stride;
-    uint8_t* vc = a.vc + (long)b * a.seq_stride;
+    // (2) RoPE (q, k) and the final requant into the head rows
+    for (int w = warp; w < 3 * nbh; w += ATT_THREADS / 32) {
+        const int t = w / nbh, k = w - t * nbh, i = k * GTN_QBLK + lane;
+        float y = tmp[t][i];
+        if (rope && t < 2) {
+            const float2* c = a.cs + (long)p * a.half;
+            if (i < a.half) {
+                const float2 cs = c[i];
+                const float p0 = tmp[t][i] * cs.x, p1 = tmp[t][i + a.half] * cs.y;
+                y = p0 - p1;
+            } else if (i < 2 * a.half) {
+                const float2 cs = c[i - a.half];
+                const float p2 = tmp[t][i - a.half] * cs.y, p3 = tmp[t][i] * cs.x;
+                y = p2 + p3;
+            }
+        }
+        requant(y, lane, GTN_QBLK, a.adt, hrow[t], k);
+    }
+    __syncthreads();
+    uint8_t* kc = a.kc + (long)b * a.seq_stride + (long)g * a.khs;
+    uint8_t* vc = a.vc + (long)b * a.seq_stride + (long)g * a.khs;
     if (h % group == 0) {
         for (int i = tid; i < hb; i += ATT_THREADS) {
-            kc[(long)p * a.kvs + (long)g * hb + i] = kh[i];
-            vc[(long)p * a.kvs + (long)g * hb + i] = vh[i];
+            kc[(long)p * a.kvs + i] = hrow[1][i];
+            vc[(long)p * a.kvs + i] = hrow[2][i];
         }
     }
-    float* pr = reinterpret_cast<float*>(sm);
-    uint8_t* vt = sm + ((n * 4 + 15) / 16) * 16;
-    float* part = reinterpret_cast<float*>(vt + (long)ATT_VTILE * hb);
-    const float scale = 1.0f / sqrtf((float)d);
-    float mx = -INFINITY;
-    for (int j = tid; j < n; j += ATT_THREADS) {
-        const uint8_t* kr = j == p ? kh : kc + (long)j * a.kvs + (long)g * hb;
-        const float dd = head_dot(qh, kr, a.adt, d);
-        const float sc = dd * scale;
-        pr[j] = sc;
-        mx = fmaxf(mx, sc);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) red[warp] = mx;
+    const AttSmem L = att_layout(sm, n, hb, d, bars, &abort_flag);
+    if (a.adt == GTN_Q8) build_prep_q8(hrow[0], 0, 0, 1, nbh, L.qp);
     __syncthreads();
-    if (tid == 0) {
-        float m = red[0];
-        for (int w = 1; w < ATT_THREADS / 32; ++w) m = fmaxf(m, red[w]);
-        s_stat[0] = m;
-    }
-    __syncthreads();
-    const float m = s_stat[0];
-    for (int j = tid; j < n; j += ATT_THREADS) pr[j] = exp_cr(pr[j] - m);
-    __syncthreads();
-    if (tid == 0) {
-        float sum = 0.0f;
-#pragma unroll 8
-        for (int j = 0; j < n; ++j) sum = sum + pr[j];
-        s_stat[1] = sum;
-    }
-    __syncthreads();
-    const float sum = s_stat[1];
-    for (int blk = warp; blk * GTN_QBLK < n; blk += ATT_THREADS / 32) {
-        const int j = blk * GTN_QBLK + lane;
-        const float pj = j < n ? pr[j] / sum : 0.0f;
-        const float back = requant(pj, lane, min(GTN_QBLK, n - blk * GTN_QBLK), a.adt, nullptr, 0);
-        __syncwarp();
-        if (j < n) pr[j] = back;
-    }
-    __syncthreads();
-    const int n8 = (n / 8) * 8;
-    const int npairs = d * 8;
-    const int per = (npairs + ATT_THREADS - 1) / ATT_THREADS;
-    float acc[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) acc[u] = 0.0f;
-    for (int t0 = 0; t0 < n; t0 += ATT_VTILE) {
-        const int nt = min(ATT_VTILE, n - t0);
-        if ((hb & 3) == 0 && (a.kvs & 3) == 0) {
-            const int wpr = (int)(hb / 4);
-            for (int i = tid; i < nt * wpr; i += ATT_THREADS) {
-                const int jj = i / wpr, ww = i % wpr;
-                const int j = t0 + jj;
-                const uint32_t* src = j == p ? reinterpret_cast<const uint32_t*>(vh)
-                                             : reinterpret_cast<const uint32_t*>(vc + (long)j * a.kvs + (long)g * hb);
-                reinterpret_cast<uint32_t*>(vt + (long)jj * hb)[ww] = src[ww];
-            }
-        } else {
-            for (int i = tid; i < nt * hb; i += ATT_THREADS) {
-                const int jj = i / hb, bb = i % hb;
-                const int j = t0 + jj;
-                vt[i] = j == p ? vh[bb] : vc[(long)j * a.kvs + (long)g * hb + bb];
-            }
-        }
-        __syncthreads();
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int pi = tid + u * ATT_THREADS;
-            if (u < per && pi < npairs) {
-                const int c = pi >> 3, l = pi & 7;
-                float acu = acc[u];
-                for (int jj = l; jj < nt && t0 + jj < n8; jj += 8) {
-                    const float vv = load_elem(vt + (long)jj * hb, a.adt, c);
-                    const float pp = pr[t0 + jj] * vv;
-                    acu = pp + acu;
-                }
-                acc[u] = acu;
-            }
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-        const int pi = tid + u * ATT_THREADS;
-        if (u < per && pi < npairs) part[(pi & 7) * d + (pi >> 3)] = acc[u];
-    }
-    __syncthreads();
+    att_core(kc, a.kvs, vc, a.kvs, (int)hb, n, p, p, hrow[1], hrow[2], hrow[0], L, a.adt, d, red, s_stat, a.err);
     asm volatile("griddepcontrol.launch_dependents;");
-    uint8_t* dst = a.out + (long)b * a.os + (long)h * hb;
-    for (int blk = warp; blk * GTN_QBLK < d; blk += ATT_THREADS / 32) {
-        const int c = blk * GTN_QBLK + lane;
-        float y = 0.0f;
-        if (c < d) {
-            y = part[c] + part[d + c];
-            for (int l = 2; l < 8; ++l) y = y + part[l * d + c];
-            for (int j = n8; j < n; ++j) {
-                const uint8_t* vr = j == p ? vh : vc + (long)j * a.kvs + (long)g * hb;
-                const float vv = load_elem(vr, a.adt, c);
-                const float pp = pr[j] * vv;
-                y = y + pp;
-            }
-        }
-        store_row_elem(dst, a.adt, blk, lane, d, y);
-    }
+    att_out(L.part, L.p, vc, a.kvs, n, p, hrow[2], a.adt, d, a.out + (long)b * a.os + (long)h * hb);
 }
 
-inline size_t fattn_smem(int n, int adt, int d) {
-    return (size_t)((n * 4 + 15) / 16) * 16 + (size_t)ATT_VTILE * row_bytes(adt, d) + (size_t)8 * d * 4 + 16;
-}
+inline size_t fattn_smem(int n, int adt, int d) { return attn_smem(n, adt, d); }
 
 // Greedy pick per sequence (sampler.cpp:30-41) + the decode loop's bookkeeping: the id becomes the
 // input token of the next position and is recorded; the position advances. grid B; block 1024.

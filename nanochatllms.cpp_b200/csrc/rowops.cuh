@@ -259,6 +259,22 @@ static __global__ void k_write_rows(const float* x, long xs, uint8_t* out, long 
     store_row_elem(out + (long)row * os, dt, blk, lane, n, v);
 }
 
+// Copies M new rows of K or V (reference layout: row m at src + m * ss, kv head g at g * hb) into
+// the engine's head-major cache (row p of head g at dst + g * hs + p * rs), rows p = p0 + m.
+// grid (kv heads, M); block 32.
+static __global__ void k_kv_scatter(const uint8_t* src, long ss, uint8_t* dst, long hs, long rs, int p0, int hb) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int g = blockIdx.x, m = blockIdx.y;
+    const uint8_t* s = src + (long)m * ss + (long)g * hb;
+    uint8_t* d = dst + (long)g * hs + (long)(p0 + m) * rs;
+    if ((((uintptr_t)s | (uintptr_t)d | (uintptr_t)hb) & 3) == 0) {
+        for (int i = threadIdx.x; i < hb / 4; i += blockDim.x)
+            reinterpret_cast<uint32_t*>(d)[i] = reinterpret_cast<const uint32_t*>(s)[i];
+    } else {
+        for (int i = threadIdx.x; i < hb; i += blockDim.x) d[i] = s[i];
+    }
+}
+
 // Greedy argmax (sampler.cpp:30-41): first index of the maximum under strict '>' from -inf.
 // One CTA of 1024 threads per row; each thread scans a contiguous slice in order, then a tree
 // keeps the larger value and, on ties, the smaller index.
