@@ -368,11 +368,12 @@ static int norm_common(const gtn_tensor* inp, const gtn_tensor* weight, const gt
         GTN_REQUIRE(bias->ndim == 1 && bias->dtype == GTN_F16 && bias->shape[0] == n, "layer_norm: bias");
     }
     const size_t smem = 2 * sizeof(float) * (size_t)n;  // values + the exact sum's scratch
+    const int nthreads = n > 1024 ? 512 : 256;  // the exact sum keeps <= 8 terms per thread up to n = 4096
     cudaError_t e;
     if (layer) {
         e = ensure_smem(k_norm<true>, smem);
         if (e == cudaSuccess)
-            e = launch_pdl(k_norm<true>, dim3(heads, n_ctx - start_pos), dim3(256), smem, S(stream),
+            e = launch_pdl(k_norm<true>, dim3(heads, n_ctx - start_pos), dim3(nthreads), smem, S(stream),
                            (const uint8_t*)inp->data, bstride(inp, 0), hs, (uint8_t*)out->data, bstride(out, 0), hs,
                            (int)inp->dtype, n, start_pos, (const uint16_t*)weight->data,
                            (const uint16_t*)bias->data);
@@ -380,7 +381,7 @@ static int norm_common(const gtn_tensor* inp, const gtn_tensor* weight, const gt
         e = ensure_smem(k_norm<false>, smem);
         // The 3-D path writes out with the input's strides (ops.cpp:879).
         if (e == cudaSuccess)
-            e = launch_pdl(k_norm<false>, dim3(heads, n_ctx - start_pos), dim3(256), smem, S(stream),
+            e = launch_pdl(k_norm<false>, dim3(heads, n_ctx - start_pos), dim3(nthreads), smem, S(stream),
                            (const uint8_t*)inp->data, bstride(inp, 0), hs, (uint8_t*)out->data,
                            inp->ndim == 3 ? bstride(inp, 0) : bstride(out, 0), hs, (int)inp->dtype, n, start_pos,
                            (const uint16_t*)weight->data, (const uint16_t*)nullptr);

@@ -43,9 +43,11 @@ __device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x);
 // q = roundf(x*scale) (half away from zero). Lanes >= n hold 0 and write nothing.
 // Returns the quantized value; every lane receives the fp16 delta in *dh.
 __device__ __forceinline__ int8_t warp_quant_block(float x, int lane, int n, uint16_t* dh) {
+    // absmax as the reference's loop finds it (std::max from 0 skips NaN): non-negative floats
+    // order like their bit patterns, so one warp max-reduction of the bits
     float a = lane < n ? fabsf(x) : 0.0f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    a = a == a ? a : 0.0f;
+    a = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(a)));
     const float delta = a / 127.0f;
     *dh = f2h(delta);
     const float scale = delta != 0.0f ? 1.0f / delta : 0.0f;

@@ -419,8 +419,8 @@ static cudaError_t norm_rows(const gtn_model* m, const uint8_t* x, uint8_t* out,
     const cudaError_t e = m->family == 1 ? ensure_smem(k_norm<true>, smem) : ensure_smem(k_norm<false>, smem);
     if (e != cudaSuccess) return e;
     if (m->family == 1)
-        return launch_pdl(k_norm<true>, dim3(1, M), dim3(256), smem, st, x, rs, 0L, out, rs, 0L, m->adt, m->d, 0, w, b);
-    return launch_pdl(k_norm<false>, dim3(1, M), dim3(256), smem, st, x, rs, 0L, out, rs, 0L, m->adt, m->d, 0, w,
+        return launch_pdl(k_norm<true>, dim3(1, M), dim3(512), smem, st, x, rs, 0L, out, rs, 0L, m->adt, m->d, 0, w, b);
+    return launch_pdl(k_norm<false>, dim3(1, M), dim3(512), smem, st, x, rs, 0L, out, rs, 0L, m->adt, m->d, 0, w,
                       (const uint16_t*)nullptr);
 }
 
@@ -563,11 +563,14 @@ static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) 
         const size_t smem = pro == PRO_RESNORM ? 2 * sizeof(float) * (size_t)a.K : 0;  // values + sum scratch
         cudaError_t e;
         if (pro == PRO_RESNORM) {
+            // one cluster of PCL CTAs per sequence (values in K floats of dynamic shared memory)
+            const size_t csmem = sizeof(float) * (size_t)a.K;
             if (dry) {
-                e = ensure_smem(k_prep<PRO_RESNORM>, smem);
+                e = ensure_smem(k_prep_cl, csmem);
             } else {
                 ++g_step_kernels;
-                e = launch_pdl(k_prep<PRO_RESNORM>, dim3(1, a.B), dim3(1024), smem, m->st, a, m->act, m->act_s);
+                e = launch_pdl_cluster(k_prep_cl, dim3(PCL, a.B), dim3(PCL_THREADS), csmem, m->st, PCL, a, m->act,
+                                       m->act_s);
             }
         } else if (!dry) {
             ++g_step_kernels;

@@ -18,6 +18,7 @@
 // weights (read-only) are prefetched with TMA before it, so a kernel's weight stream overlaps the
 // previous kernel under programmatic dependent launch.
 #pragma once
+#include <cooperative_groups.h>
 #include "attention.cuh"
 #include "matmul.cuh"
 #include "rowops.cuh"
@@ -119,11 +120,16 @@ __device__ __forceinline__ void fgemv_prologue(const FArgs& a, uint8_t* xq, floa
         }
         return;
     }
-    // PRO_RESNORM: residual update, then the norm's sequential sums (one thread per row).
+    // PRO_RESNORM: residual update, then the norm's sequential sums. Each warp takes blocks
+    // warp, warp + nwarps, ... and loads up to RN of them before computing (the loads overlap).
+    constexpr int RN = 4;
+    __shared__ unsigned int wmax[32];  // per warp: largest r*r bit pattern (row 0)
+    unsigned int mxb = 0u;
     for (int m = 0; m < mt; ++m) {
         float* sv = sval + (long)m * K;
         uint8_t* xo = (a.xout && blockIdx.x == 0) ? a.xout + (long)(m0 + m) * a.xout_s : nullptr;
         const uint8_t* xr = a.xres ? a.xres + (long)(m0 + m) * a.xres_s : nullptr;
+        const float* y = a.yadd ? a.yadd + (long)(m0 + m) * a.yadd_s : nullptr;
         const uint8_t* er = nullptr;
         if (a.emb) {
             int t = a.tok[(long)(m0 + m) * a.tok_s + a.pos[m0 + m]];
@@ -133,49 +139,66 @@ __device__ __forceinline__ void fgemv_prologue(const FArgs& a, uint8_t* xq, floa
             }
             er = a.emb + (long)t * a.emb_s;
         }
-        for (int blk = warp; blk < nbk; blk += nwarps) {
-            const int i = blk * GTN_QBLK + lane, nv = min(GTN_QBLK, K - blk * GTN_QBLK);
-            float r;
-            if (er) {
-                // token_embed (ops.cpp:526-545): Q8 / fp16 rows copied, Q4 rows requantized to Q8
-                const float e = i < K ? load_elem(er, a.emb_dt, i) : 0.0f;
-                if (a.emb_dt == a.adt) {
-                    r = e;
-                    if (xo && i < K) {
-                        if (a.adt == GTN_Q8) {
-                            const uint8_t* sb = er + (long)blk * GTN_Q8_BYTES;
-                            uint8_t* db = xo + (long)blk * GTN_Q8_BYTES;
-                            if (lane < 2) db[lane] = sb[lane];
-                            db[2 + lane] = sb[2 + lane];
-                        } else {
-                            reinterpret_cast<uint16_t*>(xo)[i] = reinterpret_cast<const uint16_t*>(er)[i];
+        for (int b0 = warp; b0 < nbk; b0 += RN * nwarps) {
+            float ev[RN], xv[RN], yv[RN];
+#pragma unroll
+            for (int j = 0; j < RN; ++j) {
+                const int blk = b0 + j * nwarps, i = blk * GTN_QBLK + lane;
+                const bool ok = blk < nbk && i < K;
+                ev[j] = ok && er ? load_elem(er, a.emb_dt, i) : 0.0f;
+                xv[j] = ok && xr ? load_elem(xr, a.adt, i) : 0.0f;
+                yv[j] = ok && y ? y[i] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < RN; ++j) {
+                const int blk = b0 + j * nwarps;
+                if (blk >= nbk) break;
+                const int i = blk * GTN_QBLK + lane, nv = min(GTN_QBLK, K - blk * GTN_QBLK);
+                float r;
+                if (er) {
+                    // token_embed (ops.cpp:526-545): Q8 / fp16 rows copied, Q4 rows requantized to Q8
+                    const float e = ev[j];
+                    if (a.emb_dt == a.adt) {
+                        r = e;
+                        if (xo && i < K) {
+                            if (a.adt == GTN_Q8) {
+                                const uint8_t* sb = er + (long)blk * GTN_Q8_BYTES;
+                                uint8_t* db = xo + (long)blk * GTN_Q8_BYTES;
+                                if (lane < 2) db[lane] = sb[lane];
+                                db[2 + lane] = sb[2 + lane];
+                            } else {
+                                reinterpret_cast<uint16_t*>(xo)[i] = reinterpret_cast<const uint16_t*>(er)[i];
+                            }
                         }
+                        if (a.scale_emb) r = requant(r * a.es, lane, nv, a.adt, xo, blk);  // minicpm.cpp:96
+                    } else {
+                        r = requant(e, lane, nv, a.adt, a.scale_emb ? nullptr : xo, blk);
+                        if (a.scale_emb) r = requant(r * a.es, lane, nv, a.adt, xo, blk);
                     }
-                    if (a.scale_emb) r = requant(r * a.es, lane, nv, a.adt, xo, blk);  // minicpm.cpp:96
-                } else {
-                    r = requant(e, lane, nv, a.adt, a.scale_emb ? nullptr : xo, blk);
-                    if (a.scale_emb) r = requant(r * a.es, lane, nv, a.adt, xo, blk);
-                }
-            } else {
-                const float xv = i < K ? load_elem(xr, a.adt, i) : 0.0f;
-                if (a.yadd) {
-                    const float* y = a.yadd + (long)(m0 + m) * a.yadd_s;
-                    float o = requant(i < K ? y[i] : 0.0f, lane, nv, a.adt, nullptr, blk);
+                } else if (y) {
+                    float o = requant(yv[j], lane, nv, a.adt, nullptr, blk);
                     if (a.scale_y) o = requant(o * a.ys, lane, nv, a.adt, nullptr, blk);  // minicpm.cpp:57-58
-                    r = requant(xv + o, lane, nv, a.adt, xo, blk);                        // ops::add
+                    r = requant(xv[j] + o, lane, nv, a.adt, xo, blk);                     // ops::add
                 } else {
-                    r = xv;
+                    r = xv[j];
+                }
+                if (i < K) {
+                    sv[i] = r;
+                    if (m == 0) mxb = max(mxb, seqsum_maxbits(r * r));
                 }
             }
-            if (i < K) sv[i] = r;
         }
     }
+    mxb = __reduce_max_sync(0xffffffffu, mxb);
+    if (lane == 0) wmax[warp] = mxb;
     __syncthreads();
     __shared__ float stat[MT][2];
     if (mt == 1 && !a.layer) {
         // one row: the exact parallel form of the sequential sum of squares (seqsum.cuh)
         __shared__ SeqSumSmem ss;
-        const float sq = seq_sum_squares(sval, K, ss, reinterpret_cast<int*>(sval + (size_t)mt * K));
+        unsigned int mb = lane < nwarps ? wmax[lane] : 0u;
+        mb = __reduce_max_sync(0xffffffffu, mb);
+        const float sq = seq_sum_squares(sval, K, ss, reinterpret_cast<int*>(sval + (size_t)mt * K), mb);
         if (tid == 0) {
             stat[0][0] = 0.0f;
             stat[0][1] = sqrtf(sq / (float)K);
@@ -209,25 +232,38 @@ __device__ __forceinline__ void fgemv_prologue(const FArgs& a, uint8_t* xq, floa
     for (int m = 0; m < mt; ++m) {
         const float* v = sval + (long)m * K;
         const float mean = stat[m][0], sd = stat[m][1];
-        for (int blk = warp; blk < nbk; blk += nwarps) {
-            const int i = blk * GTN_QBLK + lane, nv = min(GTN_QBLK, K - blk * GTN_QBLK);
-            float y = 0.0f;
-            if (i < K) {
-                if (a.layer) {
-                    const float dd = v[i] - mean;
-                    const float t = dd / (sd + 1e-05f);
-                    const float u = t * h2f(a.nw[i]);
-                    y = u + h2f(a.nb[i]);
-                } else {
-                    const float t = v[i] / (sd + 1e-6f);
-                    y = t * h2f(a.nw[i]);
-                }
+        for (int b0 = warp; b0 < nbk; b0 += RN * nwarps) {
+            float wv[RN], bv[RN];
+#pragma unroll
+            for (int j = 0; j < RN; ++j) {
+                const int blk = b0 + j * nwarps, i = blk * GTN_QBLK + lane;
+                const bool ok = blk < nbk && i < K;
+                wv[j] = ok ? h2f(a.nw[i]) : 0.0f;
+                bv[j] = ok && a.layer ? h2f(a.nb[i]) : 0.0f;
             }
-            if (a.post) {
-                const float nq = requant(y, lane, nv, a.adt, nullptr, blk);
-                requant(nq * a.ps, lane, nv, a.adt, xq + (long)m * xrb, blk);
-            } else {
-                requant(y, lane, nv, a.adt, xq + (long)m * xrb, blk);
+#pragma unroll
+            for (int j = 0; j < RN; ++j) {
+                const int blk = b0 + j * nwarps;
+                if (blk >= nbk) break;
+                const int i = blk * GTN_QBLK + lane, nv = min(GTN_QBLK, K - blk * GTN_QBLK);
+                float yv = 0.0f;
+                if (i < K) {
+                    if (a.layer) {
+                        const float dd = v[i] - mean;
+                        const float t = dd / (sd + 1e-05f);
+                        const float u = t * wv[j];
+                        yv = u + bv[j];
+                    } else {
+                        const float t = v[i] / (sd + 1e-6f);
+                        yv = t * wv[j];
+                    }
+                }
+                if (a.post) {
+                    const float nq = requant(yv, lane, nv, a.adt, nullptr, blk);
+                    requant(nq * a.ps, lane, nv, a.adt, xq + (long)m * xrb, blk);
+                } else {
+                    requant(yv, lane, nv, a.adt, xq + (long)m * xrb, blk);
+                }
             }
         }
     }
@@ -340,10 +376,10 @@ __global__ void __launch_bounds__(NW * 32) k_fgemv(const FArgs a) {
 }
 
 // Computes the activation rows of one GEMV once (residual update + norm, or the SwiGLU chain) and
-// writes them to `act` (row stride act_s bytes); grid (1, B), block 1024, dynamic smem K floats
+// writes them to `act` (row stride act_s bytes); grid (1, B), block 512, dynamic smem K floats
 // for RESNORM. It lets the following GEMV launch at once, so its weight prefetch overlaps this.
 template <int PRO>
-static __global__ void __launch_bounds__(1024) k_prep(const FArgs a, uint8_t* act, long act_s) {
+static __global__ void __launch_bounds__(512) k_prep(const FArgs a, uint8_t* act, long act_s) {
     extern __shared__ float sval[];
     if (PRO == PRO_RESNORM) {  // the norm weights do not depend on the previous kernel: warm L2 now
         const int lines = (a.K * 2 + 127) / 128;
@@ -356,6 +392,444 @@ static __global__ void __launch_bounds__(1024) k_prep(const FArgs a, uint8_t* ac
     asm volatile("griddepcontrol.launch_dependents;");
     const int m = blockIdx.y;
     fgemv_prologue<PRO, 1>(a, act + (long)m * act_s, sval, m, 1);
+}
+
+// ---- residual update + norm on a cluster of PCL CTAs ------------------------------------------
+// The same computation as k_prep<PRO_RESNORM>, spread over a thread-block cluster so that the
+// per-block requantizations (three per 32 elements) run on PCL SMs instead of one. CTA c owns the
+// 32-blocks [c*E, (c+1)*E) of the row (E = ceil(blocks / PCL)). The exact sum of squares is split
+// as in seq_sum_exact; every CTA pushes what the others need into their shared memory (remote
+// stores of distributed shared memory), so each CTA reads its own copy after the cluster barrier:
+//   B1  largest square of each CTA (and every value to rank 0, for LayerNorm and the fallback)
+//   B2  fixed-point total of each CTA (the exact global prefix of every element follows)
+//   B3  heads (index, p, increment parity), per-CTA per-binade increment totals, ties, parities
+// then every CTA walks the binades itself (same data, same result) and normalizes its blocks.
+// LayerNorm, or a failed check of the exact sum: rank 0 runs the reference's serial loops and
+// pushes (mean, sd) to all CTAs before one more barrier (the condition is the same in all CTAs).
+// grid (PCL, B), cluster (PCL, 1, 1), block PCL_THREADS, dynamic smem K floats.
+constexpr int PCL = 8;
+constexpr int PCL_THREADS = 256;
+constexpr int PCL_TIES = 32;  // ties per CTA
+
+struct PclShared {
+    // pushed by every CTA before the barrier that publishes them
+    unsigned int maxv[PCL];
+    long long T[PCL];                  // fixed-point totals per CTA
+    int head[SEQSUM_SLOTS];
+    float phead[SEQSUM_SLOTS];
+    int hpar[SEQSUM_SLOTS];            // global increment parity at the head
+    long long tot[PCL][SEQSUM_SLOTS];  // increments per CTA per binade
+    int tie[PCL][PCL_TIES], tslot[PCL][PCL_TIES], tpar[PCL][PCL_TIES];  // tpar: CTA-local parity
+    int ntie[PCL];
+    int cpar[PCL];                     // parity of each CTA's increment total
+    int bad;
+    float stat[2];                     // (mean, sd) pushed by rank 0 on the serial path
+    // CTA-local scratch
+    long long wsum[PCL_THREADS / 32];
+    int wpar[PCL_THREADS / 32];
+    unsigned int wmax[PCL_THREADS / 32];
+    long long ltot[SEQSUM_SLOTS];
+    int lt[PCL_TIES], lts[PCL_TIES], ltp[PCL_TIES];
+    int lnt;
+    int sslot[PCL * PCL_TIES], sd[PCL * PCL_TIES], d0[SEQSUM_SLOTS], x[SEQSUM_SLOTS];
+    long long btot[SEQSUM_SLOTS];
+    int gpo[PCL + 1], tbase[PCL + 1];
+    float walk[2];
+};
+
+// One block of the residual update (as in fgemv_prologue<PRO_RESNORM>): returns the new residual
+// value of element blk*32 + lane (already requantized), storing its block into xo if non-null.
+__device__ __forceinline__ float resnorm_block(const FArgs& a, int blk, int lane, const uint8_t* er, float ev,
+                                               float xv, float yv, bool has_y, uint8_t* xo) {
+    const int K = a.K, i = blk * GTN_QBLK + lane, nv = min(GTN_QBLK, K - blk * GTN_QBLK);
+    float r;
+    if (er) {
+        if (a.emb_dt == a.adt) {
+            r = ev;
+            if (xo && i < K) {
+                if (a.adt == GTN_Q8) {
+                    const uint8_t* sb = er + (long)blk * GTN_Q8_BYTES;
+                    uint8_t* db = xo + (long)blk * GTN_Q8_BYTES;
+                    if (lane < 2) db[lane] = sb[lane];
+                    db[2 + lane] = sb[2 + lane];
+                } else {
+                    reinterpret_cast<uint16_t*>(xo)[i] = reinterpret_cast<const uint16_t*>(er)[i];
+                }
+            }
+            if (a.scale_emb) r = requant(r * a.es, lane, nv, a.adt, xo, blk);  // minicpm.cpp:96
+        } else {
+            r = requant(ev, lane, nv, a.adt, a.scale_emb ? nullptr : xo, blk);
+            if (a.scale_emb) r = requant(r * a.es, lane, nv, a.adt, xo, blk);
+        }
+    } else if (has_y) {
+        float o = requant(yv, lane, nv, a.adt, nullptr, blk);
+        if (a.scale_y) o = requant(o * a.ys, lane, nv, a.adt, nullptr, blk);  // minicpm.cpp:57-58
+        r = requant(xv + o, lane, nv, a.adt, xo, blk);                        // ops::add
+    } else {
+        r = xv;
+    }
+    return r;
+}
+
+static __global__ void __launch_bounds__(PCL_THREADS) k_prep_cl(const FArgs a, uint8_t* act, long act_s) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    extern __shared__ float sv[];  // the row, at global element indices (rank 0: all of it)
+    __shared__ PclShared S;
+    const int rank = (int)cl.block_rank();
+    float* sv0 = cl.map_shared_rank(sv, 0);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarps = PCL_THREADS / 32;
+    const int K = a.K, nbk = (K + GTN_QBLK - 1) / GTN_QBLK, E = (nbk + PCL - 1) / PCL;
+    const int b0 = min(nbk, rank * E), b1 = min(nbk, b0 + E);
+    const int e0 = b0 * GTN_QBLK, e1 = min(K, b1 * GTN_QBLK);
+    {  // the norm weights do not depend on the previous kernel: warm L2 now
+        const int lines = (e1 - e0) * 2 / 128 + 2;
+        for (int i = tid; i < lines; i += PCL_THREADS) {
+            const long off = min(2L * e0 + 128L * i, 2L * K - 2);
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.nw) + off));
+            if (a.nb) asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.nb) + off));
+        }
+    }
+    // local aggregation areas (remote writes into them come after B2)
+    if (tid < SEQSUM_SLOTS) {
+        S.ltot[tid] = 0;
+        S.head[tid] = -1;
+        S.d0[tid] = -1;
+        S.x[tid] = 0;
+    }
+    if (tid == 0) {
+        S.lnt = 0;
+        S.bad = 0;
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int m = blockIdx.y;
+    // ---- residual update of this CTA's blocks
+    uint8_t* xo = a.xout ? a.xout + (long)m * a.xout_s : nullptr;  // every CTA writes its own blocks
+    const uint8_t* xr = a.xres ? a.xres + (long)m * a.xres_s : nullptr;
+    const float* y = a.yadd ? a.yadd + (long)m * a.yadd_s : nullptr;
+    const uint8_t* er = nullptr;
+    if (a.emb) {
+        int t = a.tok[(long)m * a.tok_s + a.pos[m]];
+        if (t < 0 || t >= a.n_vocab) {
+            if (tid == 0 && rank == 0 && a.err) atomicOr(a.err, GTN_DEVERR_TOKEN);
+            t = 0;
+        }
+        er = a.emb + (long)t * a.emb_s;
+    }
+    unsigned int mxb = 0u;
+    for (int blk = b0 + warp; blk < b1; blk += nwarps) {
+        const int i = blk * GTN_QBLK + lane;
+        const bool ok = i < K;
+        const float ev = ok && er ? load_elem(er, a.emb_dt, i) : 0.0f;
+        const float xv = ok && xr ? load_elem(xr, a.adt, i) : 0.0f;
+        const float yv = ok && y ? y[i] : 0.0f;
+        const float r = resnorm_block(a, blk, lane, er, ev, xv, yv, y != nullptr, xo);
+        if (ok) {
+            sv[i] = r;
+            if (rank != 0) sv0[i] = r;
+            mxb = max(mxb, seqsum_maxbits(r * r));
+        }
+    }
+    mxb = __reduce_max_sync(0xffffffffu, mxb);
+    if (lane == 0) S.wmax[warp] = mxb;
+    __syncthreads();
+    if (warp == 0) {
+        unsigned int mb = lane < nwarps ? S.wmax[lane] : 0u;
+        mb = __reduce_max_sync(0xffffffffu, mb);
+        if (lane < PCL) cl.map_shared_rank(&S, lane)->maxv[rank] = mb;
+    }
+    cl.sync();  // B1
+    const bool exact = !a.layer && K <= (1 << 14);  // K: keeps the fixed-point sum below 2^63
+    unsigned int maxbits = 0u;
+#pragma unroll
+    for (int r = 0; r < PCL; ++r) maxbits = max(maxbits, S.maxv[r]);
+    const int emax = maxbits >= 0x800000u ? (int)(maxbits >> 23) - 127 : -126;
+    const int eoff = 23 + SEQSUM_FRAC_BITS - emax;
+    auto fixed = [&](float p) -> long long {
+        unsigned int M;
+        int Ex;
+        seqsum_split(p, M, Ex);
+        const int sh = Ex - emax + SEQSUM_FRAC_BITS;
+        if (sh >= 0) return (long long)M << sh;
+        return sh > -32 ? (long long)(M >> -sh) : 0LL;
+    };
+    const int ne = e1 - e0, per = (ne + PCL_THREADS - 1) / PCL_THREADS;
+    const int i0 = min(e1, e0 + tid * per), i1 = min(e1, i0 + per);
+    // ---- fixed-point totals; the exclusive prefix of each thread's chunk within the CTA
+    long long Q = 0;
+    if (exact) {
+        long long loc = 0;
+        for (int i = i0; i < i1; ++i) loc += fixed(sv[i] * sv[i]);
+        long long inc = loc;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long t = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += t;
+        }
+        if (lane == 31) S.wsum[warp] = inc;
+        __syncthreads();
+        long long base = 0, tot = 0;
+        for (int w = 0; w < nwarps; ++w) {
+            const long long ws = S.wsum[w];
+            if (w < warp) base += ws;
+            tot += ws;
+        }
+        Q = base + inc - loc;
+        if (tid < PCL) cl.map_shared_rank(&S, tid)->T[rank] = tot;
+    }
+    cl.sync();  // B2
+    if (exact && maxbits != 0u) {
+        for (int r = 0; r < rank; ++r) Q += S.T[r];
+        // ---- heads, increments, ties, parities
+        int sl_prev = Q > 0 ? 63 - __clzll(Q) : -1;
+        int par = 0;  // parity of this thread's increments so far
+        int head_s[4], head_i[4], head_p[4], nh = 0;
+        float head_v[4];
+        int tie_i[4], tie_s[4], tie_p[4], nt = 0;
+        bool bad = maxbits >= 0x7f800000u;
+        for (int k = 0; k < per; ++k) {  // uniform trip count: the warp reductions below
+            const int i = i0 + k;
+            const bool valid = i < i1;
+            const float p = valid ? sv[i] * sv[i] : 0.0f;
+            int inc = 0, sl = -1;
+            if (valid) {
+                Q += fixed(p);
+                if (Q == 0) {
+                    if (p != 0.0f) bad = true;
+                } else {
+                    sl = 63 - __clzll(Q);
+                    if (sl != sl_prev) {
+                        if (nh < 4) {
+                            head_s[nh] = sl;
+                            head_i[nh] = i;
+                            head_v[nh] = p;
+                            head_p[nh] = par;  // increments before the head (its own is 0)
+                            ++nh;
+                        } else {
+                            bad = true;
+                        }
+                    } else {
+                        const int e = sl - eoff;
+                        unsigned int M;
+                        int Ex;
+                        seqsum_split(p, M, Ex);
+                        const int sh = e - Ex;
+                        if (sh < 0 || e < -126) {
+                            bad = true;
+                        } else if (sh == 0) {
+                            inc = (int)M;
+                        } else if (sh < 32) {
+                            inc = (int)(M >> sh);
+                            const unsigned int rem = M & ((1u << sh) - 1u), half = 1u << (sh - 1);
+                            if (rem > half) {
+                                ++inc;
+                            } else if (rem == half) {
+                                if (nt < 4) {
+                                    tie_i[nt] = i;
+                                    tie_s[nt] = sl;
+                                    tie_p[nt] = par ^ (inc & 1);
+                                    ++nt;
+                                } else {
+                                    bad = true;
+                                }
+                            }
+                        }
+                    }
+                    par ^= inc & 1;
+                    sl_prev = sl;
+                }
+            }
+            // per-binade totals: the lanes of one binade add up their increments, one atomic each
+            const unsigned int grp = __match_any_sync(0xffffffffu, sl);
+            const int gsum = __reduce_add_sync(grp, inc);
+            if (sl >= 0 && lane == __ffs(grp) - 1 && gsum)
+                atomicAdd(reinterpret_cast<unsigned long long*>(&S.ltot[sl]), (unsigned long long)(long long)gsum);
+        }
+        // exclusive parity prefix of the chunks within the CTA
+        const unsigned int pb = __ballot_sync(0xffffffffu, par & 1);
+        const int lane_pre = __popc(pb & ((1u << lane) - 1u)) & 1;
+        if (lane == 0) S.wpar[warp] = __popc(pb) & 1;
+        __syncthreads();
+        int wpre = 0, ctot = 0;
+        for (int w = 0; w < nwarps; ++w) {
+            if (w < warp) wpre ^= S.wpar[w];
+            ctot ^= S.wpar[w];
+        }
+        const int pre = wpre ^ lane_pre;  // parity of the CTA's increments before this chunk
+        for (int k = 0; k < nt; ++k) {  // this CTA's ties with their CTA-local inclusive parity
+            const int q = atomicAdd(&S.lnt, 1);
+            if (q < PCL_TIES) {
+                S.lt[q] = tie_i[k];
+                S.lts[q] = tie_s[k];
+                S.ltp[q] = pre ^ tie_p[k];
+            } else {
+                bad = true;
+            }
+        }
+        __syncthreads();
+        // push to every CTA: heads (with the CTA-local parity; the global offset is added there),
+        // per-binade totals, ties, totals, failures
+        for (int r = 0; r < PCL; ++r) {
+            PclShared* D = cl.map_shared_rank(&S, r);
+            for (int k = 0; k < nh; ++k) {
+                D->head[head_s[k]] = head_i[k];
+                D->phead[head_s[k]] = head_v[k];
+                D->hpar[head_s[k]] = pre ^ head_p[k];
+            }
+            if (bad) D->bad = 1;
+        }
+        const int nlt = min(S.lnt, PCL_TIES);
+        for (int q = tid; q < PCL * SEQSUM_SLOTS; q += PCL_THREADS)
+            cl.map_shared_rank(&S, q / SEQSUM_SLOTS)->tot[rank][q % SEQSUM_SLOTS] = S.ltot[q % SEQSUM_SLOTS];
+        for (int q = tid; q < PCL * nlt; q += PCL_THREADS) {
+            PclShared* D = cl.map_shared_rank(&S, q / nlt);
+            const int k = q % nlt;
+            D->tie[rank][k] = S.lt[k];
+            D->tslot[rank][k] = S.lts[k];
+            D->tpar[rank][k] = S.ltp[k];
+        }
+        if (tid < PCL) {
+            PclShared* D = cl.map_shared_rank(&S, tid);
+            D->ntie[rank] = nlt;
+            D->cpar[rank] = ctot;
+            if (S.lnt > PCL_TIES) D->bad = 1;
+        }
+    }
+    cl.sync();  // B3
+    // ---- the walk, in every CTA
+    bool ok = exact && !S.bad;
+    float sum = 0.0f;
+    if (exact && maxbits != 0u && ok) {
+        if (tid == 0) {
+            S.gpo[0] = 0;
+            S.tbase[0] = 0;
+            for (int r = 0; r < PCL; ++r) {
+                S.gpo[r + 1] = S.gpo[r] ^ S.cpar[r];
+                S.tbase[r + 1] = S.tbase[r] + S.ntie[r];
+            }
+        }
+        if (tid >= 32 && tid < 32 + SEQSUM_SLOTS) {  // warps 1-2: the binade totals
+            const int sl = tid - 32;
+            long long t = 0;
+#pragma unroll
+            for (int r = 0; r < PCL; ++r) t += S.tot[r][sl];
+            S.btot[sl] = t;
+        }
+        __syncthreads();
+        const int nties = S.tbase[PCL];
+        for (int k = tid; k < nties; k += PCL_THREADS) {
+            int r = 0;
+            while (k >= S.tbase[r + 1]) ++r;
+            const int kk = k - S.tbase[r];
+            const int i = S.tie[r][kk], sl = S.tslot[r][kk];
+            int rk = S.tbase[r];  // rank among all ties: earlier CTAs, then this CTA's smaller indices
+            for (int j = 0; j < S.ntie[r]; ++j) rk += S.tie[r][j] < i;
+            const int h = S.head[sl];
+            const int hr = (h / GTN_QBLK) / E;
+            S.sslot[rk] = sl;
+            S.sd[rk] = (S.gpo[r] ^ S.tpar[r][kk]) ^ (S.gpo[hr] ^ S.hpar[sl]);
+        }
+        __syncthreads();
+        for (int k = tid; k < nties; k += PCL_THREADS) {
+            const int sl = S.sslot[k];
+            if (k == 0 || S.sslot[k - 1] != sl) S.d0[sl] = S.sd[k];
+            else atomicAdd(&S.x[sl], S.sd[k] ^ S.sd[k - 1]);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            float Sx = 0.0f;
+            bool okw = true;
+            unsigned long long hm = (unsigned long long)__ballot_sync(0xffffffffu, S.head[lane] >= 0) |
+                                    ((unsigned long long)__ballot_sync(0xffffffffu, S.head[lane + 32] >= 0) << 32);
+            while (okw && hm) {
+                const int sl = __ffsll((long long)hm) - 1;
+                hm &= hm - 1;
+                const int e = sl - eoff;
+                Sx = Sx + S.phead[sl];
+                const unsigned int b = __float_as_uint(Sx);
+                if ((int)(b >> 23) - 127 != e || e < -126) {
+                    okw = false;
+                    break;
+                }
+                long long Sb = (long long)((b & 0x7fffffu) | 0x800000u);
+                const int dd = S.d0[sl];
+                if (dd >= 0) Sb += ((Sb + dd) & 1) + S.x[sl];
+                Sb += S.btot[sl];
+                if (Sb >= (1LL << 24)) {
+                    okw = false;
+                    break;
+                }
+                Sx = __uint_as_float(((unsigned int)(e + 127) << 23) | ((unsigned int)Sb & 0x7fffffu));
+            }
+            if (lane == 0) {
+                S.walk[0] = okw ? 1.0f : 0.0f;
+                S.walk[1] = Sx;
+            }
+        }
+        __syncthreads();
+        ok = S.walk[0] != 0.0f;
+        sum = S.walk[1];
+    }
+    float mean = 0.0f, sd = 0.0f;
+    if (exact && (maxbits == 0u || ok)) {
+        sd = sqrtf(sum / (float)K);  // every square +0 (sum 0), or the walk's exact sum
+    } else {
+        // LayerNorm, or a failed check: the reference's loops on rank 0, pushed to every CTA
+        if (rank == 0 && tid == 0) {
+            if (a.layer) {
+                float s0 = 0.0f;
+                for (int i = 0; i < K; ++i) s0 = s0 + sv[i];
+                mean = s0 / (float)K;
+                float ss = 0.0f;
+                for (int i = 0; i < K; ++i) {
+                    const float d = sv[i] - mean;
+                    const float d2 = d * d;
+                    ss = ss + d2;
+                }
+                sd = sqrtf(ss / (float)K);
+            } else {
+                float sq = 0.0f;
+                for (int i = 0; i < K; ++i) {
+                    const float p = sv[i] * sv[i];
+                    sq = sq + p;
+                }
+                sd = sqrtf(sq / (float)K);
+            }
+            for (int r = 0; r < PCL; ++r) {
+                PclShared* D = cl.map_shared_rank(&S, r);
+                D->stat[0] = mean;
+                D->stat[1] = sd;
+            }
+        }
+        cl.sync();  // B4 (taken by every CTA: the condition is the same everywhere)
+        mean = S.stat[0];
+        sd = S.stat[1];
+    }
+    // ---- norm of this CTA's blocks -> act
+    uint8_t* xq = act + (long)m * act_s;
+    for (int blk = b0 + warp; blk < b1; blk += nwarps) {
+        const int i = blk * GTN_QBLK + lane, nv = min(GTN_QBLK, K - blk * GTN_QBLK);
+        float yv = 0.0f;
+        if (i < K) {
+            if (a.layer) {
+                const float dd = sv[i] - mean;
+                const float t = dd / (sd + 1e-05f);
+                const float u = t * h2f(a.nw[i]);
+                yv = u + h2f(a.nb[i]);
+            } else {
+                const float t = sv[i] / (sd + 1e-6f);
+                yv = t * h2f(a.nw[i]);
+            }
+        }
+        if (a.post) {
+            const float nq = requant(yv, lane, nv, a.adt, nullptr, blk);
+            requant(nq * a.ps, lane, nv, a.adt, xq, blk);
+        } else {
+            requant(yv, lane, nv, a.adt, xq, blk);
+        }
+    }
+    // no remote access after the last cluster barrier: a CTA may leave while others still work
 }
 
 // The SwiGLU activation is block-local, so it is spread over many CTAs: grid (ceil(blocks/32), B),

@@ -64,7 +64,8 @@ static __global__ void k_rowop(const uint8_t* a, long as, const uint8_t* b, long
 // order, as the reference computes them (one thread), the rest is element-parallel.
 //   rms_norm_vec_f32 ops.cpp:830-846: x / (sqrt(sum(x^2)/n) + 1e-6) * w
 //   vec_layer_norm_f32 ops.cpp:669-698: ((x - mean) / (sqrt(sum((x-mean)^2)/n) + 1e-5)) * w + b
-// grid: (heads, rows); block 256; dynamic smem 2n floats (values + the exact sum's scratch).
+// grid: (heads, rows); block 256 (512 for n > 1024); dynamic smem 2n floats (values + the exact
+// sum's scratch).
 template <bool LAYER>
 static __global__ void k_norm(const uint8_t* x, long xs, long hs, uint8_t* out, long os, long ohs, int dt, int n,
                               int row0, const uint16_t* w, const uint16_t* bvec) {

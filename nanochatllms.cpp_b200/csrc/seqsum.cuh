@@ -15,17 +15,18 @@
 // d_j != d_(j-1): the binade's total round-ups are c_0 + sum_j (d_j xor d_(j-1)), which depends
 // on the running value only through the parity of S_head/u.
 //
-// Algorithm (one CTA, every thread owns a contiguous chunk of terms):
-//  (1) terms p_i; the exponent of the largest fixes a fixed-point scale;
+// Algorithm (one CTA, every thread owns a contiguous chunk of terms, kept in registers):
+//  (1) the exponent of the largest term fixes a fixed-point scale (the caller may supply it);
 //  (2) an exact int64 prefix scan of floor(p_i * 2^F) predicts the binade of the running sum after
 //      term i. Integer sums are associative, so every thread sees the same prediction at every
 //      index;
 //  (3) the first term of each predicted binade is its "head"; every other term gets its integer
 //      increment w.r.t. its binade's ulp (integer arithmetic on the float's bits); ties are listed;
 //  (4) an int64 prefix scan of the increments;
-//  (5) per binade (in parallel): the increments from its head to the next head, and the tie terms
-//      above; then one thread walks the binades in order: S = fl(S + p_head) (an exact IEEE add)
-//      must land in binade e, then S/u += increments + round-ups, which must stay below 2^24.
+//  (5) per binade (in parallel): the increments from its head to the next head and the tie terms
+//      above; then warp 0 walks the binades in order (their data in lane registers, fetched by
+//      shuffles): S = fl(S + p_head) (an exact IEEE add) must land in binade e, then
+//      S/u += increments + round-ups, which must stay below 2^24.
 // Any failed check (a mispredicted crossing, a term below the fixed-point resolution, a subnormal
 // binade, a non-finite term, more ties than the list holds) makes the CTA fall back to the plain
 // sequential loop, so the result is always bit-identical to the serial sum.
@@ -35,20 +36,21 @@
 namespace gtn {
 
 constexpr int SEQSUM_THREADS_MAX = 1024;
-constexpr int SEQSUM_SLOTS = 64;      // binades slot = floor(log2(Q)), Q = the fixed-point sum
+constexpr int SEQSUM_SLOTS = 64;      // binade slot = floor(log2(Q)), Q = the fixed-point sum
 constexpr int SEQSUM_TIES_MAX = 128;
 constexpr int SEQSUM_FRAC_BITS = 25;  // the largest term becomes < 2^(24 + 25)
+constexpr int SEQSUM_PER_MAX = 8;     // terms per thread kept in registers
 
 struct SeqSumSmem {
-    long long wsum[SEQSUM_THREADS_MAX / 32];
-    long long cpre[SEQSUM_THREADS_MAX];  // per-thread exclusive prefix of the increments
-    long long tot[SEQSUM_SLOTS];         // per binade: increments from its head to the next head
+    long long wsum[2][SEQSUM_THREADS_MAX / 32];  // per-warp partials of the two scans
+    long long cpre[SEQSUM_THREADS_MAX];          // per-thread exclusive prefix of the increments
+    long long tot[SEQSUM_SLOTS];                 // per binade: increments from its head to the next head
     int head[SEQSUM_SLOTS];
     float phead[SEQSUM_SLOTS];
-    int d0[SEQSUM_SLOTS];                // parity of the first tie (or -1: no tie)
-    int x[SEQSUM_SLOTS];                 // sum of d_j xor d_(j-1) over the binade's ties
+    int d0[SEQSUM_SLOTS];  // parity of the first tie (or -1: no tie)
+    int x[SEQSUM_SLOTS];   // sum of d_j xor d_(j-1) over the binade's ties
     int tie[SEQSUM_TIES_MAX], tslot[SEQSUM_TIES_MAX];
-    int stie[SEQSUM_TIES_MAX], sslot[SEQSUM_TIES_MAX], sd[SEQSUM_TIES_MAX];
+    int sslot[SEQSUM_TIES_MAX], sd[SEQSUM_TIES_MAX];
     unsigned int mask[2];
     int ntie;
     int bad;
@@ -56,7 +58,8 @@ struct SeqSumSmem {
     float result;
 };
 
-// Exclusive prefix of x over the CTA (thread order), in int64; synchronizes the CTA.
+// Exclusive prefix of x over the CTA (thread order), in int64, with per-warp partials in `wsum`
+// (not read by a scan in flight); two CTA barriers.
 __device__ __forceinline__ long long seqsum_exscan64(long long x, long long* wsum) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
     long long inc = x;
@@ -65,7 +68,6 @@ __device__ __forceinline__ long long seqsum_exscan64(long long x, long long* wsu
         const long long t = __shfl_up_sync(0xffffffffu, inc, o);
         if (lane >= o) inc += t;
     }
-    __syncthreads();  // wsum may still be read by a previous call
     if (lane == 31) wsum[warp] = inc;
     __syncthreads();
     if (warp == 0) {
@@ -89,32 +91,44 @@ __device__ __forceinline__ void seqsum_split(float p, unsigned int& M, int& E) {
     E = ef ? (int)ef - 127 : -126;
 }
 
+// Largest of non-negative floats through their bit patterns (NaN maps above +inf).
+__device__ __forceinline__ unsigned int seqsum_maxbits(float p) { return __float_as_uint(p); }
+
 // Returns fl(...fl(fl(0 + p_0) + p_1)... + p_{n-1}) where p_i = term(i) >= 0 (a float computed
-// the same way on every call). `incs`: n ints of scratch (shared memory). All threads of the CTA
-// must call it (blockDim.x <= 1024, a multiple of 32, >= 64); it synchronizes the CTA.
+// the same way on every call). `incs`: n ints of scratch (shared memory). maxbits: the largest
+// term's bit pattern if the caller knows it (from seqsum_maxbits), else 0. All threads of the
+// CTA must call it (blockDim.x <= 1024, a multiple of 32, >= 64); it synchronizes the CTA.
 template <class Term>
-__device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, int* incs) {
+__device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, int* incs, unsigned int maxbits = 0u) {
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const int per = (n + nt - 1) / nt;
     const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
+    // more than SEQSUM_PER_MAX terms per thread: the serial loop (cnt = 0 skips the parallel work)
+    const int cnt = per <= SEQSUM_PER_MAX ? i1 - i0 : 0;
+    float pv[SEQSUM_PER_MAX];
+#pragma unroll
+    for (int k = 0; k < SEQSUM_PER_MAX; ++k) pv[k] = k < cnt ? term(i0 + k) : 0.0f;
     if (tid < SEQSUM_SLOTS) {
         s.head[tid] = -1;
         s.d0[tid] = -1;
         s.x[tid] = 0;
     }
     if (tid == 0) {
-        s.bad = n > (1 << 14);  // keeps the fixed-point sum below 2^63
+        s.bad = n > (1 << 14) || per > SEQSUM_PER_MAX;  // n: keeps the fixed-point sum below 2^63
         s.ntie = 0;
-        s.maxbits = 0u;
+        s.maxbits = maxbits;
+    }
+    if (maxbits == 0u) {
+        __syncthreads();
+        // (1) largest term (non-negative floats order like their bit patterns)
+        unsigned int mb = 0u;
+#pragma unroll
+        for (int k = 0; k < SEQSUM_PER_MAX; ++k) mb = max(mb, __float_as_uint(pv[k]));  // pv >= +0
+        mb = __reduce_max_sync(0xffffffffu, mb);
+        if (lane == 0) atomicMax(&s.maxbits, mb);
     }
     __syncthreads();
-    // (1) largest term (non-negative floats order like their bit patterns)
-    unsigned int mb = 0u;
-    for (int i = i0; i < i1; ++i) mb = max(mb, __float_as_uint(term(i)));
-    mb = __reduce_max_sync(0xffffffffu, mb);
-    if (lane == 0) atomicMax(&s.maxbits, mb);
-    __syncthreads();
-    const unsigned int maxbits = s.maxbits;
+    maxbits = s.maxbits;
     if (maxbits == 0u) return 0.0f;                   // every term is +0: the sum is exactly 0
     if (maxbits >= 0x7f800000u) s.bad = 1;            // inf / nan / a negative term
     const int emax = maxbits >= 0x800000u ? (int)(maxbits >> 23) - 127 : -126;
@@ -128,19 +142,22 @@ __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, 
         if (sh >= 0) return (long long)M << sh;  // sh <= 25
         return sh > -32 ? (long long)(M >> -sh) : 0LL;
     };
-    // binade exponent of slot sl: Q = S * 2^(23 + FRAC - emax) => e = sl - (23 + FRAC - emax)
+    // binade exponent of slot sl: Q = S * 2^eoff => e = sl - eoff
     const int eoff = 23 + SEQSUM_FRAC_BITS - emax;
     // (2) exact fixed-point prefix
     long long loc = 0;
-    for (int i = i0; i < i1; ++i) loc += fixed(term(i));
-    long long Q = seqsum_exscan64(loc, s.wsum);
+#pragma unroll
+    for (int k = 0; k < SEQSUM_PER_MAX; ++k) loc += fixed(pv[k]);  // pv[k >= cnt] = 0
+    long long Q = seqsum_exscan64(loc, s.wsum[0]);
     // (3) heads, increments, ties
     int sl_prev = Q > 0 ? 63 - __clzll(Q) : -1;
     long long itot = 0;
-    for (int i = i0; i < i1; ++i) {
-        const float p = term(i);
-        const long long t = fixed(p);
-        Q += t;
+#pragma unroll
+    for (int k = 0; k < SEQSUM_PER_MAX; ++k) {
+        if (k >= cnt) break;
+        const int i = i0 + k;
+        const float p = pv[k];
+        Q += fixed(p);
         int inc = 0;
         if (Q == 0) {
             if (p != 0.0f) s.bad = 1;  // a non-zero term below the fixed-point resolution
@@ -164,10 +181,10 @@ __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, 
                     if (rem > half) {
                         ++inc;
                     } else if (rem == half) {
-                        const int k = atomicAdd(&s.ntie, 1);
-                        if (k < SEQSUM_TIES_MAX) {
-                            s.tie[k] = i;
-                            s.tslot[k] = sl;
+                        const int t = atomicAdd(&s.ntie, 1);
+                        if (t < SEQSUM_TIES_MAX) {
+                            s.tie[t] = i;
+                            s.tslot[t] = sl;
                         } else {
                             s.bad = 1;
                         }
@@ -180,8 +197,12 @@ __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, 
         itot += inc;
     }
     // (4) prefix of the increments: per-thread exclusive offsets in cpre
-    const long long ip = seqsum_exscan64(itot, s.wsum);
+    const long long ip = seqsum_exscan64(itot, s.wsum[1]);
     s.cpre[tid] = ip;
+    if (tid < SEQSUM_SLOTS) {
+        const unsigned int bal = __ballot_sync(0xffffffffu, s.head[tid] >= 0);
+        if (lane == 0) s.mask[warp] = bal;
+    }
     __syncthreads();
     auto incl = [&](int i) -> long long {  // inclusive prefix of incs at i
         const int owner = i / per;
@@ -190,18 +211,13 @@ __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, 
         return r;
     };
     const int nties = min(s.ntie, SEQSUM_TIES_MAX);
-    // (5a) per binade: increments from the head to the next head; the ties in index order
+    const unsigned long long mask = ((unsigned long long)s.mask[1] << 32) | s.mask[0];
+    // (5a) per binade: increments from the head to the next head; tie parities in index order
     if (tid < SEQSUM_SLOTS) {
         const int h = s.head[tid];
-        const unsigned int bal = __ballot_sync(0xffffffffu, h >= 0);
-        if (lane == 0) s.mask[warp] = bal;
         if (h >= 0) {
-            int hn = n;
-            for (int j = tid + 1; j < SEQSUM_SLOTS; ++j)
-                if (s.head[j] >= 0) {
-                    hn = s.head[j];
-                    break;
-                }
+            const unsigned long long above = tid < 63 ? mask & (~0ULL << (tid + 1)) : 0ULL;
+            const int hn = above ? s.head[__ffsll((long long)above) - 1] : n;
             s.tot[tid] = incl(hn - 1) - incl(h);
             s.phead[tid] = term(h);
         }
@@ -211,7 +227,6 @@ __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, 
         int r = 0;
         for (int j = 0; j < nties; ++j) r += s.tie[j] < i;
         const int sl = s.tslot[k];
-        s.stie[r] = i;
         s.sslot[r] = sl;
         s.sd[r] = (int)((incl(i) - incl(s.head[sl])) & 1);
     }
@@ -222,47 +237,74 @@ __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, 
         else atomicAdd(&s.x[sl], s.sd[r] ^ s.sd[r - 1]);
     }
     __syncthreads();
-    // (5b) the walk over the binades that have a head
-    if (tid == 0) {
+    // (5b) the walk: warp 0, binades in slot order, 32 at a time in lane registers
+    if (warp == 0) {
         bool ok = !s.bad;
-        unsigned long long m = ((unsigned long long)s.mask[1] << 32) | s.mask[0];
         float S = 0.0f;
+        unsigned long long m = mask;
         while (ok && m) {
-            const int sl = __ffsll((long long)m) - 1;
-            m &= m - 1;
-            const int e = sl - eoff;
-            S = S + s.phead[sl];
-            const unsigned int b = __float_as_uint(S);
-            if ((int)(b >> 23) - 127 != e || e < -126) {
-                ok = false;
-                break;
+            // lane j takes the j-th remaining binade
+            unsigned long long mm = m;
+            int mine = -1;
+            for (int j = 0; j < 32 && mm; ++j) {
+                const int sl = __ffsll((long long)mm) - 1;
+                mm &= mm - 1;
+                if (j == lane) mine = sl;
             }
-            long long Sb = (long long)((b & 0x7fffffu) | 0x800000u);  // S / u
-            const int d0 = s.d0[sl];
-            if (d0 >= 0) Sb += ((Sb + d0) & 1) + s.x[sl];
-            Sb += s.tot[sl];
-            if (Sb >= (1LL << 24)) {
-                ok = false;
-                break;
+            const int cnt = min(32, __popcll(m));
+            float ph = 0.0f;
+            long long tt = 0;
+            int dd = -1, xx = 0;
+            if (mine >= 0) {
+                ph = s.phead[mine];
+                tt = s.tot[mine];
+                dd = s.d0[mine];
+                xx = s.x[mine];
             }
-            S = __uint_as_float(((unsigned int)(e + 127) << 23) | ((unsigned int)Sb & 0x7fffffu));
+            for (int j = 0; j < cnt; ++j) {
+                const int sl = __shfl_sync(0xffffffffu, mine, j);
+                const float phj = __shfl_sync(0xffffffffu, ph, j);
+                const long long ttj = __shfl_sync(0xffffffffu, tt, j);
+                const int ddj = __shfl_sync(0xffffffffu, dd, j);
+                const int xxj = __shfl_sync(0xffffffffu, xx, j);
+                if (!ok) continue;
+                const int e = sl - eoff;
+                S = S + phj;
+                const unsigned int b = __float_as_uint(S);
+                if ((int)(b >> 23) - 127 != e || e < -126) {
+                    ok = false;
+                    continue;
+                }
+                long long Sb = (long long)((b & 0x7fffffu) | 0x800000u);  // S / u
+                if (ddj >= 0) Sb += ((Sb + ddj) & 1) + xxj;
+                Sb += ttj;
+                if (Sb >= (1LL << 24)) {
+                    ok = false;
+                    continue;
+                }
+                S = __uint_as_float(((unsigned int)(e + 127) << 23) | ((unsigned int)Sb & 0x7fffffu));
+            }
+            m = mm;
         }
-        if (!ok) {  // fallback: the reference's loop as is
-            S = 0.0f;
-            for (int i = 0; i < n; ++i) {
-                const float p = term(i);
-                S = S + p;
+        if (lane == 0) {
+            if (!ok) {  // fallback: the reference's loop as is
+                S = 0.0f;
+                for (int i = 0; i < n; ++i) {
+                    const float p = term(i);
+                    S = S + p;
+                }
             }
+            s.result = S;
         }
-        s.result = S;
     }
     __syncthreads();
     return s.result;
 }
 
 // The sum of squares of v[0..n) (RMSNorm, ops.cpp:830-836: glibc powf(x, 2) == x*x exactly).
-__device__ __forceinline__ float seq_sum_squares(const float* v, int n, SeqSumSmem& s, int* incs) {
-    return seq_sum_exact([v](int i) { return v[i] * v[i]; }, n, s, incs);
+__device__ __forceinline__ float seq_sum_squares(const float* v, int n, SeqSumSmem& s, int* incs,
+                                                 unsigned int maxbits = 0u) {
+    return seq_sum_exact([v](int i) { return v[i] * v[i]; }, n, s, incs, maxbits);
 }
 
 }  // namespace gtn
