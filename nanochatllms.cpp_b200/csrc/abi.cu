@@ -216,7 +216,7 @@ bool gemv_q_fits(int M, int wdt, int K) {
 // k_gemv3 plan for one activation row: rows per stage R = RP * passes (RP = rows covered by one
 // pass of 256 threads), as many passes (up to 16 rows) as keep two CTAs per SM.
 template <int WDT>
-static bool gv3_plan(const uint8_t* W, long ws, int K, int* R, int* RP) {
+static bool gv3_plan(const uint8_t* W, long ws, int N, int K, int* R, int* RP) {
     const int nb = K / GTN_QBLK;
     if (K % GTN_QBLK || nb % 4 || nb / 4 > GV3_THREADS || nb == 0) return false;
     if ((reinterpret_cast<uintptr_t>(W) & 15) || (ws & 15)) return false;
@@ -225,6 +225,8 @@ static bool gv3_plan(const uint8_t* W, long ws, int K, int* R, int* RP) {
         if (gv3_smem<WDT>(rp * passes, K) <= 110 * 1024) {
             *R = rp * passes;
             *RP = rp;
+            // few rows (e.g. 2048-2560): halve the group so that every SM gets two groups
+            if (passes == 1 && rp >= 16 && (N + rp - 1) / rp < 2 * sm_count()) *R = *RP = rp / 2;
             return true;
         }
     return false;
@@ -247,9 +249,9 @@ static cudaError_t launch_gv3(const uint8_t* X, const uint8_t* W, long ws, int N
 cudaError_t gemv_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
                    long ldy, cudaStream_t st, bool dry) {
     int R = 0, RP = 0;
-    if (M == 1 && wdt == GTN_Q8 && gv3_plan<GTN_Q8>(W, ws, K, &R, &RP))
+    if (M == 1 && wdt == GTN_Q8 && gv3_plan<GTN_Q8>(W, ws, N, K, &R, &RP))
         return launch_gv3<GTN_Q8>(X, W, ws, N, K, Y, R, RP, st, dry);
-    if (M == 1 && wdt == GTN_Q4 && gv3_plan<GTN_Q4>(W, ws, K, &R, &RP))
+    if (M == 1 && wdt == GTN_Q4 && gv3_plan<GTN_Q4>(W, ws, N, K, &R, &RP))
         return launch_gv3<GTN_Q4>(X, W, ws, N, K, Y, R, RP, st, dry);
     if (wdt == GTN_Q8) return gemv2<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, st, dry);
     return gemv2<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, st, dry);

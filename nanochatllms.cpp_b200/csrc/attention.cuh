@@ -351,7 +351,7 @@ __device__ __forceinline__ void att_softmax(float* p, int n, int last, float mx,
 __device__ __forceinline__ void att_core(const uint8_t* k, long ks, const uint8_t* v, long vs, int hb, int n, int last,
                                          int jp, const uint8_t* kspecial, const uint8_t* vspecial,
                                          const uint8_t* qraw, const AttSmem& sm, int dt, int d, float* red,
-                                         float* stat, unsigned int* err) {
+                                         float* stat, unsigned int* err, bool prefetched = false) {
     const int tid = threadIdx.x;
     const int T = att_tile(hb);
     const bool kb = att_bulk(k, ks, hb), vb = att_bulk(v, vs, hb);
@@ -361,8 +361,10 @@ __device__ __forceinline__ void att_core(const uint8_t* k, long ks, const uint8_
     const int n8 = (n / 8) * 8;
     uint32_t kpar = 0, vpar = 0;
     float mx = -INFINITY;
-    att_fetch(sm.kt, krs, k, ks, 0, max(0, min(min(T, n), last + 1)), hb, kb, &sm.bars[0]);
-    att_fetch(sm.vt, vrs, v, vs, 0, min(T, n8), hb, vb, &sm.bars[1]);
+    if (!prefetched) {  // else the caller issued exactly these two fetches (att_prefetch)
+        att_fetch(sm.kt, krs, k, ks, 0, max(0, min(min(T, n), last + 1)), hb, kb, &sm.bars[0]);
+        att_fetch(sm.vt, vrs, v, vs, 0, min(T, n8), hb, vb, &sm.bars[1]);
+    }
     for (int t0 = 0; t0 < n; t0 += T) {
         const int nt = min(T, n - t0);
         const int nv = max(0, min(nt, last + 1 - t0));
@@ -419,6 +421,16 @@ __device__ __forceinline__ void att_core(const uint8_t* k, long ks, const uint8_
             if (mbar_try_wait(&sm.bars[1], vpar ^ 1u)) break;
     }
     __syncthreads();
+}
+
+// The first K and V tile fetches of att_core, issued early (e.g. before a kernel waits for the
+// previous one: the cache rows below the new key do not depend on it).
+__device__ __forceinline__ void att_prefetch(const uint8_t* k, long ks, const uint8_t* v, long vs, int hb, int n,
+                                             int last, const AttSmem& sm) {
+    const int T = att_tile(hb), n8 = (n / 8) * 8;
+    const bool kb = att_bulk(k, ks, hb), vb = att_bulk(v, vs, hb);
+    att_fetch(sm.kt, kb ? (int)ks : att_rs(hb), k, ks, 0, max(0, min(min(T, n), last + 1)), hb, kb, &sm.bars[0]);
+    att_fetch(sm.vt, vb ? (int)vs : att_rs(hb), v, vs, 0, min(T, n8), hb, vb, &sm.bars[1]);
 }
 
 // Output row of one head: the lane partials summed left to right, then the tail keys n8..n-1

@@ -877,14 +877,21 @@ static __global__ void __launch_bounds__(ATT_THREADS) k_fattn(const AArgs a) {
     __shared__ float s_stat[2];
     __shared__ __align__(8) uint64_t bars[2];
     __shared__ int abort_flag;
-    att_init_bars(bars, &abort_flag);
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int h = blockIdx.x, b = blockIdx.y;
     const int group = a.q_heads / a.kv_heads, g = h / group;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int d = a.d, nbh = d / GTN_QBLK;
     const long hb = row_bytes(a.adt, d);
+    // The position was written by the previous step's last kernel, and the cache rows below it by
+    // earlier steps: both are complete before this kernel starts, so the first K/V tiles are
+    // fetched before waiting for the q/k/v projection (row p is replaced when the tiles land).
     const int p = a.pos[b], n = p + 1;
+    uint8_t* kc = a.kc + (long)b * a.seq_stride + (long)g * a.khs;
+    uint8_t* vc = a.vc + (long)b * a.seq_stride + (long)g * a.khs;
+    const AttSmem L = att_layout(sm, n, hb, d, bars, &abort_flag);
+    att_init_bars(bars, &abort_flag);
+    att_prefetch(kc, a.kvs, vc, a.kvs, (int)hb, n, p, L);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const float* yrow = a.y + (long)b * a.ys;
     const int qd = a.q_heads * d, kvd = a.kv_heads * d;
     const bool rope = a.half > 0;
@@ -917,18 +924,16 @@ static __global__ void __launch_bounds__(ATT_THREADS) k_fattn(const AArgs a) {
         requant(y, lane, GTN_QBLK, a.adt, hrow[t], k);
     }
     __syncthreads();
-    uint8_t* kc = a.kc + (long)b * a.seq_stride + (long)g * a.khs;
-    uint8_t* vc = a.vc + (long)b * a.seq_stride + (long)g * a.khs;
     if (h % group == 0) {
         for (int i = tid; i < hb; i += ATT_THREADS) {
             kc[(long)p * a.kvs + i] = hrow[1][i];
             vc[(long)p * a.kvs + i] = hrow[2][i];
         }
     }
-    const AttSmem L = att_layout(sm, n, hb, d, bars, &abort_flag);
     if (a.adt == GTN_Q8) build_prep_q8(hrow[0], 0, 0, 1, nbh, L.qp);
     __syncthreads();
-    att_core(kc, a.kvs, vc, a.kvs, (int)hb, n, p, p, hrow[1], hrow[2], hrow[0], L, a.adt, d, red, s_stat, a.err);
+    att_core(kc, a.kvs, vc, a.kvs, (int)hb, n, p, p, hrow[1], hrow[2], hrow[0], L, a.adt, d, red, s_stat, a.err,
+             true);
     asm volatile("griddepcontrol.launch_dependents;");
     att_out(L.part, L.p, vc, a.kvs, n, p, hrow[2], a.adt, d, a.out + (long)b * a.os + (long)h * hb);
 }
