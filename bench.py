@@ -144,11 +144,13 @@ def cpu_reference_sample(image, wdt: int, prompt, n_decode: int = 16):
     return tps, {"prefill_s": t_prefill, "decode_ms_per_token": t_dec * 1e3}
 
 
-def gemv_roofline(G, torch, wdt: int, device, hbm_peak: float):
+def gemv_roofline(G, torch, wdt: int, device, hbm_peak: float, only: str | None = None):
     """Live timing of the exact quantized GEMV on TinyLlama's weight shapes (M = 1)."""
     from gten_b200 import row_bytes
     shapes = [(2560, 2048, "qkv"), (2048, 2048, "o"), (11264, 2048, "gate_up"), (2048, 5632, "down"),
               (32003, 2048, "lm_head")]
+    if only:
+        shapes = [s for s in shapes if s[2] == only]
     out = {}
     dom = None
     stream = torch.cuda.current_stream()
@@ -186,7 +188,7 @@ def gemv_roofline(G, torch, wdt: int, device, hbm_peak: float):
         gbs = wb / t / 1e9
         out[name] = {"N": N, "K": K, "bytes": wb, "us": round(t * 1e6, 2), "GB_s": round(gbs, 1),
                      "frac": round(gbs / hbm_peak, 3)}
-        if name == "gate_up":
+        if name == "gate_up" or only:
             dom = out[name]
         del ws
     torch.cuda.empty_cache()
@@ -344,6 +346,8 @@ def main():
     ap.add_argument("--wdtype", type=int, default=3, choices=[1, 3, 4], help="1 fp16, 3 q8, 4 q4")
     ap.add_argument("--gemv-only", action="store_true",
                     help="only the exact GEMV sweep on TinyLlama's shapes (M=1), e.g. for profiling")
+    ap.add_argument("--gemv-shape", default=None, choices=["qkv", "o", "gate_up", "down", "lm_head"],
+                    help="with --gemv-only: one shape only")
     ap.add_argument("--decode-only", type=int, default=0, metavar="T",
                     help="only load the model and run one request of T generated tokens (for a launch list)")
     args = ap.parse_args()
@@ -366,7 +370,7 @@ def main():
 
         import gten_b200 as G
         hbm, _ = peaks()
-        _, sweep = gemv_roofline(G, torch, args.wdtype, torch.device("cuda", 0), hbm)
+        _, sweep = gemv_roofline(G, torch, args.wdtype, torch.device("cuda", 0), hbm, args.gemv_shape)
         print(json.dumps({"gemv_sweep": sweep, "wdtype": WDT_NAMES[args.wdtype]}), flush=True)
         return
     if args.impl == "reference":

@@ -478,7 +478,8 @@ __host__ __device__ inline int gv3_rstride(int K) {
 __host__ __device__ inline int gv3_pstr(int nb) { return ((nb + 7) & ~7) + 4; }
 template <int WDT>
 __host__ __device__ inline size_t gv3_smem(int R, int K) {
-    return 128 + (size_t)2 * R * gv3_rstride<WDT>(K) + (size_t)R * 4 * gv3_pstr(K / GTN_QBLK) * sizeof(float);
+    return 128 + (size_t)2 * R * gv3_rstride<WDT>(K) + (size_t)R * 4 * gv3_pstr(K / GTN_QBLK) * sizeof(float) +
+           (((size_t)(K / GTN_QBLK) * GTN_Q8_BYTES + 15) & ~(size_t)15);  // + the activation row
 }
 
 // Little-endian u16 at even byte offset o of a register-resident byte array (o folds at compile
@@ -533,23 +534,43 @@ __global__ void __launch_bounds__(GV3_THREADS, 2) k_gemv3(const uint8_t* __restr
         if (g0 + (int)gridDim.x < ngroups) issue(g0 + gridDim.x, 1), ++nissued1;
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // activation lane words of blocks 4j..4j+3 (same packing as build_prep_q8)
+    // the activation row into shared memory (coalesced), then this thread's lane words of blocks
+    // 4j..4j+3 (same packing as build_prep_q8) from four 34-byte blocks read as 8-byte words
+    uint8_t* xs = reinterpret_cast<uint8_t*>(prod + (size_t)R * 4 * pstr);
+    {
+        const int xbytes = nb * GTN_Q8_BYTES;
+        if ((reinterpret_cast<uintptr_t>(X) & 3) == 0) {
+            for (int i = tid; i < xbytes / 4; i += GV3_THREADS)
+                reinterpret_cast<uint32_t*>(xs)[i] = reinterpret_cast<const uint32_t*>(X)[i];
+            if (tid < (xbytes & 3)) xs[(xbytes & ~3) + tid] = X[(xbytes & ~3) + tid];
+        } else {
+            for (int i = tid; i < xbytes; i += GV3_THREADS) xs[i] = X[i];
+        }
+    }
+    __syncthreads();
     int a0[16], a1[16], asum[16];
     float da[4];
+    {
+        uint32_t xw[34];
+        const uint2* xsrc = reinterpret_cast<const uint2*>(xs + (size_t)j * 4 * GTN_Q8_BYTES);  // 8-byte aligned
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const uint8_t* xb = X + (size_t)(4 * j + k) * GTN_Q8_BYTES;
-        da[k] = p1 ? h2f(ld_u16(xb)) : 0.0f;
+        for (int q = 0; q < 17; ++q) {
+            const uint2 t = p1 ? xsrc[q] : make_uint2(0u, 0u);
+            xw[2 * q] = t.x;
+            xw[2 * q + 1] = t.y;
+        }
 #pragma unroll
-        for (int l = 0; l < 4; ++l) {
-            int w0 = 0, w1 = 0;
-            if (p1) {
-                w0 = (int)ld_u16(xb + 2 + 2 * l) | ((int)ld_u16(xb + 10 + 2 * l) << 16);
-                w1 = (int)ld_u16(xb + 18 + 2 * l) | ((int)ld_u16(xb + 26 + 2 * l) << 16);
+        for (int k = 0; k < 4; ++k) {
+            const int ob = k * GTN_Q8_BYTES;
+            da[k] = h2f((uint16_t)gv3_u16(xw, ob));
+#pragma unroll
+            for (int l = 0; l < 4; ++l) {
+                const int w0 = gv3_pair(xw, ob + 2 + 2 * l, ob + 10 + 2 * l);
+                const int w1 = gv3_pair(xw, ob + 18 + 2 * l, ob + 26 + 2 * l);
+                a0[k * 4 + l] = w0;
+                a1[k * 4 + l] = w1;
+                asum[k * 4 + l] = dp4a(w0, 0x01010101, dp4a(w1, 0x01010101, 0));
             }
-            a0[k * 4 + l] = w0;
-            a1[k * 4 + l] = w1;
-            asum[k * 4 + l] = dp4a(w0, 0x01010101, dp4a(w1, 0x01010101, 0));
         }
     }
     int it = 0;
