@@ -257,9 +257,43 @@ cudaError_t gemv_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, 
     return gemv2<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, st, dry);
 }
 
+// k_gemm3 plan: R rows per CTA (one pass of 256 threads over the 4-block groups), MT activation
+// rows per CTA, MC rows per product chunk, within 200 KB of shared memory.
+template <int WDT>
+static bool gm3_plan(const uint8_t* W, long ws, int M, int K, GM3Plan* p) {
+    const int nb = K / GTN_QBLK;
+    if (K % GTN_QBLK || nb % 4 || nb == 0 || nb / 4 > GV3_THREADS) return false;
+    if ((reinterpret_cast<uintptr_t>(W) & 15) || (ws & 15)) return false;
+    const int R = std::min(GV3_THREADS / (nb / 4), 64);
+    for (int mt = std::min(M, 16); mt >= 1; mt = mt > 1 ? mt / 2 : 0) {
+        for (int mc = std::min(mt, std::max(1, GV3_THREADS / (R * 4))); mc >= 1; --mc) {
+            if (gm3_smem<WDT>(R, mt, mc, K) <= 200 * 1024) {
+                p->R = R;
+                p->MT = mt;
+                p->MC = mc;
+                return true;
+            }
+        }
+    }
+    return false;
+}
+
+template <int WDT>
+static cudaError_t launch_gm3(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y,
+                              long ldy, const GM3Plan& p, cudaStream_t st) {
+    const size_t smem = gm3_smem<WDT>(p.R, p.MT, p.MC, K);
+    const cudaError_t e = ensure_smem(k_gemm3<WDT>, smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k_gemm3<WDT>, dim3((N + p.R - 1) / p.R, (M + p.MT - 1) / p.MT), dim3(GV3_THREADS), smem, st, W,
+                      ws, N, K, X, xs, M, Y, ldy, p.R, p.MT, p.MC, device_error_word());
+}
+
 static cudaError_t matmul_tma(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K,
                               float* Y, long ldy, cudaStream_t st) {
     if (gemv_q_fits(M, wdt, K)) return gemv_q(X, xs, M, W, ws, wdt, N, K, Y, ldy, st, false);
+    GM3Plan gp{};
+    if (wdt == GTN_Q8 && gm3_plan<GTN_Q8>(W, ws, M, K, &gp)) return launch_gm3<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, gp, st);
+    if (wdt == GTN_Q4 && gm3_plan<GTN_Q4>(W, ws, M, K, &gp)) return launch_gm3<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, gp, st);
     const int mt = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
     if (wdt == GTN_F16) {
         int nw = 4;

@@ -653,6 +653,157 @@ __global__ void __launch_bounds__(GV3_THREADS, 2) k_gemv3(const uint8_t* __restr
     }
 }
 
+// ---- exact GEMM for M >= 2 activation rows (prefill, batched decode) ----------------------------
+// The arithmetic and order of k_gemv3, for a tile of R weight rows x MT activation rows per CTA:
+// thread (row slot rs < R, block group j) keeps the weight bytes of blocks 4j..4j+3 of its row in
+// registers; the activation lane words of the MT rows are built once in shared memory; the rows
+// are processed MC at a time: phase 1 writes the 16 products per (activation row, thread) as four
+// float4, phase 2 runs the MC*R*4 lane chains in block order and the (L0+L1)+(L2+L3) combine.
+// The R weight rows arrive with one TMA bulk copy each (16-byte aligned rows). grid (ceil(N/R),
+// ceil(M/MT)); block 256.
+struct GM3Plan {
+    int R, MT, MC;
+};
+template <int WDT>
+__host__ __device__ inline size_t gm3_smem(int R, int MT, int MC, int K) {
+    const int nb = K / GTN_QBLK;
+    const size_t prep = (size_t)MT * nb * (4 * 8 + 4 + (WDT == GTN_Q4 ? 16 : 0));  // lane words, da, [sums]
+    return 128 + (size_t)R * gv3_rstride<WDT>(K) + ((prep + 15) & ~(size_t)15) +
+           (size_t)MC * R * 4 * gv3_pstr(nb) * sizeof(float);
+}
+
+template <int WDT>
+__global__ void __launch_bounds__(GV3_THREADS, 1) k_gemm3(const uint8_t* __restrict__ W, long w_stride, int N, int K,
+                                                         const uint8_t* __restrict__ X, long x_stride, int M,
+                                                         float* __restrict__ Y, long y_stride, int R, int MT, int MC,
+                                                         unsigned int* err) {
+    using C = MMCfg<WDT>;
+    constexpr int GB = 4 * C::BLK_BYTES, GW = GB / 4;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+    const int nb = K / GTN_QBLK, nbg = nb / 4;
+    const int rstride = gv3_rstride<WDT>(K), pstr = gv3_pstr(nb);
+    uint8_t* stage = smem + 128;
+    // activation lane words [MT][4 blocks k][4 lanes][nbg groups j] (block 4j+k): a warp's threads
+    // (consecutive j) read consecutive words; da [MT][4][nbg]; lane sums (Q4) like the words
+    int2* pa = reinterpret_cast<int2*>(stage + (size_t)R * rstride);
+    float* pda = reinterpret_cast<float*>(pa + (size_t)MT * nb * 4);
+    int* ps = reinterpret_cast<int*>(pda + (size_t)MT * nb);
+    const size_t prep = (size_t)MT * nb * (4 * 8 + 4 + (WDT == GTN_Q4 ? 16 : 0));
+    float* prod = reinterpret_cast<float*>(stage + (size_t)R * rstride + ((prep + 15) & ~(size_t)15));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int j = tid % nbg, rs = tid / nbg;
+    const int r0 = blockIdx.x * R, nr = min(R, N - r0);
+    const int m0 = blockIdx.y * MT, mt = min(MT, M - m0);
+    const bool p1 = rs < nr;
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(bar, (uint32_t)rstride * (uint32_t)nr);
+    }
+    __syncwarp();
+    if (warp == 0)
+        for (int r = lane; r < nr; r += 32)
+            bulk_g2s(stage + (size_t)r * rstride, W + (size_t)(r0 + r) * w_stride, (uint32_t)rstride, bar);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // activation lane words of the MT rows
+    for (int i = tid; i < mt * nb * 4; i += GV3_THREADS) {
+        const int l = i & 3, b = (i >> 2) % nb, m = (i >> 2) / nb;
+        const uint8_t* blk = X + (long)(m0 + m) * x_stride + (long)b * GTN_Q8_BYTES;
+        const uint8_t* q = blk + 2;
+        const int w0 = (int)ld_u16(q + 2 * l) | ((int)ld_u16(q + 8 + 2 * l) << 16);
+        const int w1 = (int)ld_u16(q + 16 + 2 * l) | ((int)ld_u16(q + 24 + 2 * l) << 16);
+        const int jj = b >> 2, k = b & 3;
+        const size_t o = ((size_t)(m * 4 + k) * 4 + l) * nbg + jj;
+        pa[o] = make_int2(w0, w1);
+        if (WDT == GTN_Q4) ps[o] = dp4a(w0, 0x01010101, dp4a(w1, 0x01010101, 0));
+        if (l == 0) pda[(size_t)(m * 4 + k) * nbg + jj] = h2f(ld_u16(blk));
+    }
+    const bool ok = __syncthreads_and(mbar_wait_bounded(bar, 0, err));
+    if (!ok) {  // the copy did not land in time: wait (bounded) for it before leaving
+        if (tid == 0)
+            for (uint32_t it = 0; it < GTN_WAIT_LIMIT; ++it)
+                if (mbar_try_wait(bar, 0)) break;
+        return;
+    }
+    uint32_t w[GW];
+    if (p1) {
+        const uint2* src = reinterpret_cast<const uint2*>(stage + (size_t)rs * rstride + (size_t)j * GB);
+#pragma unroll
+        for (int q = 0; q < GW / 2; ++q) {
+            const uint2 t = src[q];
+            w[2 * q] = t.x;
+            w[2 * q + 1] = t.y;
+        }
+    }
+    float dw[4];
+    int wl0[16], wl1[16];  // weight lane words per (block, lane)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int ob = k * C::BLK_BYTES;
+        dw[k] = p1 ? h2f((uint16_t)gv3_u16(w, ob)) : 0.0f;
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            if (WDT == GTN_Q8) {
+                wl0[k * 4 + l] = p1 ? gv3_pair(w, ob + 2 + 2 * l, ob + 10 + 2 * l) : 0;
+                wl1[k * 4 + l] = p1 ? gv3_pair(w, ob + 18 + 2 * l, ob + 26 + 2 * l) : 0;
+            } else {
+                const int wb = p1 ? gv3_pair(w, ob + 2 + 2 * l, ob + 10 + 2 * l) : 0;
+                wl0[k * 4 + l] = (wb >> 4) & 0x0f0f0f0f;
+                wl1[k * 4 + l] = wb & 0x0f0f0f0f;
+            }
+        }
+    }
+    const int nch = R * 4;  // chains per activation row
+    for (int c0 = 0; c0 < mt; c0 += MC) {
+        const int mc = min(MC, mt - c0);
+        if (p1) {
+            for (int mm = 0; mm < mc; ++mm) {
+                const int m = c0 + mm;
+                float o[4][4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float sc = pda[(size_t)(m * 4 + k) * nbg + j] * dw[k];
+#pragma unroll
+                    for (int l = 0; l < 4; ++l) {
+                        const size_t o2 = ((size_t)(m * 4 + k) * 4 + l) * nbg + j;
+                        const int2 av = pa[o2];
+                        int L = dp4a(wl0[k * 4 + l], av.x, dp4a(wl1[k * 4 + l], av.y, 0));
+                        if (WDT == GTN_Q4) L -= 7 * ps[o2];
+                        o[l][k] = (float)L * sc;
+                    }
+                }
+#pragma unroll
+                for (int l = 0; l < 4; ++l)
+                    *reinterpret_cast<float4*>(prod + ((size_t)(mm * R + rs) * 4 + l) * pstr + 4 * j) =
+                        make_float4(o[l][0], o[l][1], o[l][2], o[l][3]);
+            }
+        }
+        __syncthreads();
+        for (int cb = 0; cb < mc * nch; cb += GV3_THREADS) {  // whole warps: the combine shuffles
+            const int c = cb + tid;
+            const int mm = c / nch, rl = c - mm * nch, r = rl >> 2;
+            const bool valid = c < mc * nch && r < nr;
+            float acc = 0.0f;
+            if (valid) {
+                const float4* pp = reinterpret_cast<const float4*>(prod + (size_t)c * pstr);
+                for (int b4 = 0; b4 < nbg; ++b4) {
+                    const float4 v = pp[b4];
+                    acc = acc + v.x;
+                    acc = acc + v.y;
+                    acc = acc + v.z;
+                    acc = acc + v.w;
+                }
+            }
+            const float t01 = acc + __shfl_xor_sync(0xffffffffu, acc, 1);
+            const float t = t01 + __shfl_xor_sync(0xffffffffu, t01, 2);
+            if (valid && (c & 3) == 0) Y[(long)(m0 + c0 + mm) * y_stride + r0 + r] = t;
+        }
+        __syncthreads();
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+}
+
 // Plain-load variant for rows whose TMA tiles could reach outside the caller's weight buffer (an
 // unaligned base, or a last row that does not end on a 16-byte boundary). One warp per
 // (row, activation row): lanes 0..3 (Q8/Q4) or 0..7 (fp16) run the reference's lane chains with
