@@ -885,7 +885,7 @@ static __global__ void __launch_bounds__(ATT_THREADS) k_fattn(const AArgs a) {
     // The position was written by the previous step's last kernel, and the cache rows below it by
     // earlier steps: both are complete before this kernel starts, so the first K/V tiles are
     // fetched before waiting for the q/k/v projection (row p is replaced when the tiles land).
-    const int p = a.pos[b], n = p + 1;
+    const int p = __ldcg(a.pos + b), n = p + 1;  // L2 only: no L1 line of an earlier step
     uint8_t* kc = a.kc + (long)b * a.seq_stride + (long)g * a.khs;
     uint8_t* vc = a.vc + (long)b * a.seq_stride + (long)g * a.khs;
     const AttSmem L = att_layout(sm, n, hb, d, bars, &abort_flag);
