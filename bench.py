@@ -296,6 +296,76 @@ def run_ours(args, rank, world, local):
     return result
 
 
+BATCH_MODELS = {"tinyllama": ("TinyLlama-1.1B", 0), "minicpm": ("MiniCPM-2B", 2)}
+
+
+def run_batch(args, rank, world, local):
+    """--batch B: a global batch of B independent sequences sharded by sequence over the ranks
+    (gten_b200.shard): each rank decodes its shard with its own replica in one fused batched step;
+    value = B * generated tokens / (max over ranks of the device time of the shard); e2e = the same
+    through generate_sharded (host prompts, ids gathered to rank 0), wall clock."""
+    import numpy as np
+    import torch
+
+    import gten_b200 as G
+    from gten_b200 import gtenfile
+    from gten_b200.shard import generate_sharded, shard_range
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    name, kind = BATCH_MODELS[args.model]
+    n_prompt = 128 if args.model == "minicpm" else N_PROMPT
+    start, count = shard_range(args.batch, world, rank)
+    m = G.Model(kind, args.wdtype, n_prompt + N_GEN, max(1, count))
+    m.load(gtenfile.synthetic_image_device(kind, args.wdtype, SEED))
+    prompts = np.random.default_rng(42).integers(0, 32000, (args.batch, n_prompt)).astype(np.int32)
+    mine = prompts[start:start + count]
+    st = torch.cuda.ExternalStream(m.stream_ptr, device=device)
+    for _ in range(args.warmup):
+        if count:
+            m.generate_batch(mine, N_GEN)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = Clocks(local)
+    launches0 = G.kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        if count:
+            m.generate_batch(mine, N_GEN)
+    e1.record(st)
+    torch.cuda.synchronize()
+    launches = G.kernel_launches() - launches0
+    clk = clocks.stop()
+    t = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        out = generate_sharded(m, prompts, N_GEN) if world > 1 else m.generate_batch(prompts, N_GEN)
+    t_e2e = max_over_ranks(time.perf_counter() - t0, world)
+    m.close()
+    if rank != 0:
+        return None
+    tot = args.batch * N_GEN * args.steps
+    res = {
+        "metric": "decode tok/s", "value": round(tot / t, 2), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8-blocks/fp32-accum (Q8 weights, Q8 activations)" if args.wdtype == 3 else WDT_NAMES[args.wdtype],
+        "data": "synthetic: seeded N(0,0.02) weights (CUDA generator), uniform-random prompt ids",
+        "config": {"workload": f"{name} {WDT_NAMES[args.wdtype].upper()} batch {args.batch} sharded by sequence over "
+                               f"{world} GPU(s), {n_prompt}-token prompts + {N_GEN} greedy tokens",
+                   "model": args.model, "global_batch": args.batch, "seq_len": n_prompt + N_GEN,
+                   "parallelism": f"sequence shards x{world} (no collective on the data path)"},
+        "e2e": {"value": round(tot / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": args.batch * n_prompt * 4,
+                "d2h_bytes_per_step": args.batch * N_GEN * 4},
+        "gpu_launches": int(launches),
+        "first_ids": [int(x) for x in out[0, :4]],
+    }
+    if clk:
+        res["clocks"] = clk
+    return res
+
+
 def run_reference(args, rank, world):
     """The reference arm: the compiled reference CPU path on this host (rank 0 only)."""
     if rank != 0:
@@ -348,6 +418,9 @@ def main():
                     help="only the exact GEMV sweep on TinyLlama's shapes (M=1), e.g. for profiling")
     ap.add_argument("--gemv-shape", default=None, choices=["qkv", "o", "gate_up", "down", "lm_head"],
                     help="with --gemv-only: one shape only")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="global batch of sequences sharded over the ranks (default 1: the headline bs1 request)")
+    ap.add_argument("--model", default="tinyllama", choices=sorted(BATCH_MODELS), help="with --batch > 1")
     ap.add_argument("--decode-only", type=int, default=0, metavar="T",
                     help="only load the model and run one request of T generated tokens (for a launch list)")
     args = ap.parse_args()
@@ -379,7 +452,7 @@ def main():
         res = run_reference(args, rank, world)
     else:
         rank, world, local = dist_init()
-        res = run_ours(args, rank, world, local)
+        res = run_batch(args, rank, world, local) if args.batch > 1 else run_ours(args, rank, world, local)
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()

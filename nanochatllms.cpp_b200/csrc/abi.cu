@@ -280,12 +280,29 @@ static bool gm3_plan(const uint8_t* W, long ws, int M, int K, GM3Plan* p) {
 
 template <int WDT>
 static cudaError_t launch_gm3(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y,
-                              long ldy, const GM3Plan& p, cudaStream_t st) {
+                              long ldy, const GM3Plan& p, cudaStream_t st, bool dry = false) {
     const size_t smem = gm3_smem<WDT>(p.R, p.MT, p.MC, K);
     const cudaError_t e = ensure_smem(k_gemm3<WDT>, smem);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess || dry) return e;
     return launch_pdl(k_gemm3<WDT>, dim3((N + p.R - 1) / p.R, (M + p.MT - 1) / p.MT), dim3(GV3_THREADS), smem, st, W,
                       ws, N, K, X, xs, M, Y, ldy, p.R, p.MT, p.MC, device_error_word());
+}
+
+bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K) {
+    GM3Plan gp{};
+    if (wdt == GTN_Q8) return gm3_plan<GTN_Q8>(W, ws, M, K, &gp);
+    if (wdt == GTN_Q4) return gm3_plan<GTN_Q4>(W, ws, M, K, &gp);
+    return false;
+}
+
+cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
+                   long ldy, cudaStream_t st, bool dry) {
+    GM3Plan gp{};
+    if (wdt == GTN_Q8 && gm3_plan<GTN_Q8>(W, ws, M, K, &gp))
+        return launch_gm3<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, gp, st, dry);
+    if (wdt == GTN_Q4 && gm3_plan<GTN_Q4>(W, ws, M, K, &gp))
+        return launch_gm3<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, gp, st, dry);
+    return cudaErrorInvalidValue;
 }
 
 static cudaError_t matmul_tma(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K,

@@ -587,6 +587,10 @@ static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) 
         if (!dry) ++g_step_kernels;
         return gemv_q(g.xin, g.xin_s, g.B, g.W, g.ws, m->wdt, g.N, g.K, g.Y, g.ldy, m->st, dry);
     }
+    if (gemm_q_fits(g.W, g.ws, g.B, m->wdt, g.K)) {  // batches of 5 or more sequences
+        if (!dry) ++g_step_kernels;
+        return gemm_q(g.xin, g.xin_s, g.B, g.W, g.ws, m->wdt, g.N, g.K, g.Y, g.ldy, m->st, dry);
+    }
     if (m->wdt == GTN_Q8) return fg_mt<GTN_Q8, PRO_COPY>(g, m->st, dry);
     return fg_mt<GTN_Q4, PRO_COPY>(g, m->st, dry);
 }

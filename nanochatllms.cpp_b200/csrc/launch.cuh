@@ -91,6 +91,12 @@ bool gemv_q_fits(int M, int wdt, int K);
 cudaError_t gemv_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
                    long ldy, cudaStream_t st, bool dry);
 
+// Exact GEMM (k_gemm3) for M >= 2 activation rows of Q8 against Q8 or Q4 weights (16-byte aligned
+// weight rows, same `padded` precondition); `dry` only configures shared memory.
+bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K);
+cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
+                   long ldy, cudaStream_t st, bool dry);
+
 // Host table of (cos, sin) for positions [0, npos) and j < rd/2, as rotary_emb_impl computes them
 // (ops.cpp:791-812): theta = m * powf(10000, -((2j)/rd)), then cosf / sinf.
 std::vector<float2> rope_table_host(int npos, int rd);
