@@ -10,9 +10,11 @@ definition divides by the whole inference time, tinyllama.cpp:176-178).
   HBM; the 1.17 GB of weights are far larger than L2 (126 MB), so every step streams from HBM.
 * e2e: the same request through the public C ABI call gtn_model_generate with host buffers (prompt
   from pinned memory -> HBM, ids -> host) inside the timed region.
-* roofline: the dominant kernel, the exact Q8 GEMV (k_mm_q), timed live with CUDA events on the
-  launching stream over the model's weight shapes (rotating weight copies > L2 between launches);
-  achieved = weight bytes per launch / mean launch time.
+* roofline: the dominant kernel, the exact Q8 GEMV (k_gemv3), timed live with CUDA events on the
+  launching stream over the model's weight shapes (rotating weight copies > L2 between launches,
+  launches replayed from a CUDA graph); achieved = weight bytes per launch / mean launch time;
+  traffic = DRAM bytes read + written per launch of the same kernel and shape from one ncu capture
+  (profiles/k_gemv3_gate_up_q8.md).
 * cpu_baseline: the compiled reference (oracle/_ref/libgtenref.so) on this host's cores, a bounded
   sample (prefill + 16 decode steps) extrapolated to the 256-token request.
 * --impl reference: the reference arm, same config and metric, on rank 0.
@@ -33,6 +35,10 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "nanochatllms.cpp_b200"))
 
 N_PROMPT, N_GEN, SEED = 64, 256, 1234
+# dram__bytes_read.sum + dram__bytes_write.sum of one k_gemv3 launch on gate_up 11264x2048 (Q8), from
+# `ncu --set full --clock-control none -k regex:k_gemv3 -s 3 -c 1 python bench.py --gemv-only
+# --gemv-shape gate_up` (profiles/k_gemv3_gate_up_q8.md)
+GATE_UP_TRAFFIC_BYTES = 24_539_648
 WDT_NAMES = {3: "q8", 4: "q4", 1: "f16"}
 
 
@@ -283,10 +289,11 @@ def run_ours(args, rank, world, local):
                        "l2": "weights 1.17 GB > 126 MB L2; no flush needed"},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": N_PROMPT * 4,
                     "d2h_bytes_per_step": N_GEN * 4},
-            "roofline": {"bound": "hbm", "kernel": "k_mm_q (exact Q8 GEMV, gate_up 11264x2048)",
+            "roofline": {"bound": "hbm", "kernel": "k_gemv3 (exact Q8 GEMV, gate_up 11264x2048)",
                          "achieved": dom["GB_s"], "peak": hbm, "unit": "GB/s",
                          "frac": round(dom["GB_s"] / hbm, 3), "peak_kind": peak_kind,
-                         "traffic": None, "per_launch_bytes": dom["bytes"], "gemv_sweep": sweep},
+                         "traffic": GATE_UP_TRAFFIC_BYTES if wdt == 3 else None,
+                         "per_launch_bytes": dom["bytes"], "gemv_sweep": sweep},
             "gpu_launches": int(launches),
             "cpu_baseline": cpu,
         }
