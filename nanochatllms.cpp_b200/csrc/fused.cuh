@@ -581,34 +581,34 @@ static __global__ void __launch_bounds__(PCL_THREADS) k_prep_cl(const FArgs a, u
     cl.sync();  // B2
     if (exact && maxbits != 0u) {
         for (int r = 0; r < rank; ++r) Q += S.T[r];
-        // ---- heads, increments, ties, parities
+        // ---- heads, increments, ties, parities; at most PCL_PER elements per thread, kept in
+        // registers (a longer chunk takes the serial path)
+        constexpr int PCL_PER = 2;
         int sl_prev = Q > 0 ? 63 - __clzll(Q) : -1;
         int par = 0;  // parity of this thread's increments so far
-        int head_s[4], head_i[4], head_p[4], nh = 0;
-        float head_v[4];
-        int tie_i[4], tie_s[4], tie_p[4], nt = 0;
-        bool bad = maxbits >= 0x7f800000u;
-        for (int k = 0; k < per; ++k) {  // uniform trip count: the warp reductions below
+        int esl[PCL_PER], einc[PCL_PER], epar[PCL_PER];
+        bool ehead[PCL_PER], etie[PCL_PER];
+        float ep[PCL_PER];
+        bool bad = maxbits >= 0x7f800000u || per > PCL_PER;
+#pragma unroll
+        for (int k = 0; k < PCL_PER; ++k) {
             const int i = i0 + k;
-            const bool valid = i < i1;
-            const float p = valid ? sv[i] * sv[i] : 0.0f;
-            int inc = 0, sl = -1;
-            if (valid) {
+            esl[k] = -1;
+            einc[k] = 0;
+            epar[k] = par;
+            ehead[k] = false;
+            etie[k] = false;
+            ep[k] = 0.0f;
+            if (k < per && i < i1) {
+                const float p = sv[i] * sv[i];
                 Q += fixed(p);
                 if (Q == 0) {
                     if (p != 0.0f) bad = true;
                 } else {
-                    sl = 63 - __clzll(Q);
+                    const int sl = 63 - __clzll(Q);
+                    int inc = 0;
                     if (sl != sl_prev) {
-                        if (nh < 4) {
-                            head_s[nh] = sl;
-                            head_i[nh] = i;
-                            head_v[nh] = p;
-                            head_p[nh] = par;  // increments before the head (its own is 0)
-                            ++nh;
-                        } else {
-                            bad = true;
-                        }
+                        ehead[k] = true;  // the binade's first term: its own increment is 0
                     } else {
                         const int e = sl - eoff;
                         unsigned int M;
@@ -622,27 +622,24 @@ static __global__ void __launch_bounds__(PCL_THREADS) k_prep_cl(const FArgs a, u
                         } else if (sh < 32) {
                             inc = (int)(M >> sh);
                             const unsigned int rem = M & ((1u << sh) - 1u), half = 1u << (sh - 1);
-                            if (rem > half) {
-                                ++inc;
-                            } else if (rem == half) {
-                                if (nt < 4) {
-                                    tie_i[nt] = i;
-                                    tie_s[nt] = sl;
-                                    tie_p[nt] = par ^ (inc & 1);
-                                    ++nt;
-                                } else {
-                                    bad = true;
-                                }
-                            }
+                            if (rem > half) ++inc;
+                            else if (rem == half) etie[k] = true;
                         }
                     }
+                    esl[k] = sl;
+                    einc[k] = inc;
+                    ep[k] = p;
                     par ^= inc & 1;
                     sl_prev = sl;
                 }
             }
-            // per-binade totals: the lanes of one binade add up their increments, one atomic each
+        }
+        // per-binade totals: the lanes of one binade add up their increments, one atomic each
+#pragma unroll
+        for (int k = 0; k < PCL_PER; ++k) {
+            const int sl = esl[k];
             const unsigned int grp = __match_any_sync(0xffffffffu, sl);
-            const int gsum = __reduce_add_sync(grp, inc);
+            const int gsum = __reduce_add_sync(grp, einc[k]);
             if (sl >= 0 && lane == __ffs(grp) - 1 && gsum)
                 atomicAdd(reinterpret_cast<unsigned long long*>(&S.ltot[sl]), (unsigned long long)(long long)gsum);
         }
@@ -657,14 +654,22 @@ static __global__ void __launch_bounds__(PCL_THREADS) k_prep_cl(const FArgs a, u
             ctot ^= S.wpar[w];
         }
         const int pre = wpre ^ lane_pre;  // parity of the CTA's increments before this chunk
-        for (int k = 0; k < nt; ++k) {  // this CTA's ties with their CTA-local inclusive parity
-            const int q = atomicAdd(&S.lnt, 1);
-            if (q < PCL_TIES) {
-                S.lt[q] = tie_i[k];
-                S.lts[q] = tie_s[k];
-                S.ltp[q] = pre ^ tie_p[k];
-            } else {
-                bad = true;
+        // this CTA's ties with their CTA-local inclusive parity: one slot reservation per warp
+#pragma unroll
+        for (int k = 0; k < PCL_PER; ++k) {
+            const unsigned int tb = __ballot_sync(0xffffffffu, etie[k]);
+            int base = 0;
+            if (lane == 0 && tb) base = atomicAdd(&S.lnt, __popc(tb));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (etie[k]) {
+                const int q = base + __popc(tb & ((1u << lane) - 1u));
+                if (q < PCL_TIES) {
+                    S.lt[q] = i0 + k;
+                    S.lts[q] = esl[k];
+                    S.ltp[q] = pre ^ epar[k] ^ (einc[k] & 1);
+                } else {
+                    bad = true;
+                }
             }
         }
         __syncthreads();
@@ -672,10 +677,13 @@ static __global__ void __launch_bounds__(PCL_THREADS) k_prep_cl(const FArgs a, u
         // per-binade totals, ties, totals, failures
         for (int r = 0; r < PCL; ++r) {
             PclShared* D = cl.map_shared_rank(&S, r);
-            for (int k = 0; k < nh; ++k) {
-                D->head[head_s[k]] = head_i[k];
-                D->phead[head_s[k]] = head_v[k];
-                D->hpar[head_s[k]] = pre ^ head_p[k];
+#pragma unroll
+            for (int k = 0; k < PCL_PER; ++k) {
+                if (ehead[k]) {
+                    D->head[esl[k]] = i0 + k;
+                    D->phead[esl[k]] = ep[k];
+                    D->hpar[esl[k]] = pre ^ epar[k];
+                }
             }
             if (bad) D->bad = 1;
         }
@@ -720,7 +728,8 @@ static __global__ void __launch_bounds__(PCL_THREADS) k_prep_cl(const FArgs a, u
         const int nties = S.tbase[PCL];
         for (int k = tid; k < nties; k += PCL_THREADS) {
             int r = 0;
-            while (k >= S.tbase[r + 1]) ++r;
+#pragma unroll
+            for (int q = 1; q < PCL; ++q) r += k >= S.tbase[q];  // tbase is non-decreasing
             const int kk = k - S.tbase[r];
             const int i = S.tie[r][kk], sl = S.tslot[r][kk];
             int rk = S.tbase[r];  // rank among all ties: earlier CTAs, then this CTA's smaller indices
