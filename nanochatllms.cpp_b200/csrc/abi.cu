@@ -265,16 +265,18 @@ static bool gm3_plan(const uint8_t* W, long ws, int M, int K, GM3Plan* p) {
     if (K % GTN_QBLK || nb % 4 || nb == 0 || nb / 4 > GV3_THREADS) return false;
     if ((reinterpret_cast<uintptr_t>(W) & 15) || (ws & 15)) return false;
     const int R = std::min(GV3_THREADS / (nb / 4), 64);
-    for (int mt = std::min(M, 16); mt >= 1; mt = mt > 1 ? mt / 2 : 0) {
-        for (int mc = std::min(mt, std::max(1, GV3_THREADS / (R * 4))); mc >= 1; --mc) {
-            if (gm3_smem<WDT>(R, mt, mc, K) <= 200 * 1024) {
-                p->R = R;
-                p->MT = mt;
-                p->MC = mc;
-                return true;
+    // two CTAs per SM if a plan fits in 110 KB (registers allow two), else one
+    for (size_t lim : {(size_t)110 * 1024, (size_t)200 * 1024})
+        for (int mt = std::min(M, 16); mt >= 1; mt = mt > 1 ? mt / 2 : 0) {
+            for (int mc = std::min(mt, std::max(1, GV3_THREADS / (R * 4))); mc >= 1; --mc) {
+                if (gm3_smem<WDT>(R, mt, mc, K) <= lim && (mt <= 4 || mc >= 2 || lim > 110 * 1024)) {
+                    p->R = R;
+                    p->MT = mt;
+                    p->MC = mc;
+                    return true;
+                }
             }
         }
-    }
     return false;
 }
 

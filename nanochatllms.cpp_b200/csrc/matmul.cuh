@@ -673,7 +673,7 @@ __host__ __device__ inline size_t gm3_smem(int R, int MT, int MC, int K) {
 }
 
 template <int WDT>
-__global__ void __launch_bounds__(GV3_THREADS, 1) k_gemm3(const uint8_t* __restrict__ W, long w_stride, int N, int K,
+__global__ void __launch_bounds__(GV3_THREADS, 2) k_gemm3(const uint8_t* __restrict__ W, long w_stride, int N, int K,
                                                          const uint8_t* __restrict__ X, long x_stride, int M,
                                                          float* __restrict__ Y, long y_stride, int R, int MT, int MC,
                                                          unsigned int* err) {
@@ -706,10 +706,27 @@ __global__ void __launch_bounds__(GV3_THREADS, 1) k_gemm3(const uint8_t* __restr
         for (int r = lane; r < nr; r += 32)
             bulk_g2s(stage + (size_t)r * rstride, W + (size_t)(r0 + r) * w_stride, (uint32_t)rstride, bar);
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // activation lane words of the MT rows
+    // activation lane words of the MT rows; the raw rows are first copied with coalesced 4-byte
+    // loads into the (not yet used) product buffer when they fit there and are word aligned
+    const int xrow = nb * GTN_Q8_BYTES;
+    const bool stage_x = (size_t)mt * xrow <= (size_t)MC * R * 4 * pstr * sizeof(float) &&
+                         ((reinterpret_cast<uintptr_t>(X) | (uintptr_t)x_stride | (uintptr_t)xrow) & 3) == 0;
+    const uint8_t* xsrc = X + (long)m0 * x_stride;
+    long xss = x_stride;
+    if (stage_x) {
+        const int wpr = xrow / 4;
+        uint32_t* xd = reinterpret_cast<uint32_t*>(prod);
+        for (int i = tid; i < mt * wpr; i += GV3_THREADS) {
+            const int m = i / wpr, w = i - m * wpr;
+            xd[i] = reinterpret_cast<const uint32_t*>(xsrc + (long)m * x_stride)[w];
+        }
+        __syncthreads();
+        xsrc = reinterpret_cast<const uint8_t*>(prod);
+        xss = xrow;
+    }
     for (int i = tid; i < mt * nb * 4; i += GV3_THREADS) {
         const int l = i & 3, b = (i >> 2) % nb, m = (i >> 2) / nb;
-        const uint8_t* blk = X + (long)(m0 + m) * x_stride + (long)b * GTN_Q8_BYTES;
+        const uint8_t* blk = xsrc + (long)m * xss + (long)b * GTN_Q8_BYTES;
         const uint8_t* q = blk + 2;
         const int w0 = (int)ld_u16(q + 2 * l) | ((int)ld_u16(q + 8 + 2 * l) << 16);
         const int w1 = (int)ld_u16(q + 16 + 2 * l) | ((int)ld_u16(q + 24 + 2 * l) << 16);
