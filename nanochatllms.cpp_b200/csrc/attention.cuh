@@ -306,17 +306,18 @@ __device__ __forceinline__ void att_pv_tile(const uint8_t* vt, int rs, int t0, i
 // `red` holds ATT_THREADS / 32 floats, `stat` 2.
 __device__ __forceinline__ void att_softmax(float* p, int n, int last, float mx, int dt, float* red, float* stat) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // the maximum as an order-preserving unsigned key (NaN ranks lowest, as a '>' scan skips it):
+    // one warp max-reduction, then every thread combines the warps' keys
+    const unsigned int ub = __float_as_uint(mx);
+    unsigned int key = mx != mx ? 0u : ((ub & 0x80000000u) ? ~ub : (ub | 0x80000000u));
+    key = __reduce_max_sync(0xffffffffu, key);
+    unsigned int* redk = reinterpret_cast<unsigned int*>(red);
+    if (lane == 0) redk[warp] = key;
+    __syncthreads();
+    unsigned int mk = 0u;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();
-    if (tid == 0) {
-        float m = red[0];
-        for (int w = 1; w < ATT_THREADS / 32; ++w) m = fmaxf(m, red[w]);
-        stat[0] = m;
-    }
-    __syncthreads();
-    const float m = stat[0];
+    for (int w = 0; w < ATT_THREADS / 32; ++w) mk = max(mk, redk[w]);
+    const float m = __uint_as_float((mk & 0x80000000u) ? (mk ^ 0x80000000u) : ~mk);
     for (int j = tid; j < n; j += ATT_THREADS) p[j] = j <= last ? exp_cr(p[j] - m) : 0.0f;
     __syncthreads();
     if (tid == 0) {

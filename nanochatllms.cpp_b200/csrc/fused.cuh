@@ -900,10 +900,15 @@ static __global__ void __launch_bounds__(ATT_THREADS) k_fattn(const AArgs a) {
     const AttSmem L = att_layout(sm, n, hb, d, bars, &abort_flag);
     att_init_bars(bars, &abort_flag);
     att_prefetch(kc, a.kvs, vc, a.kvs, (int)hb, n, p, L);
+    const bool rope = a.half > 0;
+    float2 cs_first = make_float2(0.0f, 0.0f);  // this warp's first RoPE (cos, sin): a constant table
+    if (rope && warp < 2 * nbh) {
+        const int i = (warp % nbh) * GTN_QBLK + lane;
+        if (i < 2 * a.half) cs_first = a.cs[(long)p * a.half + (i < a.half ? i : i - a.half)];
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const float* yrow = a.y + (long)b * a.ys;
     const int qd = a.q_heads * d, kvd = a.kv_heads * d;
-    const bool rope = a.half > 0;
     // (1) Linear requant [+ bias requant], one warp per (tensor t, block k)
     for (int w = warp; w < 3 * nbh; w += ATT_THREADS / 32) {
         const int t = w / nbh, k = w - t * nbh, i = k * GTN_QBLK + lane;
@@ -921,11 +926,11 @@ static __global__ void __launch_bounds__(ATT_THREADS) k_fattn(const AArgs a) {
         if (rope && t < 2) {
             const float2* c = a.cs + (long)p * a.half;
             if (i < a.half) {
-                const float2 cs = c[i];
+                const float2 cs = w == warp ? cs_first : c[i];
                 const float p0 = tmp[t][i] * cs.x, p1 = tmp[t][i + a.half] * cs.y;
                 y = p0 - p1;
             } else if (i < 2 * a.half) {
-                const float2 cs = c[i - a.half];
+                const float2 cs = w == warp ? cs_first : c[i - a.half];
                 const float p2 = tmp[t][i - a.half] * cs.y, p3 = tmp[t][i] * cs.x;
                 y = p2 + p3;
             }
