@@ -132,6 +132,24 @@ int gtn_quantize_q8_rows(const float* x, int64_t rows, int64_t cols, void* out, 
  * device int32. */
 int gtn_argmax(const float* logits, int n, int32_t* out_index, void* stream);
 
+/* Seeded random number state for gtn_sample_topk: the Mersenne Twister MT19937 state of
+ * std::mt19937(seed), kept on the current device. Replaces sampler.cpp:70-71, where the generator is
+ * seeded from std::random_device (not reproducible). */
+typedef struct gtn_rng gtn_rng;
+int gtn_rng_create(uint32_t seed, gtn_rng** out);
+int gtn_rng_free(gtn_rng* rng);
+
+/* One top-k / temperature draw of topk_sample (sampler.cpp:63-128, the body of its loop after
+ * model->logits): logits/temp in double, the top_k largest (partial_sort), exp and their sum in
+ * double, the probabilities over the vocabulary, std::discrete_distribution (sum, normalize,
+ * partial sums, lower_bound of one generate_canonical<double> draw of two 32-bit outputs).
+ * top_k is clamped to 1000 and temp to 2.0 as the reference does; 1 <= top_k <= n, temp > 0.
+ * logits: device fp32 [n]; out_index: device int32. Advances rng by two outputs. Among logits
+ * equal to the k-th largest, the lowest indices are taken (the reference's heap selection may take
+ * others). */
+int gtn_sample_topk(const float* logits, int n, float temp, int top_k, gtn_rng* rng, int32_t* out_index,
+                    void* stream);
+
 /* ---- models (src/gten/abc.h:12-28 Model; src/tinyllama, zephyr, minicpm, openelm) -------- */
 
 typedef struct gtn_model gtn_model;

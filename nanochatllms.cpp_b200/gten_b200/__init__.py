@@ -64,6 +64,9 @@ def lib() -> C.CDLL:
         for name in ("gtn_pack_q8", "gtn_pack_q4", "gtn_quantize_q8_rows"):
             getattr(L, name).argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p]
         L.gtn_argmax.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
+        L.gtn_rng_create.argtypes = [C.c_uint32, C.POINTER(C.c_void_p)]
+        L.gtn_rng_free.argtypes = [C.c_void_p]
+        L.gtn_sample_topk.argtypes = [C.c_void_p, C.c_int, C.c_float, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
         _lib = L
     return _lib
 
@@ -214,6 +217,33 @@ def quantize_q8_rows(x, out, stream=None):
 
 def argmax(logits, out_index, stream=None):
     _check(lib().gtn_argmax(_ptr(logits), logits.numel(), _ptr(out_index), _stream(stream)), "argmax")
+
+
+class Rng:
+    """std::mt19937(seed) state on the current CUDA device, for sample_topk (the reference seeds from
+    std::random_device, sampler.cpp:70-71)."""
+
+    def __init__(self, seed: int):
+        self._h = C.c_void_p()
+        _check(lib().gtn_rng_create(C.c_uint32(seed & 0xFFFFFFFF), C.byref(self._h)), "rng_create")
+
+    def close(self):
+        if self._h:
+            lib().gtn_rng_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def sample_topk(logits, temp: float, top_k: int, rng: Rng, out_index, stream=None):
+    """One top-k / temperature draw of topk_sample (sampler.cpp:90-128) from device fp32 logits into
+    a device int32 tensor; advances rng."""
+    _check(lib().gtn_sample_topk(_ptr(logits), logits.numel(), C.c_float(temp), top_k, rng._h, _ptr(out_index),
+                                 _stream(stream)), "sample_topk")
 
 
 # ---- models (src/gten/abc.h) ----------------------------------------------------------------

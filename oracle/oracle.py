@@ -231,6 +231,24 @@ class Reference(_Lib):
         return out
 
 
+class SamplerOracle(_Lib):
+    """oracle/sampler_oracle.cpp: the reference's top-k sampling step with std::mt19937(seed)."""
+
+    def __init__(self, path: str | None = None):
+        super().__init__(path or os.path.join(HERE, "_build", "libsampleroracle.so"))
+        self.lib.or_topk_sample.argtypes = [C.c_void_p, C.c_int, C.c_float, C.c_int, C.c_uint32, C.c_int,
+                                            C.c_void_p]
+
+    def topk_sample(self, logits: np.ndarray, temp: float, top_k: int, seed: int) -> np.ndarray:
+        """logits [draws, n] fp32: one draw per row, one generator for all rows."""
+        x = np.ascontiguousarray(np.atleast_2d(logits), np.float32)
+        out = np.zeros(x.shape[0], np.int32)
+        rc = self.lib.or_topk_sample(_p(x), x.shape[1], C.c_float(temp), top_k, C.c_uint32(seed), x.shape[0], _p(out))
+        if rc != 0:
+            raise ValueError("or_topk_sample: bad arguments")
+        return out
+
+
 class ReferenceModel:
     def __init__(self, ref: Reference, kind: int, wdt: int, n_ctx: int, path: str, n_vocab: int):
         self.r = ref
