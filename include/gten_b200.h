@@ -144,7 +144,8 @@ int gtn_rng_free(gtn_rng* rng);
  * double, the probabilities over the vocabulary, std::discrete_distribution (sum, normalize,
  * partial sums, lower_bound of one generate_canonical<double> draw of two 32-bit outputs).
  * top_k is clamped to 1000 and temp to 2.0 as the reference does; 1 <= top_k <= n, temp > 0.
- * logits: device fp32 [n]; out_index: device int32. Advances rng by two outputs. Among logits
+ * logits: device fp32 [n]; out_index: device int32. Advances rng by two outputs (none when n = 1);
+ * rng must live on the current device. Among logits
  * equal to the k-th largest, the lowest indices are taken (the reference's heap selection may take
  * others). */
 int gtn_sample_topk(const float* logits, int n, float temp, int top_k, gtn_rng* rng, int32_t* out_index,
@@ -187,6 +188,13 @@ int gtn_model_logits(gtn_model* m, const int32_t* tokens, int n_tokens, int star
  * prompt (host int32), then n_gen greedy steps; out_tokens (host) receives the n_gen ids.
  * Synchronous. */
 int gtn_model_generate(gtn_model* m, const int32_t* prompt, int n_prompt, int n_gen, int32_t* out_tokens);
+
+/* topk_sample (sampler.cpp:63-143) without tokenization and without the EOS stop: prefill the
+ * prompt, then n_gen steps, each drawing its id as gtn_sample_topk does (same clamps and argument
+ * rules) with the caller's seeded generator, which advances by two outputs per step. The draw runs
+ * on the device inside the decode step. Synchronous; rng must live on the current device. */
+int gtn_model_generate_topk(gtn_model* m, const int32_t* prompt, int n_prompt, int n_gen, float temp, int top_k,
+                            gtn_rng* rng, int32_t* out_tokens);
 
 /* greedy_sample for `batch` independent sequences (the reference has no batching: each sequence
  * gives exactly the ids it would give alone). prompts: host [batch][n_prompt]; out_tokens: host

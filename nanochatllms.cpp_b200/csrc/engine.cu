@@ -70,6 +70,13 @@ struct gtn_model {
     cudaGraphExec_t graph = nullptr;
     int graph_B = 0;
     long graph_kernels = 0;
+    // top-k sampling of gtn_model_generate_topk (s_mt null: greedy); the captured step is keyed on it
+    uint32_t* s_mt = nullptr;
+    float s_temp = 1.0f;
+    int s_topk = 1;
+    uint32_t* graph_mt = nullptr;
+    float graph_temp = 0.0f;
+    int graph_topk = 0;
     int* pos_host = nullptr;  // pinned staging for position uploads
 };
 
@@ -598,6 +605,17 @@ static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) 
 // One greedy decode step for sequences 0..B-1 at positions m->pos[b] (their input tokens are at
 // m->tok[b*max_ctx + pos[b]]): the reference's block sequence (tinyllama.cpp:99-104 and the
 // siblings) as five kernels per layer, then the lm_head GEMV and the greedy pick.
+// The decode loop's bookkeeping for a sampled id of sequence 0 (as k_fargmax does for greedy ids).
+static SampleDst sample_dst(gtn_model* m, unsigned int* err) {
+    SampleDst sd;
+    sd.tok = m->tok;
+    sd.gen = m->gen;
+    sd.pos = m->pos;
+    sd.max_ctx = m->max_ctx + 1;
+    sd.err = err;
+    return sd;
+}
+
 static int decode_step(gtn_model* m, int B, bool dry) {
     cudaStream_t st = m->st;
     const int adt = m->adt, d = m->d, dh = m->dh;
@@ -670,10 +688,15 @@ static int decode_step(gtn_model* m, int B, bool dry) {
     hd.nw = m->nfw; hd.nb = m->nfb; hd.layer = m->family == 1; hd.post = cpm; hd.ps = 1.0f / 9;
     hd.W = m->lm_head; hd.ws = m->emb_rs; hd.N = m->n_vocab; hd.Y = m->logits; hd.ldy = m->n_vocab;
     SK(fgemv(m, hd, PRO_RESNORM, dry));
-    if (!dry) {
+    if (dry) {
+        SK(prepare_topk_sample(m->n_vocab));
+    } else {
         ++g_step_kernels;
-        SK(launch_pdl(k_fargmax, dim3(B), dim3(1024), 0, st, (const float*)m->logits, (long)m->n_vocab, m->n_vocab,
-                      m->tok, m->gen, (long)m->max_ctx + 1, m->pos, m->max_ctx + 1, err));
+        if (m->s_mt)
+            SK(launch_topk_sample(st, m->logits, m->n_vocab, m->s_temp, m->s_topk, m->s_mt, sample_dst(m, err)));
+        else
+            SK(launch_pdl(k_fargmax, dim3(B), dim3(1024), 0, st, (const float*)m->logits, (long)m->n_vocab,
+                          m->n_vocab, m->tok, m->gen, (long)m->max_ctx + 1, m->pos, m->max_ctx + 1, err));
     }
 #undef SK
     return GTN_OK;
@@ -681,7 +704,8 @@ static int decode_step(gtn_model* m, int B, bool dry) {
 
 // Captures decode_step(B) into a CUDA graph (once per B) and launches it.
 static int run_step(gtn_model* m, int B) {
-    if (!m->graph || m->graph_B != B) {
+    if (!m->graph || m->graph_B != B || m->graph_mt != m->s_mt || m->graph_temp != m->s_temp ||
+        m->graph_topk != m->s_topk) {
         if (m->graph) {
             cudaGraphExecDestroy(m->graph);
             m->graph = nullptr;
@@ -702,6 +726,9 @@ static int run_step(gtn_model* m, int B) {
         cudaGraphDestroy(g);
         ECHK(ei, "graph instantiate");
         m->graph_B = B;
+        m->graph_mt = m->s_mt;
+        m->graph_temp = m->s_temp;
+        m->graph_topk = m->s_topk;
         m->graph_kernels = g_step_kernels;
     }
     ECHK(cudaGraphLaunch(m->graph, m->st), "graph launch");
@@ -728,10 +755,16 @@ static int generate_fused(gtn_model* m, int B, int n_prompt, int n_gen) {
     }
     int rc = set_positions(m, B, n_prompt - 1);
     if (rc != GTN_OK) return rc;
-    count_launch();
-    ECHK(launch_pdl(k_fargmax, dim3(B), dim3(1024), 0, m->st, (const float*)m->logits, (long)m->n_vocab, m->n_vocab,
-                    m->tok, m->gen, (long)m->max_ctx + 1, m->pos, m->max_ctx + 1, device_error_word()),
-         "first token");
+    if (m->s_mt) {
+        ECHK(launch_topk_sample(m->st, m->logits, m->n_vocab, m->s_temp, m->s_topk, m->s_mt,
+                                sample_dst(m, device_error_word())),
+             "first token");
+    } else {
+        ECHK(launch_pdl(k_fargmax, dim3(B), dim3(1024), 0, m->st, (const float*)m->logits, (long)m->n_vocab,
+                        m->n_vocab, m->tok, m->gen, (long)m->max_ctx + 1, m->pos, m->max_ctx + 1,
+                        device_error_word()),
+             "first token");
+    }
     for (int i = 1; i < n_gen; ++i) {
         rc = run_step(m, B);
         if (rc != GTN_OK) return rc;
@@ -753,6 +786,11 @@ static int generate_dev(gtn_model* m, int n_prompt, int n_gen, int32_t* out) {
     for (int i = 0; i < n_gen; ++i) {
         const int rc = forward(m, 0, n, i == 0 ? 0 : n - 1);
         if (rc != GTN_OK) return rc;
+        if (m->s_mt) {  // the sampled id replaces the argmax in m->next
+            SampleDst sd;
+            sd.out = m->next;
+            ECHK(launch_topk_sample(m->st, m->logits, m->n_vocab, m->s_temp, m->s_topk, m->s_mt, sd), "sample");
+        }
         if (i + 1 < n_gen)
             ECHK(cudaMemcpyAsync(m->tok + n, m->next, sizeof(int32_t), cudaMemcpyDeviceToDevice, m->st), "next");
         ECHK(cudaMemcpyAsync(out + i, m->next, sizeof(int32_t), cudaMemcpyDeviceToDevice, m->st), "out");
@@ -800,6 +838,26 @@ int gtn_model_generate(gtn_model* m, const int32_t* prompt, int n_prompt, int n_
     }
     ECHK(cudaStreamSynchronize(m->st), "model_generate");
     return check_dev_err();
+}
+
+int gtn_model_generate_topk(gtn_model* m, const int32_t* prompt, int n_prompt, int n_gen, float temp, int top_k,
+                            gtn_rng* rng, int32_t* out_tokens) {
+    if (!m || !m->loaded || !rng) return fail(GTN_ERR_ARG, "model_generate_topk: arguments");
+    int dev = -1;
+    cudaGetDevice(&dev);
+    if (dev != rng->device)
+        return fail(GTN_ERR_ARG, "model_generate_topk: rng lives on device %d, current device %d", rng->device, dev);
+    if (!(temp > 0.0f)) return fail(GTN_ERR_ARG, "model_generate_topk: temp must be > 0");
+    top_k = top_k < 1000 ? top_k : 1000;  // sampler.cpp:66-67
+    temp = temp < 2.0f ? temp : 2.0f;
+    if (top_k < 1 || top_k > m->n_vocab)
+        return fail(GTN_ERR_ARG, "model_generate_topk: top_k %d outside [1, %d]", top_k, m->n_vocab);
+    m->s_mt = rng->state;
+    m->s_temp = temp;
+    m->s_topk = top_k;
+    const int rc = gtn_model_generate(m, prompt, n_prompt, n_gen, out_tokens);
+    m->s_mt = nullptr;
+    return rc;
 }
 
 int gtn_model_generate_batch(gtn_model* m, const int32_t* prompts, int batch, int n_prompt, int n_gen,

@@ -10,6 +10,12 @@
 #include "matmul.cuh"
 #include "rowops.cuh"
 
+// Seeded generator state of gtn_sample_topk (std::mt19937 restated on the device).
+struct gtn_rng {
+    uint32_t* state = nullptr;  // device: 624 words, then the index of the next output
+    int device = 0;
+};
+
 namespace gtn {
 
 void set_error(const std::string& msg);
@@ -69,6 +75,25 @@ inline cudaError_t ensure_smem(K kern, size_t smem) {
     if (!smem_attr_needed(reinterpret_cast<const void*>(kern), smem)) return cudaSuccess;
     return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
+
+// Destination of one top-k draw (csrc/sample.cu): `out[0]` when out is set; when tok is set, the
+// decode loop's bookkeeping of k_fargmax (the id becomes token pos[0] + 1 of tok and gen, pos[0]
+// advances; at the end of the token rows bit 4 of *err is set instead).
+struct SampleDst {
+    int32_t* out = nullptr;
+    int32_t* tok = nullptr;
+    int32_t* gen = nullptr;
+    int* pos = nullptr;
+    int max_ctx = 0;
+    unsigned int* err = nullptr;
+};
+
+// One top-k / temperature draw from n fp32 logits with the MT19937 state `mt` (k and temp already
+// clamped and checked). Launched with programmatic dependent launch; counts one launch.
+cudaError_t launch_topk_sample(cudaStream_t st, const float* logits, int n, float temp, int k, uint32_t* mt,
+                               SampleDst dst);
+// Sets the sampler's shared memory limit for n logits (outside stream capture; idempotent).
+cudaError_t prepare_topk_sample(int n);
 
 // Device error word written by kernels whose bounded waits expired (GTN_DEVERR_*).
 unsigned int* device_error_word();

@@ -67,6 +67,8 @@ def lib() -> C.CDLL:
         L.gtn_rng_create.argtypes = [C.c_uint32, C.POINTER(C.c_void_p)]
         L.gtn_rng_free.argtypes = [C.c_void_p]
         L.gtn_sample_topk.argtypes = [C.c_void_p, C.c_int, C.c_float, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+        L.gtn_model_generate_topk.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_int,
+                                              C.c_void_p, C.c_void_p]
         _lib = L
     return _lib
 
@@ -281,6 +283,15 @@ class Model:
         p = np.ascontiguousarray(prompt, np.int32)
         out = np.zeros(n_gen, np.int32)
         _check(lib().gtn_model_generate(self._h, p.ctypes.data, p.size, n_gen, out.ctypes.data), "model_generate")
+        return out
+
+    def generate_topk(self, prompt, n_gen: int, temp: float, top_k: int, rng: "Rng"):
+        """topk_sample (sampler.cpp:63-143) without tokenization: n_gen ids drawn with rng."""
+        import numpy as np
+        p = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(n_gen, np.int32)
+        _check(lib().gtn_model_generate_topk(self._h, p.ctypes.data, p.size, n_gen, C.c_float(temp), top_k, rng._h,
+                                             out.ctypes.data), "model_generate_topk")
         return out
 
     def generate_batch(self, prompts, n_gen: int):

@@ -248,6 +248,33 @@ class SamplerOracle(_Lib):
             raise ValueError("or_topk_sample: bad arguments")
         return out
 
+    def generator(self, seed: int) -> "OracleSampler":
+        return OracleSampler(self, seed)
+
+
+class OracleSampler:
+    """One std::mt19937(seed) that persists across topk_sample steps (a decode loop)."""
+
+    def __init__(self, so: SamplerOracle, seed: int):
+        self.lib = so.lib
+        self.lib.or_sampler_new.restype = C.c_void_p
+        self.lib.or_sampler_new.argtypes = [C.c_uint32]
+        self.lib.or_sampler_step.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_int]
+        self.lib.or_sampler_free.argtypes = [C.c_void_p]
+        self.h = self.lib.or_sampler_new(C.c_uint32(seed))
+
+    def step(self, logits: np.ndarray, temp: float, top_k: int) -> int:
+        x = np.ascontiguousarray(logits, np.float32).ravel()
+        r = self.lib.or_sampler_step(self.h, _p(x), x.size, C.c_float(temp), top_k)
+        if r < 0:
+            raise ValueError("or_sampler_step: bad arguments")
+        return int(r)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.lib.or_sampler_free(self.h)
+            self.h = None
+
 
 class ReferenceModel:
     def __init__(self, ref: Reference, kind: int, wdt: int, n_ctx: int, path: str, n_vocab: int):

@@ -11,8 +11,14 @@ where the reference checkout exists; the GPU box only reads the outputs).
   the oracle's packer, which pack.npz pins to the reference packer), a seeded 64-token prompt and
   the first 64 greedy token ids of the compiled reference (ref_model_greedy = sampler.cpp:11-53
   without the EOS stop), with each step's top-2 logit margin.
+* sampled_tokens.json: the same TinyLlama Q8 model and prompt decoded by the reference's top-k loop
+  (sampler.cpp:63-143 without tokenization or the EOS stop): each step's logits from the compiled
+  reference's Model::logits, each draw by oracle/sampler_oracle.cpp (the loop body with the same
+  libstdc++ calls) from one std::mt19937(seed) in place of std::random_device; with each step's gap
+  between the k-th and (k+1)-th largest logit (a tie there would make the pick library-specific).
 
 Usage: python tests/golden/make_golden.py [reference_dir]
+       python tests/golden/make_golden.py --sampled     (sampled_tokens.json only)
 """
 import io
 import json
@@ -26,7 +32,7 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "nanochatllms.cpp_b200"))
 
-from oracle.oracle import F16, F32, Q4, Q8, Oracle, Reference, ReferenceModel, row_bytes  # noqa: E402
+from oracle.oracle import F16, F32, Q4, Q8, Oracle, Reference, ReferenceModel, SamplerOracle, row_bytes  # noqa: E402
 
 
 def reference_packer(ref_dir):
@@ -139,5 +145,42 @@ def main():
         json.dump(gold, f)
 
 
+def sampled():
+    from gten_b200 import gtenfile
+    orc, ref = Oracle(), Reference()
+
+    def pack(wt, dt):
+        return orc.pack_q8(wt.numpy()) if dt == Q8 else orc.pack_q4(wt.numpy())
+
+    gold = {}
+    for wdt, temp, top_k, rng_seed in ((Q8, 0.9, 40, 20240607), (Q4, 1.7, 200, 7)):
+        seed, n_ctx, n_gen = 1234, 128, 48
+        img = gtenfile.synthetic_image(0, wdt, seed, pack)
+        path = f"/tmp/golden_tinyllama_sampled_{wdt}.gten"
+        img.tofile(path)
+        prompt = np.random.default_rng(42).integers(0, 32000, 64).astype(np.int32)
+        rm = ReferenceModel(ref, 0, wdt, n_ctx, path, 32003)
+        gen = SamplerOracle().generator(rng_seed)
+        toks, out, gaps = list(prompt), [], []
+        for i in range(n_gen):
+            lg = rm.logits(np.array(toks, np.int32), 0 if i == 0 else len(toks) - 1)
+            top = np.sort(lg)[::-1]
+            gaps.append(float(top[min(top_k, 1000) - 1] - top[min(top_k, 1000)]))
+            t = gen.step(lg, temp, top_k)
+            out.append(t)
+            toks.append(t)
+        del rm
+        os.remove(path)
+        gold[f"tinyllama_w{wdt}"] = {"seed": seed, "n_ctx": n_ctx, "prompt": prompt.tolist(), "temp": temp,
+                                     "top_k": top_k, "rng_seed": rng_seed, "tokens": out, "kth_gaps": gaps}
+        print(wdt, out[:16], "min k-th gap", min(gaps))
+    with open(os.path.join(HERE, "sampled_tokens.json"), "w") as f:
+        json.dump(gold, f)
+
+
 if __name__ == "__main__":
-    main()
+    if "--sampled" in sys.argv:
+        sampled()
+    else:
+        main()
+        sampled()

@@ -110,3 +110,69 @@ def test_tinyllama_greedy_matches_reference(orc, gpu, wdt):
     got = m.generate(prompt, len(case["tokens"]))
     assert got.tolist() == case["tokens"]
     m.close()
+
+
+def _oracle_topk_loop(om, sampler, prompt, n_gen, temp, top_k):
+    """topk_sample's loop (sampler.cpp:80-139) over the oracle model: logits of the whole prompt,
+    then of each new token; asserts no tie across the k-th place (a tie makes the pick
+    library-specific)."""
+    toks, out = [int(t) for t in prompt], []
+    k = min(top_k, 1000)
+    for i in range(n_gen):
+        lg = om.logits(np.array(toks, np.int32), 0 if i == 0 else len(toks) - 1)
+        top = np.sort(lg)[::-1]
+        assert k == lg.size or top[k - 1] != top[k], f"tie across the k-th place at step {i}"
+        t = sampler.step(lg, temp, top_k)
+        out.append(t)
+        toks.append(t)
+    return out
+
+
+@pytest.mark.parametrize("name", list(CUSTOM))
+@pytest.mark.parametrize("wdt", [Q8, Q4, F16])
+def test_topk_generation_matches_oracle(orc, gpu, name, wdt):
+    """gtn_model_generate_topk draws inside the decode step; the ids must equal the oracle model's
+    logits followed by the reference's sampling step with the same seeded std::mt19937."""
+    from oracle.oracle import OracleModel, SamplerOracle
+    dims = CUSTOM[name]
+    img = gtenfile.synthetic_image(6, wdt, 31, cpu_pack(orc), dims=dims, std=0.05, gain_std=0.1)
+    n_prompt, n_gen, temp, top_k, seed = 9, 14, 0.8, 40, 2024 + wdt
+    max_ctx = 2 * (n_prompt + n_gen)
+    prompt = np.random.default_rng(17).integers(0, dims[0], n_prompt).astype(np.int32)
+    want = _oracle_topk_loop(OracleModel(orc, 6, wdt, max_ctx, img, dims=dims), SamplerOracle().generator(seed),
+                             prompt, n_gen, temp, top_k)
+    m = G.Model(G.CUSTOM, wdt, max_ctx, dims=dims)
+    m.load(img)
+    r = G.Rng(seed)
+    assert m.generate_topk(prompt, n_gen, temp, top_k, r).tolist() == want
+    # greedy afterwards rebuilds the captured step without the sampler
+    assert np.array_equal(m.generate(prompt, 5), OracleModel(orc, 6, wdt, max_ctx, img, dims=dims).greedy(prompt, 5))
+    # top_k = 1 is greedy, through the sampler
+    assert np.array_equal(m.generate_topk(prompt, 5, 1.0, 1, r), m.generate(prompt, 5))
+    with pytest.raises(G.GtenError, match="status 1"):
+        m.generate_topk(prompt, 2, 0.0, 5, r)
+    with pytest.raises(G.GtenError, match="status 1"):
+        m.generate_topk(prompt, 2, 1.0, 0, r)
+    r.close()
+    m.close()
+
+
+SAMPLED = os.path.join(HERE, "golden", "sampled_tokens.json")
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("wdt", [Q8, Q4])
+def test_tinyllama_topk_matches_reference(orc, gpu, wdt):
+    """Full-size TinyLlama, seeded weights and prompt as the greedy golden case, 48 top-k draws
+    (Q8: temp 0.9, top_k 40; Q4: temp 1.7, top_k 200) from one seeded std::mt19937: the ids must equal
+    tests/golden/sampled_tokens.json (compiled reference logits + the reference's sampling step)."""
+    with open(SAMPLED) as f:
+        case = json.load(f)[f"tinyllama_w{wdt}"]
+    img = gtenfile.synthetic_image(0, wdt, case["seed"], gtenfile.cuda_packer())
+    m = G.Model(G.TINYLLAMA, wdt, case["n_ctx"])
+    m.load(img)
+    r = G.Rng(case["rng_seed"])
+    got = m.generate_topk(np.array(case["prompt"], np.int32), len(case["tokens"]), case["temp"], case["top_k"], r)
+    assert got.tolist() == case["tokens"]
+    r.close()
+    m.close()
