@@ -567,11 +567,10 @@ static cudaError_t fg_mt(const FArgs& a, cudaStream_t st, bool dry) {
 static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) {
     FArgs g = a;
     if (pro != PRO_COPY) {
-        const size_t smem = pro == PRO_RESNORM ? 2 * sizeof(float) * (size_t)a.K : 0;  // values + sum scratch
         cudaError_t e;
         if (pro == PRO_RESNORM) {
-            // one cluster of PCL CTAs per sequence (values in K floats of dynamic shared memory)
-            const size_t csmem = sizeof(float) * (size_t)a.K;
+            // one cluster of PCL CTAs per sequence (the row and the sum's scratch: 2K floats)
+            const size_t csmem = 2 * sizeof(float) * (size_t)a.K;
             if (dry) {
                 e = ensure_smem(k_prep_cl, csmem);
             } else {

@@ -396,45 +396,23 @@ static __global__ void __launch_bounds__(512) k_prep(const FArgs a, uint8_t* act
 
 // ---- residual update + norm on a cluster of PCL CTAs ------------------------------------------
 // The same computation as k_prep<PRO_RESNORM>, spread over a thread-block cluster so that the
-// per-block requantizations (three per 32 elements) run on PCL SMs instead of one. CTA c owns the
-// 32-blocks [c*E, (c+1)*E) of the row (E = ceil(blocks / PCL)). The exact sum of squares is split
-// as in seq_sum_exact; every CTA pushes what the others need into their shared memory (remote
-// stores of distributed shared memory), so each CTA reads its own copy after the cluster barrier:
-//   B1  largest square of each CTA (and every value to rank 0, for LayerNorm and the fallback)
-//   B2  fixed-point total of each CTA (the exact global prefix of every element follows)
-//   B3  heads (index, p, increment parity), per-CTA per-binade increment totals, ties, parities
-// then every CTA walks the binades itself (same data, same result) and normalizes its blocks.
-// LayerNorm, or a failed check of the exact sum: rank 0 runs the reference's serial loops and
-// pushes (mean, sd) to all CTAs before one more barrier (the condition is the same in all CTAs).
-// grid (PCL, B), cluster (PCL, 1, 1), block PCL_THREADS, dynamic smem K floats.
+// per-block requantizations (three per 32 elements) run on PCL SMs instead of one. CTA c updates
+// the 32-blocks [c*E, (c+1)*E) of the residual row (E = ceil(blocks / PCL)) and stores the new
+// values into the shared memory of every CTA of the cluster (distributed shared memory); after one
+// cluster barrier every CTA holds the whole row and computes the norm's statistics itself:
+//   RMSNorm    the exact sequential sum of squares (seq_sum_exact);
+//   LayerNorm  the reference's serial mean, then the exact sequential sum of squared deviations;
+// then normalizes its own blocks. grid (PCL, B), cluster (PCL, 1, 1), block PCL_THREADS, dynamic
+// shared memory 2K floats (the row, then K ints of scratch for the sum).
 constexpr int PCL = 8;
-constexpr int PCL_THREADS = 256;
-constexpr int PCL_TIES = 32;  // ties per CTA
+constexpr int PCL_THREADS = 512;
+constexpr int PCL_PER = 5;  // terms per thread of the exact sum in registers (K <= 2560)
 
 struct PclShared {
-    // pushed by every CTA before the barrier that publishes them
-    unsigned int maxv[PCL];
-    long long T[PCL];                  // fixed-point totals per CTA
-    int head[SEQSUM_SLOTS];
-    float phead[SEQSUM_SLOTS];
-    int hpar[SEQSUM_SLOTS];            // global increment parity at the head
-    long long tot[PCL][SEQSUM_SLOTS];  // increments per CTA per binade
-    int tie[PCL][PCL_TIES], tslot[PCL][PCL_TIES], tpar[PCL][PCL_TIES];  // tpar: CTA-local parity
-    int ntie[PCL];
-    int cpar[PCL];                     // parity of each CTA's increment total
-    int bad;
-    float stat[2];                     // (mean, sd) pushed by rank 0 on the serial path
-    // CTA-local scratch
-    long long wsum[PCL_THREADS / 32];
-    int wpar[PCL_THREADS / 32];
+    unsigned int maxv[PCL];  // largest square per CTA, pushed by every CTA before the barrier
     unsigned int wmax[PCL_THREADS / 32];
-    long long ltot[SEQSUM_SLOTS];
-    int lt[PCL_TIES], lts[PCL_TIES], ltp[PCL_TIES];
-    int lnt;
-    int sslot[PCL * PCL_TIES], sd[PCL * PCL_TIES], d0[SEQSUM_SLOTS], x[SEQSUM_SLOTS];
-    long long btot[SEQSUM_SLOTS];
-    int gpo[PCL + 1], tbase[PCL + 1];
-    float walk[2];
+    float mean;
+    SeqSumSmem ss;
 };
 
 // One block of the residual update (as in fgemv_prologue<PRO_RESNORM>): returns the new residual
@@ -474,10 +452,11 @@ __device__ __forceinline__ float resnorm_block(const FArgs& a, int blk, int lane
 static __global__ void __launch_bounds__(PCL_THREADS) k_prep_cl(const FArgs a, uint8_t* act, long act_s) {
     namespace cg = cooperative_groups;
     cg::cluster_group cl = cg::this_cluster();
-    extern __shared__ float sv[];  // the row, at global element indices (rank 0: all of it)
+    extern __shared__ float sv[];  // the row at global element indices, then K ints of scratch
     __shared__ PclShared S;
+    // every CTA of the cluster has started before the first remote store: arrive now, wait below
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     const int rank = (int)cl.block_rank();
-    float* sv0 = cl.map_shared_rank(sv, 0);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarps = PCL_THREADS / 32;
     const int K = a.K, nbk = (K + GTN_QBLK - 1) / GTN_QBLK, E = (nbk + PCL - 1) / PCL;
     const int b0 = min(nbk, rank * E), b1 = min(nbk, b0 + E);
@@ -490,21 +469,10 @@ static __global__ void __launch_bounds__(PCL_THREADS) k_prep_cl(const FArgs a, u
             if (a.nb) asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.nb) + off));
         }
     }
-    // local aggregation areas (remote writes into them come after B2)
-    if (tid < SEQSUM_SLOTS) {
-        S.ltot[tid] = 0;
-        S.head[tid] = -1;
-        S.d0[tid] = -1;
-        S.x[tid] = 0;
-    }
-    if (tid == 0) {
-        S.lnt = 0;
-        S.bad = 0;
-    }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     const int m = blockIdx.y;
-    // ---- residual update of this CTA's blocks
+    // ---- residual update of this CTA's blocks, stored into every CTA
     uint8_t* xo = a.xout ? a.xout + (long)m * a.xout_s : nullptr;  // every CTA writes its own blocks
     const uint8_t* xr = a.xres ? a.xres + (long)m * a.xres_s : nullptr;
     const float* y = a.yadd ? a.yadd + (long)m * a.yadd_s : nullptr;
@@ -517,6 +485,7 @@ static __global__ void __launch_bounds__(PCL_THREADS) k_prep_cl(const FArgs a, u
         }
         er = a.emb + (long)t * a.emb_s;
     }
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
     unsigned int mxb = 0u;
     for (int blk = b0 + warp; blk < b1; blk += nwarps) {
         const int i = blk * GTN_QBLK + lane;
@@ -526,8 +495,11 @@ static __global__ void __launch_bounds__(PCL_THREADS) k_prep_cl(const FArgs a, u
         const float yv = ok && y ? y[i] : 0.0f;
         const float r = resnorm_block(a, blk, lane, er, ev, xv, yv, y != nullptr, xo);
         if (ok) {
-            sv[i] = r;
-            if (rank != 0) sv0[i] = r;
+#pragma unroll
+            for (int q = 0; q < PCL; ++q) {
+                float* d = q == rank ? sv : cl.map_shared_rank(sv, q);
+                d[i] = r;
+            }
             mxb = max(mxb, seqsum_maxbits(r * r));
         }
     }
@@ -539,281 +511,31 @@ static __global__ void __launch_bounds__(PCL_THREADS) k_prep_cl(const FArgs a, u
         mb = __reduce_max_sync(0xffffffffu, mb);
         if (lane < PCL) cl.map_shared_rank(&S, lane)->maxv[rank] = mb;
     }
-    cl.sync();  // B1
-    const bool exact = !a.layer && K <= (1 << 14);  // K: keeps the fixed-point sum below 2^63
-    unsigned int maxbits = 0u;
+    cl.sync();  // the whole row and every CTA's largest square are in place
+    // ---- statistics, in every CTA (no remote access from here on)
+    int* incs = reinterpret_cast<int*>(sv + K);
+    float mean = 0.0f, sd;
+    if (!a.layer) {
+        unsigned int maxbits = 0u;
 #pragma unroll
-    for (int r = 0; r < PCL; ++r) maxbits = max(maxbits, S.maxv[r]);
-    const int emax = maxbits >= 0x800000u ? (int)(maxbits >> 23) - 127 : -126;
-    const int eoff = 23 + SEQSUM_FRAC_BITS - emax;
-    auto fixed = [&](float p) -> long long {
-        unsigned int M;
-        int Ex;
-        seqsum_split(p, M, Ex);
-        const int sh = Ex - emax + SEQSUM_FRAC_BITS;
-        if (sh >= 0) return (long long)M << sh;
-        return sh > -32 ? (long long)(M >> -sh) : 0LL;
-    };
-    const int ne = e1 - e0, per = (ne + PCL_THREADS - 1) / PCL_THREADS;
-    const int i0 = min(e1, e0 + tid * per), i1 = min(e1, i0 + per);
-    // ---- fixed-point totals; the exclusive prefix of each thread's chunk within the CTA
-    long long Q = 0;
-    if (exact) {
-        long long loc = 0;
-        for (int i = i0; i < i1; ++i) loc += fixed(sv[i] * sv[i]);
-        long long inc = loc;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const long long t = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += t;
-        }
-        if (lane == 31) S.wsum[warp] = inc;
-        __syncthreads();
-        long long base = 0, tot = 0;
-        for (int w = 0; w < nwarps; ++w) {
-            const long long ws = S.wsum[w];
-            if (w < warp) base += ws;
-            tot += ws;
-        }
-        Q = base + inc - loc;
-        if (tid < PCL) cl.map_shared_rank(&S, tid)->T[rank] = tot;
-    }
-    cl.sync();  // B2
-    if (exact && maxbits != 0u) {
-        for (int r = 0; r < rank; ++r) Q += S.T[r];
-        // ---- heads, increments, ties, parities; at most PCL_PER elements per thread, kept in
-        // registers (a longer chunk takes the serial path)
-        constexpr int PCL_PER = 2;
-        int sl_prev = Q > 0 ? 63 - __clzll(Q) : -1;
-        int par = 0;  // parity of this thread's increments so far
-        int esl[PCL_PER], einc[PCL_PER], epar[PCL_PER];
-        bool ehead[PCL_PER], etie[PCL_PER];
-        float ep[PCL_PER];
-        bool bad = maxbits >= 0x7f800000u || per > PCL_PER;
-#pragma unroll
-        for (int k = 0; k < PCL_PER; ++k) {
-            const int i = i0 + k;
-            esl[k] = -1;
-            einc[k] = 0;
-            epar[k] = par;
-            ehead[k] = false;
-            etie[k] = false;
-            ep[k] = 0.0f;
-            if (k < per && i < i1) {
-                const float p = sv[i] * sv[i];
-                Q += fixed(p);
-                if (Q == 0) {
-                    if (p != 0.0f) bad = true;
-                } else {
-                    const int sl = 63 - __clzll(Q);
-                    int inc = 0;
-                    if (sl != sl_prev) {
-                        ehead[k] = true;  // the binade's first term: its own increment is 0
-                    } else {
-                        const int e = sl - eoff;
-                        unsigned int M;
-                        int Ex;
-                        seqsum_split(p, M, Ex);
-                        const int sh = e - Ex;
-                        if (sh < 0 || e < -126) {
-                            bad = true;
-                        } else if (sh == 0) {
-                            inc = (int)M;
-                        } else if (sh < 32) {
-                            inc = (int)(M >> sh);
-                            const unsigned int rem = M & ((1u << sh) - 1u), half = 1u << (sh - 1);
-                            if (rem > half) ++inc;
-                            else if (rem == half) etie[k] = true;
-                        }
-                    }
-                    esl[k] = sl;
-                    einc[k] = inc;
-                    ep[k] = p;
-                    par ^= inc & 1;
-                    sl_prev = sl;
-                }
-            }
-        }
-        // per-binade totals: the lanes of one binade add up their increments, one atomic each
-#pragma unroll
-        for (int k = 0; k < PCL_PER; ++k) {
-            const int sl = esl[k];
-            const unsigned int grp = __match_any_sync(0xffffffffu, sl);
-            const int gsum = __reduce_add_sync(grp, einc[k]);
-            if (sl >= 0 && lane == __ffs(grp) - 1 && gsum)
-                atomicAdd(reinterpret_cast<unsigned long long*>(&S.ltot[sl]), (unsigned long long)(long long)gsum);
-        }
-        // exclusive parity prefix of the chunks within the CTA
-        const unsigned int pb = __ballot_sync(0xffffffffu, par & 1);
-        const int lane_pre = __popc(pb & ((1u << lane) - 1u)) & 1;
-        if (lane == 0) S.wpar[warp] = __popc(pb) & 1;
-        __syncthreads();
-        int wpre = 0, ctot = 0;
-        for (int w = 0; w < nwarps; ++w) {
-            if (w < warp) wpre ^= S.wpar[w];
-            ctot ^= S.wpar[w];
-        }
-        const int pre = wpre ^ lane_pre;  // parity of the CTA's increments before this chunk
-        // this CTA's ties with their CTA-local inclusive parity: one slot reservation per warp
-#pragma unroll
-        for (int k = 0; k < PCL_PER; ++k) {
-            const unsigned int tb = __ballot_sync(0xffffffffu, etie[k]);
-            int base = 0;
-            if (lane == 0 && tb) base = atomicAdd(&S.lnt, __popc(tb));
-            base = __shfl_sync(0xffffffffu, base, 0);
-            if (etie[k]) {
-                const int q = base + __popc(tb & ((1u << lane) - 1u));
-                if (q < PCL_TIES) {
-                    S.lt[q] = i0 + k;
-                    S.lts[q] = esl[k];
-                    S.ltp[q] = pre ^ epar[k] ^ (einc[k] & 1);
-                } else {
-                    bad = true;
-                }
-            }
-        }
-        __syncthreads();
-        // push to every CTA: heads (with the CTA-local parity; the global offset is added there),
-        // per-binade totals, ties, totals, failures
-        for (int r = 0; r < PCL; ++r) {
-            PclShared* D = cl.map_shared_rank(&S, r);
-#pragma unroll
-            for (int k = 0; k < PCL_PER; ++k) {
-                if (ehead[k]) {
-                    D->head[esl[k]] = i0 + k;
-                    D->phead[esl[k]] = ep[k];
-                    D->hpar[esl[k]] = pre ^ epar[k];
-                }
-            }
-            if (bad) D->bad = 1;
-        }
-        const int nlt = min(S.lnt, PCL_TIES);
-        for (int q = tid; q < PCL * SEQSUM_SLOTS; q += PCL_THREADS)
-            cl.map_shared_rank(&S, q / SEQSUM_SLOTS)->tot[rank][q % SEQSUM_SLOTS] = S.ltot[q % SEQSUM_SLOTS];
-        for (int q = tid; q < PCL * nlt; q += PCL_THREADS) {
-            PclShared* D = cl.map_shared_rank(&S, q / nlt);
-            const int k = q % nlt;
-            D->tie[rank][k] = S.lt[k];
-            D->tslot[rank][k] = S.lts[k];
-            D->tpar[rank][k] = S.ltp[k];
-        }
-        if (tid < PCL) {
-            PclShared* D = cl.map_shared_rank(&S, tid);
-            D->ntie[rank] = nlt;
-            D->cpar[rank] = ctot;
-            if (S.lnt > PCL_TIES) D->bad = 1;
-        }
-    }
-    cl.sync();  // B3
-    // ---- the walk, in every CTA
-    bool ok = exact && !S.bad;
-    float sum = 0.0f;
-    if (exact && maxbits != 0u && ok) {
-        if (tid == 0) {
-            S.gpo[0] = 0;
-            S.tbase[0] = 0;
-            for (int r = 0; r < PCL; ++r) {
-                S.gpo[r + 1] = S.gpo[r] ^ S.cpar[r];
-                S.tbase[r + 1] = S.tbase[r] + S.ntie[r];
-            }
-        }
-        if (tid >= 32 && tid < 32 + SEQSUM_SLOTS) {  // warps 1-2: the binade totals
-            const int sl = tid - 32;
-            long long t = 0;
-#pragma unroll
-            for (int r = 0; r < PCL; ++r) t += S.tot[r][sl];
-            S.btot[sl] = t;
-        }
-        __syncthreads();
-        const int nties = S.tbase[PCL];
-        for (int k = tid; k < nties; k += PCL_THREADS) {
-            int r = 0;
-#pragma unroll
-            for (int q = 1; q < PCL; ++q) r += k >= S.tbase[q];  // tbase is non-decreasing
-            const int kk = k - S.tbase[r];
-            const int i = S.tie[r][kk], sl = S.tslot[r][kk];
-            int rk = S.tbase[r];  // rank among all ties: earlier CTAs, then this CTA's smaller indices
-            for (int j = 0; j < S.ntie[r]; ++j) rk += S.tie[r][j] < i;
-            const int h = S.head[sl];
-            const int hr = (h / GTN_QBLK) / E;
-            S.sslot[rk] = sl;
-            S.sd[rk] = (S.gpo[r] ^ S.tpar[r][kk]) ^ (S.gpo[hr] ^ S.hpar[sl]);
-        }
-        __syncthreads();
-        for (int k = tid; k < nties; k += PCL_THREADS) {
-            const int sl = S.sslot[k];
-            if (k == 0 || S.sslot[k - 1] != sl) S.d0[sl] = S.sd[k];
-            else atomicAdd(&S.x[sl], S.sd[k] ^ S.sd[k - 1]);
-        }
-        __syncthreads();
-        if (warp == 0) {
-            float Sx = 0.0f;
-            bool okw = true;
-            unsigned long long hm = (unsigned long long)__ballot_sync(0xffffffffu, S.head[lane] >= 0) |
-                                    ((unsigned long long)__ballot_sync(0xffffffffu, S.head[lane + 32] >= 0) << 32);
-            while (okw && hm) {
-                const int sl = __ffsll((long long)hm) - 1;
-                hm &= hm - 1;
-                const int e = sl - eoff;
-                Sx = Sx + S.phead[sl];
-                const unsigned int b = __float_as_uint(Sx);
-                if ((int)(b >> 23) - 127 != e || e < -126) {
-                    okw = false;
-                    break;
-                }
-                long long Sb = (long long)((b & 0x7fffffu) | 0x800000u);
-                const int dd = S.d0[sl];
-                if (dd >= 0) Sb += ((Sb + dd) & 1) + S.x[sl];
-                Sb += S.btot[sl];
-                if (Sb >= (1LL << 24)) {
-                    okw = false;
-                    break;
-                }
-                Sx = __uint_as_float(((unsigned int)(e + 127) << 23) | ((unsigned int)Sb & 0x7fffffu));
-            }
-            if (lane == 0) {
-                S.walk[0] = okw ? 1.0f : 0.0f;
-                S.walk[1] = Sx;
-            }
-        }
-        __syncthreads();
-        ok = S.walk[0] != 0.0f;
-        sum = S.walk[1];
-    }
-    float mean = 0.0f, sd = 0.0f;
-    if (exact && (maxbits == 0u || ok)) {
-        sd = sqrtf(sum / (float)K);  // every square +0 (sum 0), or the walk's exact sum
+        for (int r = 0; r < PCL; ++r) maxbits = max(maxbits, S.maxv[r]);
+        const float sq = seq_sum_squares<PCL_PER>(sv, K, S.ss, incs, maxbits);
+        sd = sqrtf(sq / (float)K);
     } else {
-        // LayerNorm, or a failed check: the reference's loops on rank 0, pushed to every CTA
-        if (rank == 0 && tid == 0) {
-            if (a.layer) {
-                float s0 = 0.0f;
-                for (int i = 0; i < K; ++i) s0 = s0 + sv[i];
-                mean = s0 / (float)K;
-                float ss = 0.0f;
-                for (int i = 0; i < K; ++i) {
-                    const float d = sv[i] - mean;
-                    const float d2 = d * d;
-                    ss = ss + d2;
-                }
-                sd = sqrtf(ss / (float)K);
-            } else {
-                float sq = 0.0f;
-                for (int i = 0; i < K; ++i) {
-                    const float p = sv[i] * sv[i];
-                    sq = sq + p;
-                }
-                sd = sqrtf(sq / (float)K);
-            }
-            for (int r = 0; r < PCL; ++r) {
-                PclShared* D = cl.map_shared_rank(&S, r);
-                D->stat[0] = mean;
-                D->stat[1] = sd;
-            }
+        if (tid == 0) {  // the signed sum of the mean: the reference's loop
+            float s0 = 0.0f;
+            for (int i = 0; i < K; ++i) s0 = s0 + sv[i];
+            S.mean = s0 / (float)K;
         }
-        cl.sync();  // B4 (taken by every CTA: the condition is the same everywhere)
-        mean = S.stat[0];
-        sd = S.stat[1];
+        __syncthreads();
+        mean = S.mean;
+        const float ss = seq_sum_exact<PCL_PER>(
+            [mean](int i) {
+                const float d = sv[i] - mean;
+                return d * d;
+            },
+            K, S.ss, incs);
+        sd = sqrtf(ss / (float)K);
     }
     // ---- norm of this CTA's blocks -> act
     uint8_t* xq = act + (long)m * act_s;
@@ -838,7 +560,6 @@ static __global__ void __launch_bounds__(PCL_THREADS) k_prep_cl(const FArgs a, u
             requant(yv, lane, nv, a.adt, xq, blk);
         }
     }
-    // no remote access after the last cluster barrier: a CTA may leave while others still work
 }
 
 // The SwiGLU activation is block-local, so it is spread over many CTAs: grid (ceil(blocks/32), B),

@@ -21,12 +21,13 @@
 //      term i. Integer sums are associative, so every thread sees the same prediction at every
 //      index;
 //  (3) the first term of each predicted binade is its "head"; every other term gets its integer
-//      increment w.r.t. its binade's ulp (integer arithmetic on the float's bits); ties are listed;
-//  (4) an int64 prefix scan of the increments;
-//  (5) per binade (in parallel): the increments from its head to the next head and the tie terms
-//      above; then warp 0 walks the binades in order (their data in lane registers, fetched by
-//      shuffles): S = fl(S + p_head) (an exact IEEE add) must land in binade e, then
-//      S/u += increments + round-ups, which must stay below 2^24.
+//      increment w.r.t. its binade's ulp (integer arithmetic on the float's bits) or is a tie;
+//  (4) one int64 prefix scan of (increments + tie count * 2^48) gives every thread the increments
+//      and the ties before its chunk, so heads record their increment prefix and ties land in
+//      index order;
+//  (5) per binade (in parallel): the increments from its head to the next head, and the tie
+//      parities d_j; then one warp walks the binades in order: S = fl(S + p_head) (an exact IEEE
+//      add) must land in binade e, then S/u += increments + round-ups, which must stay below 2^24.
 // Any failed check (a mispredicted crossing, a term below the fixed-point resolution, a subnormal
 // binade, a non-finite term, more ties than the list holds) makes the CTA fall back to the plain
 // sequential loop, so the result is always bit-identical to the serial sum.
@@ -43,16 +44,17 @@ constexpr int SEQSUM_PER_MAX = 8;     // terms per thread kept in registers
 
 struct SeqSumSmem {
     long long wsum[2][SEQSUM_THREADS_MAX / 32];  // per-warp partials of the two scans
-    long long cpre[SEQSUM_THREADS_MAX];          // per-thread exclusive prefix of the increments
-    long long tot[SEQSUM_SLOTS];                 // per binade: increments from its head to the next head
+    long long hpre[SEQSUM_SLOTS];                // per binade: increments before its head
     int head[SEQSUM_SLOTS];
     float phead[SEQSUM_SLOTS];
     int d0[SEQSUM_SLOTS];  // parity of the first tie (or -1: no tie)
     int x[SEQSUM_SLOTS];   // sum of d_j xor d_(j-1) over the binade's ties
-    int tie[SEQSUM_TIES_MAX], tslot[SEQSUM_TIES_MAX];
-    int sslot[SEQSUM_TIES_MAX], sd[SEQSUM_TIES_MAX];
-    unsigned int mask[2];
-    int ntie;
+    int sslot[SEQSUM_TIES_MAX], sd[SEQSUM_TIES_MAX];  // ties in index order: binade, parity d_j
+    // the walk's inputs, binades in order
+    float wph[SEQSUM_SLOTS];
+    int we[SEQSUM_SLOTS], wdd[SEQSUM_SLOTS];
+    long long wadd[SEQSUM_SLOTS];
+    int nbin;
     int bad;
     unsigned int maxbits;
     float result;
@@ -95,27 +97,29 @@ __device__ __forceinline__ void seqsum_split(float p, unsigned int& M, int& E) {
 __device__ __forceinline__ unsigned int seqsum_maxbits(float p) { return __float_as_uint(p); }
 
 // Returns fl(...fl(fl(0 + p_0) + p_1)... + p_{n-1}) where p_i = term(i) >= 0 (a float computed
-// the same way on every call). `incs`: n ints of scratch (shared memory). maxbits: the largest
-// term's bit pattern if the caller knows it (from seqsum_maxbits), else 0. All threads of the
-// CTA must call it (blockDim.x <= 1024, a multiple of 32, >= 64); it synchronizes the CTA.
-template <class Term>
+// the same way on every call). `incs`: unused scratch (kept for callers' layouts). maxbits: the
+// largest term's bit pattern if the caller knows it (from seqsum_maxbits), else 0. All threads of
+// the CTA must call it (blockDim.x <= 1024, a multiple of 32, >= 64); it synchronizes the CTA.
+// PER: terms per thread kept in registers (more per thread: the serial loop).
+template <int PER = SEQSUM_PER_MAX, class Term>
 __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, int* incs, unsigned int maxbits = 0u) {
+    (void)incs;
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
+    const int nw = (nt + 31) >> 5;
     const int per = (n + nt - 1) / nt;
     const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
-    // more than SEQSUM_PER_MAX terms per thread: the serial loop (cnt = 0 skips the parallel work)
-    const int cnt = per <= SEQSUM_PER_MAX ? i1 - i0 : 0;
-    float pv[SEQSUM_PER_MAX];
+    // more than PER terms per thread: the serial loop (cnt = 0 skips the parallel work)
+    const int cnt = per <= PER ? i1 - i0 : 0;
+    float pv[PER];
 #pragma unroll
-    for (int k = 0; k < SEQSUM_PER_MAX; ++k) pv[k] = k < cnt ? term(i0 + k) : 0.0f;
+    for (int k = 0; k < PER; ++k) pv[k] = k < cnt ? term(i0 + k) : 0.0f;
     if (tid < SEQSUM_SLOTS) {
         s.head[tid] = -1;
         s.d0[tid] = -1;
         s.x[tid] = 0;
     }
     if (tid == 0) {
-        s.bad = n > (1 << 14) || per > SEQSUM_PER_MAX;  // n: keeps the fixed-point sum below 2^63
-        s.ntie = 0;
+        s.bad = n > (1 << 14) || per > PER;  // n: keeps the fixed-point sum below 2^63
         s.maxbits = maxbits;
     }
     if (maxbits == 0u) {
@@ -123,7 +127,7 @@ __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, 
         // (1) largest term (non-negative floats order like their bit patterns)
         unsigned int mb = 0u;
 #pragma unroll
-        for (int k = 0; k < SEQSUM_PER_MAX; ++k) mb = max(mb, __float_as_uint(pv[k]));  // pv >= +0
+        for (int k = 0; k < PER; ++k) mb = max(mb, __float_as_uint(pv[k]));  // pv >= +0
         mb = __reduce_max_sync(0xffffffffu, mb);
         if (lane == 0) atomicMax(&s.maxbits, mb);
     }
@@ -132,159 +136,153 @@ __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, 
     if (maxbits == 0u) return 0.0f;                   // every term is +0: the sum is exactly 0
     if (maxbits >= 0x7f800000u) s.bad = 1;            // inf / nan / a negative term
     const int emax = maxbits >= 0x800000u ? (int)(maxbits >> 23) - 127 : -126;
-    // t_i = floor(p_i * 2^eoff), eoff = 23 + SEQSUM_FRAC_BITS - emax, i.e. with p = M * 2^(E-23):
-    // t_i = M << (E - emax + SEQSUM_FRAC_BITS), truncated when the shift is negative.
-    auto fixed = [&](float p) -> long long {
-        unsigned int M;
-        int E;
-        seqsum_split(p, M, E);
-        const int sh = E - emax + SEQSUM_FRAC_BITS;
-        if (sh >= 0) return (long long)M << sh;  // sh <= 25
-        return sh > -32 ? (long long)(M >> -sh) : 0LL;
-    };
     // binade exponent of slot sl: Q = S * 2^eoff => e = sl - eoff
     const int eoff = 23 + SEQSUM_FRAC_BITS - emax;
-    // (2) exact fixed-point prefix
-    long long loc = 0;
+    // (2) t_i = floor(p_i * 2^eoff): with p = M * 2^(E-23), t_i = M << (E - emax + SEQSUM_FRAC_BITS),
+    // truncated when the shift is negative; then the exact exclusive prefix over the CTA
+    unsigned int Mv[PER];
+    int Ev[PER];
+    long long fx[PER], loc = 0;
 #pragma unroll
-    for (int k = 0; k < SEQSUM_PER_MAX; ++k) loc += fixed(pv[k]);  // pv[k >= cnt] = 0
-    long long Q = seqsum_exscan64(loc, s.wsum[0]);
-    // (3) heads, increments, ties
-    int sl_prev = Q > 0 ? 63 - __clzll(Q) : -1;
+    for (int k = 0; k < PER; ++k) {
+        seqsum_split(pv[k], Mv[k], Ev[k]);
+        const int sh = Ev[k] - emax + SEQSUM_FRAC_BITS;
+        fx[k] = sh >= 0 ? (long long)Mv[k] << sh : (sh > -32 ? (long long)(Mv[k] >> -sh) : 0LL);  // sh <= 25
+        loc += fx[k];  // pv[k >= cnt] = 0
+    }
+    const long long Q0 = seqsum_exscan64(loc, s.wsum[0]);
+    // (3) per term: binade slot, head flag, increment, tie (independent once the slots are known)
+    int slv[PER], inc[PER];
+    bool hd[PER], tie[PER];
+    bool bad = false;
+    {
+        long long Q = Q0;
+        int slp = Q0 > 0 ? 63 - __clzll(Q0) : -1;
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            Q += fx[k];
+            const bool valid = k < cnt;
+            const int sk = Q > 0 ? 63 - __clzll(Q) : -1;  // < 63 since Q < 2^63
+            bad |= valid && Q == 0 && pv[k] != 0.0f;      // a non-zero term below the resolution
+            const bool live = valid && sk >= 0;
+            hd[k] = live && sk != slp;
+            const int e = sk - eoff, sh = e - Ev[k];  // p / u = M * 2^-sh
+            const bool rest = live && !hd[k];
+            bad |= rest && (sh < 0 || e < -126);
+            const int shc = min(max(sh, 1), 31);
+            const unsigned int rem = Mv[k] & ((1u << shc) - 1u), half = 1u << (shc - 1);
+            int v = sh == 0 ? (int)Mv[k] : (int)(Mv[k] >> shc) + (rem > half ? 1 : 0);
+            v = (sh < 0 || sh >= 32) ? 0 : v;  // sh >= 32: p < u/2^8, the add does not change S
+            inc[k] = rest ? v : 0;
+            tie[k] = rest && sh > 0 && sh < 32 && rem == half;
+            slv[k] = valid ? sk : -1;
+            slp = live ? sk : slp;
+        }
+    }
+    if (bad) s.bad = 1;
+    // (4) one scan of (increments + ties * 2^48): increments < 2^24 per term, ties <= 2^14
     long long itot = 0;
+    int ntl = 0;
 #pragma unroll
-    for (int k = 0; k < SEQSUM_PER_MAX; ++k) {
-        if (k >= cnt) break;
-        const int i = i0 + k;
-        const float p = pv[k];
-        Q += fixed(p);
-        int inc = 0;
-        if (Q == 0) {
-            if (p != 0.0f) s.bad = 1;  // a non-zero term below the fixed-point resolution
-        } else {
-            const int sl = 63 - __clzll(Q);  // < 63 since Q < 2^63
-            if (sl != sl_prev) {
-                s.head[sl] = i;
-            } else {
-                const int e = sl - eoff;
-                unsigned int M;
-                int E;
-                seqsum_split(p, M, E);
-                const int sh = e - E;  // p / u = M * 2^-sh
-                if (sh < 0 || e < -126) {
-                    s.bad = 1;
-                } else if (sh == 0) {
-                    inc = (int)M;
-                } else if (sh < 32) {
-                    inc = (int)(M >> sh);
-                    const unsigned int rem = M & ((1u << sh) - 1u), half = 1u << (sh - 1);
-                    if (rem > half) {
-                        ++inc;
-                    } else if (rem == half) {
-                        const int t = atomicAdd(&s.ntie, 1);
-                        if (t < SEQSUM_TIES_MAX) {
-                            s.tie[t] = i;
-                            s.tslot[t] = sl;
-                        } else {
-                            s.bad = 1;
-                        }
-                    }
-                }  // sh >= 32: p < u/2^8, the add does not change S
+    for (int k = 0; k < PER; ++k) {
+        itot += inc[k];
+        ntl += tie[k] ? 1 : 0;
+    }
+    constexpr long long LOW48 = (1LL << 48) - 1;
+    const long long P = seqsum_exscan64(itot + ((long long)ntl << 48), s.wsum[1]);
+    const long long total = s.wsum[1][nw - 1] & LOW48;  // inclusive over the last warp
+    const int ntie_all = (int)(s.wsum[1][nw - 1] >> 48);
+    long long cur = P & LOW48;
+    int trank = (int)(P >> 48);
+    long long tpre[PER];  // inclusive increment prefix at each term
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        cur += inc[k];
+        tpre[k] = cur;
+        if (hd[k]) {
+            s.head[slv[k]] = i0 + k;
+            s.hpre[slv[k]] = cur;  // a head's own increment is 0
+            s.phead[slv[k]] = pv[k];
+        }
+    }
+    __syncthreads();
+    // (5a) ties in index order: binade and the parity of the binade's increments up to the tie
+    const int nties = min(ntie_all, SEQSUM_TIES_MAX);
+    if (ntie_all > SEQSUM_TIES_MAX && tid == 0) s.bad = 1;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        if (tie[k]) {
+            if (trank < SEQSUM_TIES_MAX) {
+                s.sslot[trank] = slv[k];
+                s.sd[trank] = (int)((tpre[k] - s.hpre[slv[k]]) & 1);
             }
-            sl_prev = sl;
-        }
-        incs[i] = inc;
-        itot += inc;
-    }
-    // (4) prefix of the increments: per-thread exclusive offsets in cpre
-    const long long ip = seqsum_exscan64(itot, s.wsum[1]);
-    s.cpre[tid] = ip;
-    if (tid < SEQSUM_SLOTS) {
-        const unsigned int bal = __ballot_sync(0xffffffffu, s.head[tid] >= 0);
-        if (lane == 0) s.mask[warp] = bal;
-    }
-    __syncthreads();
-    auto incl = [&](int i) -> long long {  // inclusive prefix of incs at i
-        const int owner = i / per;
-        long long r = s.cpre[owner];
-        for (int j = owner * per; j <= i; ++j) r += incs[j];
-        return r;
-    };
-    const int nties = min(s.ntie, SEQSUM_TIES_MAX);
-    const unsigned long long mask = ((unsigned long long)s.mask[1] << 32) | s.mask[0];
-    // (5a) per binade: increments from the head to the next head; tie parities in index order
-    if (tid < SEQSUM_SLOTS) {
-        const int h = s.head[tid];
-        if (h >= 0) {
-            const unsigned long long above = tid < 63 ? mask & (~0ULL << (tid + 1)) : 0ULL;
-            const int hn = above ? s.head[__ffsll((long long)above) - 1] : n;
-            s.tot[tid] = incl(hn - 1) - incl(h);
-            s.phead[tid] = term(h);
+            ++trank;
         }
     }
-    for (int k = tid - SEQSUM_SLOTS; k >= 0 && k < nties; k += nt) {  // rank sort of the ties
-        const int i = s.tie[k];
-        int r = 0;
-        for (int j = 0; j < nties; ++j) r += s.tie[j] < i;
-        const int sl = s.tslot[k];
-        s.sslot[r] = sl;
-        s.sd[r] = (int)((incl(i) - incl(s.head[sl])) & 1);
+    // (5b) warps 0-1, one binade slot per thread: the binades in order (64 slots as two ballots)
+    // and their increment totals
+    if (tid < SEQSUM_SLOTS) {
+        const unsigned long long mask = (unsigned long long)__ballot_sync(0xffffffffu, s.head[lane] >= 0) |
+                                        ((unsigned long long)__ballot_sync(0xffffffffu, s.head[lane + 32] >= 0) << 32);
+        const int sl = tid;
+        if ((mask >> sl) & 1ULL) {
+            const unsigned long long above = sl < 63 ? mask & (~0ULL << (sl + 1)) : 0ULL;
+            const long long nxt = above ? s.hpre[__ffsll((long long)above) - 1] : total;
+            const int r = __popcll(mask & ((1ULL << sl) - 1ULL));
+            s.wph[r] = s.phead[sl];
+            s.we[r] = sl - eoff;
+            s.wadd[r] = nxt - s.hpre[sl];
+        }
+        if (tid == 0) s.nbin = __popcll(mask);
     }
     __syncthreads();
+    // (5c) per binade: the first tie's parity and the changes between consecutive ties
     for (int r = tid; r < nties; r += nt) {
         const int sl = s.sslot[r];
         if (r == 0 || s.sslot[r - 1] != sl) s.d0[sl] = s.sd[r];
         else atomicAdd(&s.x[sl], s.sd[r] ^ s.sd[r - 1]);
     }
     __syncthreads();
-    // (5b) the walk: warp 0, binades in slot order, 32 at a time in lane registers
+    // (5d) the walk (warp 0, every lane the same chain; lane 0 keeps the result). Lane j holds
+    // binades j and j + 32 in registers; the chain takes them by shuffles.
     if (warp == 0) {
         bool ok = !s.bad;
         float S = 0.0f;
-        unsigned long long m = mask;
-        while (ok && m) {
-            // lane j takes the j-th remaining binade
-            unsigned long long mm = m;
-            int mine = -1;
-            for (int j = 0; j < 32 && mm; ++j) {
-                const int sl = __ffsll((long long)mm) - 1;
-                mm &= mm - 1;
-                if (j == lane) mine = sl;
+        const int nb = s.nbin;
+        float ph[2];
+        int ee[2], dd[2];
+        long long ad[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int j = lane + 32 * h;
+            ph[h] = 0.0f;
+            ee[h] = 0;
+            dd[h] = -1;
+            ad[h] = 0;
+            if (j < nb) {
+                const int sl = s.we[j] + eoff;  // x is 0 without ties
+                ph[h] = s.wph[j];
+                ee[h] = s.we[j];
+                dd[h] = s.d0[sl];
+                ad[h] = s.wadd[j] + s.x[sl];
             }
-            const int cnt = min(32, __popcll(m));
-            float ph = 0.0f;
-            long long tt = 0;
-            int dd = -1, xx = 0;
-            if (mine >= 0) {
-                ph = s.phead[mine];
-                tt = s.tot[mine];
-                dd = s.d0[mine];
-                xx = s.x[mine];
-            }
-            for (int j = 0; j < cnt; ++j) {
-                const int sl = __shfl_sync(0xffffffffu, mine, j);
-                const float phj = __shfl_sync(0xffffffffu, ph, j);
-                const long long ttj = __shfl_sync(0xffffffffu, tt, j);
-                const int ddj = __shfl_sync(0xffffffffu, dd, j);
-                const int xxj = __shfl_sync(0xffffffffu, xx, j);
-                if (!ok) continue;
-                const int e = sl - eoff;
-                S = S + phj;
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll 4
+            for (int jj = 0; jj < 32; ++jj) {
+                if (!ok || 32 * h + jj >= nb) break;
+                const float p = __shfl_sync(0xffffffffu, ph[h], jj);
+                const int e = __shfl_sync(0xffffffffu, ee[h], jj), d = __shfl_sync(0xffffffffu, dd[h], jj);
+                const long long add = __shfl_sync(0xffffffffu, ad[h], jj);
+                S = S + p;
                 const unsigned int b = __float_as_uint(S);
-                if ((int)(b >> 23) - 127 != e || e < -126) {
-                    ok = false;
-                    continue;
-                }
                 long long Sb = (long long)((b & 0x7fffffu) | 0x800000u);  // S / u
-                if (ddj >= 0) Sb += ((Sb + ddj) & 1) + xxj;
-                Sb += ttj;
-                if (Sb >= (1LL << 24)) {
-                    ok = false;
-                    continue;
-                }
+                Sb += d >= 0 ? ((Sb + d) & 1) : 0;
+                Sb += add;
+                ok = (int)(b >> 23) - 127 == e && e >= -126 && Sb < (1LL << 24);
                 S = __uint_as_float(((unsigned int)(e + 127) << 23) | ((unsigned int)Sb & 0x7fffffu));
             }
-            m = mm;
         }
         if (lane == 0) {
             if (!ok) {  // fallback: the reference's loop as is
@@ -302,9 +300,10 @@ __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, 
 }
 
 // The sum of squares of v[0..n) (RMSNorm, ops.cpp:830-836: glibc powf(x, 2) == x*x exactly).
+template <int PER = SEQSUM_PER_MAX>
 __device__ __forceinline__ float seq_sum_squares(const float* v, int n, SeqSumSmem& s, int* incs,
                                                  unsigned int maxbits = 0u) {
-    return seq_sum_exact([v](int i) { return v[i] * v[i]; }, n, s, incs, maxbits);
+    return seq_sum_exact<PER>([v](int i) { return v[i] * v[i]; }, n, s, incs, maxbits);
 }
 
 }  // namespace gtn
