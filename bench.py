@@ -39,6 +39,7 @@ N_PROMPT, N_GEN, SEED = 64, 256, 1234
 # `ncu --set full --clock-control none -k regex:k_gemv3 -s 3 -c 1 python bench.py --gemv-only
 # --gemv-shape gate_up` (profiles/k_gemv3_gate_up_q8.md)
 GATE_UP_TRAFFIC_BYTES = 24_539_648
+WEIGHT_GB = {1: 2.07, 3: 1.10, 4: 0.58}  # TinyLlama weight bytes streamed per token
 WDT_NAMES = {3: "q8", 4: "q4", 1: "f16"}
 
 
@@ -286,10 +287,10 @@ def run_ours(args, rank, world, local):
                                    f"decode tokens per request (BASELINE configs[0])",
                        "model": "tinyllama-1.1b", "global_batch": world, "seq_len": N_PROMPT + N_GEN,
                        "parallelism": f"replicas x{world} (a batch-1 request does not shard)",
-                       "l2": "weights 1.17 GB > 126 MB L2; no flush needed"},
+                       "l2": f"weights {WEIGHT_GB[wdt]} GB > 126 MB L2; no flush needed"},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": N_PROMPT * 4,
                     "d2h_bytes_per_step": N_GEN * 4},
-            "roofline": {"bound": "hbm", "kernel": "k_gemv3 (exact Q8 GEMV, gate_up 11264x2048)",
+            "roofline": {"bound": "hbm", "kernel": f"k_gemv3 (exact {WDT_NAMES[wdt].upper()} GEMV, gate_up 11264x2048)",
                          "achieved": dom["GB_s"], "peak": hbm, "unit": "GB/s",
                          "frac": round(dom["GB_s"] / hbm, 3), "peak_kind": peak_kind,
                          "traffic": GATE_UP_TRAFFIC_BYTES if wdt == 3 else None,
@@ -373,6 +374,42 @@ def run_batch(args, rank, world, local):
     return res
 
 
+def run_load(args):
+    """Model upload throughput: a TinyLlama image (host memory) through gtn_model_load, and the same
+    bytes from a file (written first, so it is in the page cache) through gtn_model_load_file."""
+    import tempfile
+
+    import torch
+
+    import gten_b200 as G
+    from gten_b200 import gtenfile
+    img = gtenfile.synthetic_image_device(G.TINYLLAMA, args.wdtype, SEED)
+    m = G.Model(G.TINYLLAMA, args.wdtype, N_PROMPT + N_GEN)
+    m.load(img)  # first load: the arena and the pinned upload buffers are allocated
+    res = {"metric": "model upload GB/s", "unit": "GB/s", "bytes": int(img.size),
+           "config": {"workload": f"TinyLlama-1.1B {WDT_NAMES[args.wdtype].upper()} .gten image"}}
+    for key, fn in (("host_image", lambda: m.load(img)), ("file", None)):
+        if fn is None:
+            d = "/dev/shm" if os.path.isdir("/dev/shm") else tempfile.gettempdir()
+            path = os.path.join(d, f"bench_load_{os.getpid()}.gten")
+            img.tofile(path)
+            fn = (lambda p: (lambda: m.load_file(p)))(path)
+        ts = []
+        for _ in range(max(args.steps, 3)):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize()
+            ts.append(time.perf_counter() - t0)
+        res[key] = {"GB_s": round(img.size / min(ts) / 1e9, 2), "ms_best": round(min(ts) * 1e3, 2),
+                    "ms_median": round(sorted(ts)[len(ts) // 2] * 1e3, 2)}
+        if key == "file":
+            os.remove(path)
+    res["value"] = res["host_image"]["GB_s"]
+    m.close()
+    return res
+
+
 def run_reference(args, rank, world):
     """The reference arm: the compiled reference CPU path on this host (rank 0 only)."""
     if rank != 0:
@@ -428,6 +465,9 @@ def main():
     ap.add_argument("--batch", type=int, default=1,
                     help="global batch of sequences sharded over the ranks (default 1: the headline bs1 request)")
     ap.add_argument("--model", default="tinyllama", choices=sorted(BATCH_MODELS), help="with --batch > 1")
+    ap.add_argument("--load", action="store_true",
+                    help="only time the model upload (gtn_model_load from host memory, gtn_model_load_file "
+                         "from a file in the page cache)")
     ap.add_argument("--decode-only", type=int, default=0, metavar="T",
                     help="only load the model and run one request of T generated tokens (for a launch list)")
     args = ap.parse_args()
@@ -444,6 +484,9 @@ def main():
         m.check()
         m.close()
         print(json.dumps({"decode_only": args.decode_only, "first_ids": [int(x) for x in out[:8]]}), flush=True)
+        return
+    if args.load:
+        print(json.dumps(run_load(args)), flush=True)
         return
     if args.gemv_only:
         import torch

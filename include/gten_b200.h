@@ -177,8 +177,14 @@ void gtn_model_free(gtn_model* m);
 int gtn_model_n_vocab(const gtn_model* m);
 
 /* load_from_ckpt (e.g. tinyllama.cpp:195-251; reader utils.cpp:29-61) from a complete .gten
- * image in host memory (magic, then records in the model's load order). */
+ * image in host memory (magic, then records in the model's load order). The records go to HBM
+ * through pinned staging buffers with asynchronous copies (host threads fill one buffer while
+ * the copy engine drains the others). Synchronous. */
 int gtn_model_load(gtn_model* m, const void* host_image, size_t nbytes);
+
+/* load_from_ckpt from a .gten file path, as the reference opens it (utils.cpp:29-61): the file
+ * is memory-mapped and loaded as gtn_model_load does. */
+int gtn_model_load_file(gtn_model* m, const char* path);
 
 /* Model::logits(tokens, start_pos) for sequence 0 (abc.h:25): tokens (host int32, n_tokens total,
  * rows [start_pos, n_tokens) are new) -> host fp32 logits of the last row. Synchronous. */

@@ -11,10 +11,16 @@
 // The KV cache of layer l is the K/V Linear activation buffer of the reference (modules.cpp:78-87):
 // [max_batch][max_ctx][kv_dim] rows in the activation dtype, post-RoPE keys.
 // Activations of the rows being computed use local row indices 0..M-1.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <memory>
+#include <thread>
 #include <vector>
 
 #include "fused.cuh"
@@ -78,6 +84,11 @@ struct gtn_model {
     float graph_temp = 0.0f;
     int graph_topk = 0;
     int* pos_host = nullptr;  // pinned staging for position uploads
+    // pinned staging of the model upload (allocated by the first load): one buffer, event and
+    // stream per upload worker
+    uint8_t* stage[8] = {};
+    cudaEvent_t stage_ev[8] = {};
+    cudaStream_t stage_st[8] = {};
 };
 
 namespace gtn {
@@ -264,6 +275,11 @@ void gtn_model_free(gtn_model* m) {
     if (m->st) cudaStreamSynchronize(m->st);
     if (m->graph) cudaGraphExecDestroy(m->graph);
     if (m->pos_host) cudaFreeHost(m->pos_host);
+    for (int i = 0; i < 8; ++i) {
+        if (m->stage[i]) cudaFreeHost(m->stage[i]);
+        if (m->stage_ev[i]) cudaEventDestroy(m->stage_ev[i]);
+        if (m->stage_st[i]) cudaStreamDestroy(m->stage_st[i]);
+    }
     free_all(m);
     if (m->arena) cudaFree(m->arena);
     if (m->st) cudaStreamDestroy(m->st);
@@ -272,8 +288,146 @@ void gtn_model_free(gtn_model* m) {
 
 int gtn_model_n_vocab(const gtn_model* m) { return m ? m->n_vocab : 0; }
 
+}  // extern "C"
+
+namespace gtn {
+
+struct LoadPiece {
+    const uint8_t* src;  // host bytes of the record (rows of rb bytes, back to back)
+    long rows, rb;
+    long off;            // arena offset; rows land at a stride of pad16(rb) when rows > 1
+};
+
+constexpr int LOAD_WORKERS = 8;
+constexpr size_t LOAD_STAGE_BYTES = 8u << 20;
+
+struct LoadChunk {
+    const LoadPiece* p;
+    long a, b;  // rows [a, b) of a padded piece, or bytes [a, b) of an unpadded one
+};
+
+// Host -> arena upload: the records are cut into chunks of at most LOAD_STAGE_BYTES and worker w
+// takes chunks w, w + W, ...: it copies the chunk into its pinned buffer (rows placed at the
+// arena's padded stride, pad bytes zero), issues the asynchronous copy on its own stream and,
+// before refilling the buffer, waits for the event recorded behind that copy. W single-threaded
+// host copies run side by side while the copy engines drain the buffers already filled.
+// With fd >= 0 the record bytes are read from that file (src - base is the file offset) straight
+// into the pinned buffers instead of copied from memory.
+static int upload_pieces(gtn_model* m, const std::vector<LoadPiece>& pieces, int fd = -1,
+                         const uint8_t* base = nullptr) {
+    for (int i = 0; i < LOAD_WORKERS; ++i) {
+        if (!m->stage[i]) ECHK(cudaHostAlloc((void**)&m->stage[i], LOAD_STAGE_BYTES, cudaHostAllocDefault), "model_load: staging");
+        if (!m->stage_ev[i]) ECHK(cudaEventCreateWithFlags(&m->stage_ev[i], cudaEventDisableTiming), "model_load: staging");
+        if (!m->stage_st[i]) ECHK(cudaStreamCreateWithFlags(&m->stage_st[i], cudaStreamNonBlocking), "model_load: staging");
+    }
+    std::vector<LoadChunk> chunks;
+    for (const LoadPiece& p : pieces) {
+        const long stride = p.rows > 1 ? pad16(p.rb) : p.rb;
+        if (stride == p.rb) {
+            const long total = p.rows * p.rb;
+            for (long x = 0; x < total; x += (long)LOAD_STAGE_BYTES)
+                chunks.push_back({&p, x, std::min(total, x + (long)LOAD_STAGE_BYTES)});
+        } else {
+            const long per = std::max(1L, (long)LOAD_STAGE_BYTES / stride);
+            for (long r = 0; r < p.rows; r += per) chunks.push_back({&p, r, std::min(p.rows, r + per)});
+        }
+    }
+    // the arena clear (model stream) comes before every upload copy
+    ECHK(cudaStreamSynchronize(m->st), "model_load");
+    int dev = 0;
+    ECHK(cudaGetDevice(&dev), "model_load");
+    std::vector<cudaError_t> err(LOAD_WORKERS, cudaSuccess);
+    auto work = [&](int w) {
+        cudaError_t e = cudaSetDevice(dev);
+        uint8_t* st = m->stage[w];
+        bool pending = false;
+        for (size_t c = (size_t)w; c < chunks.size() && e == cudaSuccess; c += LOAD_WORKERS) {
+            const LoadChunk& k = chunks[c];
+            const LoadPiece& p = *k.p;
+            if (pending) e = cudaEventSynchronize(m->stage_ev[w]);
+            if (e != cudaSuccess) break;
+            const long stride = p.rows > 1 ? pad16(p.rb) : p.rb;
+            size_t len;
+            uint8_t* dst;
+            // the chunk's source bytes are contiguous: bytes [a, b), or rows [a, b) of rb bytes
+            const long s0 = stride == p.rb ? k.a : k.a * p.rb;
+            const size_t raw = (size_t)(stride == p.rb ? k.b - k.a : (k.b - k.a) * p.rb);
+            if (fd >= 0) {
+                size_t got = 0;
+                while (got < raw) {
+                    const ssize_t r = pread(fd, st + got, raw - got, (off_t)(p.src - base + s0 + (long)got));
+                    if (r <= 0) break;
+                    got += (size_t)r;
+                }
+                if (got != raw) {
+                    e = cudaErrorInvalidValue;
+                    break;
+                }
+            } else {
+                memcpy(st, p.src + s0, raw);
+            }
+            if (stride == p.rb) {
+                len = raw;
+                dst = m->arena + p.off + k.a;
+            } else {  // spread the rows to the padded stride, last row first (in place)
+                for (long r = k.b - k.a - 1; r >= 0; --r) {
+                    memmove(st + r * stride, st + r * p.rb, (size_t)p.rb);
+                    memset(st + r * stride + p.rb, 0, (size_t)(stride - p.rb));
+                }
+                len = (size_t)((k.b - k.a) * stride);
+                dst = m->arena + p.off + k.a * stride;
+            }
+            e = cudaMemcpyAsync(dst, st, len, cudaMemcpyHostToDevice, m->stage_st[w]);
+            if (e == cudaSuccess) e = cudaEventRecord(m->stage_ev[w], m->stage_st[w]);
+            pending = true;
+        }
+        const cudaError_t e2 = cudaStreamSynchronize(m->stage_st[w]);
+        err[w] = e != cudaSuccess ? e : e2;
+    };
+    std::vector<std::thread> th;
+    for (int w = 1; w < LOAD_WORKERS; ++w) th.emplace_back(work, w);
+    work(0);
+    for (auto& t : th) t.join();
+    for (int w = 0; w < LOAD_WORKERS; ++w) ECHK(err[w], "model_load: upload");
+    return GTN_OK;
+}
+
+}  // namespace gtn
+
+extern "C" {
+
+static int load_image(gtn_model* m, const void* host_image, size_t nbytes, int fd);
+
+// load_from_ckpt from a path (the reference opens the .gten file itself, utils.cpp:29-61): the
+// file is mapped to parse the record headers; the payload bytes are read from the file straight
+// into the pinned upload buffers.
+int gtn_model_load_file(gtn_model* m, const char* path) {
+    if (!m || !path) return fail(GTN_ERR_ARG, "model_load_file: arguments");
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) return fail(GTN_ERR_ARG, "model_load_file: cannot open %s", path);
+    struct stat sb;
+    if (fstat(fd, &sb) != 0 || sb.st_size < 8) {
+        close(fd);
+        return fail(GTN_ERR_FORMAT, "model_load_file: %s is not a .gten file", path);
+    }
+    const size_t n = (size_t)sb.st_size;
+    void* map = mmap(nullptr, n, PROT_READ, MAP_PRIVATE, fd, 0);
+    if (map == MAP_FAILED) {
+        close(fd);
+        return fail(GTN_ERR_ARG, "model_load_file: cannot map %s", path);
+    }
+    const int rc = load_image(m, map, n, fd);
+    munmap(map, n);
+    close(fd);
+    return rc;
+}
+
 // load_from_ckpt: tinyllama.cpp:195-251, zephyr.cpp:79-150, minicpm.cpp:113-166, openelm.cpp:201-262.
 int gtn_model_load(gtn_model* m, const void* host_image, size_t nbytes) {
+    return load_image(m, host_image, nbytes, -1);
+}
+
+static int load_image(gtn_model* m, const void* host_image, size_t nbytes, int fd) {
     if (!m || !host_image) return fail(GTN_ERR_ARG, "model_load: arguments");
     const uint8_t* img = (const uint8_t*)host_image;
     int64_t magic = 0;
@@ -284,8 +438,7 @@ int gtn_model_load(gtn_model* m, const void* host_image, size_t nbytes) {
     const int d = m->d, wdt = m->wdt, dh = m->dh;
     const bool fam1 = m->family == 1, fam3 = m->family == 3;
     // First pass: locate records and size the arena.
-    struct Piece { const uint8_t* src; long rows; long rb; long off; };
-    std::vector<Piece> pieces;
+    std::vector<LoadPiece> pieces;
     long off = 0;
     auto place = [&](const uint8_t* src, long rows, long rb) -> long {
         const long o = off;
@@ -358,21 +511,19 @@ int gtn_model_load(gtn_model* m, const void* host_image, size_t nbytes) {
     const long nfb_off = fam1 ? place(nfb, 1, 2L * d) : -1;
     const long lmh_off = lmh ? place(lmh, m->n_vocab, rbd) : -1;
 
-    if (m->arena) {
+    m->loaded = false;
+    if (m->arena && m->arena_bytes < (size_t)off) {  // a reload of the same model reuses the arena
         cudaFree(m->arena);
         m->arena = nullptr;
-        m->loaded = false;
     }
-    ECHK(cudaMalloc((void**)&m->arena, (size_t)off), "model_load: arena");
-    m->arena_bytes = (size_t)off;
-    ECHK(cudaMemset(m->arena, 0, (size_t)off), "model_load: arena clear");
-    for (const Piece& p : pieces) {
-        if (pad16(p.rb) == p.rb || p.rows == 1)
-            ECHK(cudaMemcpy(m->arena + p.off, p.src, (size_t)(p.rows * p.rb), cudaMemcpyHostToDevice), "model_load");
-        else
-            ECHK(cudaMemcpy2D(m->arena + p.off, (size_t)pad16(p.rb), p.src, (size_t)p.rb, (size_t)p.rb,
-                              (size_t)p.rows, cudaMemcpyHostToDevice),
-                 "model_load");
+    if (!m->arena) {
+        ECHK(cudaMalloc((void**)&m->arena, (size_t)off), "model_load: arena");
+        m->arena_bytes = (size_t)off;
+    }
+    ECHK(cudaMemsetAsync(m->arena, 0, (size_t)off, m->st), "model_load: arena clear");
+    {
+        const int rc = upload_pieces(m, pieces, fd, img);
+        if (rc != GTN_OK) return rc;
     }
     uint8_t* A = m->arena;
     m->emb = A + emb_off;

@@ -54,6 +54,7 @@ def lib() -> C.CDLL:
         L.gtn_model_free.argtypes = [C.c_void_p]
         L.gtn_model_n_vocab.argtypes = [C.c_void_p]
         L.gtn_model_load.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t]
+        L.gtn_model_load_file.argtypes = [C.c_void_p, C.c_char_p]
         L.gtn_model_logits.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
         L.gtn_model_generate.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
         L.gtn_model_generate_device.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
@@ -270,6 +271,10 @@ class Model:
         arr = np.frombuffer(image, np.uint8) if isinstance(image, (bytes, bytearray, memoryview)) else image
         arr = np.ascontiguousarray(arr, np.uint8)
         _check(lib().gtn_model_load(self._h, arr.ctypes.data, arr.size), "model_load")
+
+    def load_file(self, path: str) -> None:
+        """load_from_ckpt from a .gten file path."""
+        _check(lib().gtn_model_load_file(self._h, os.fsencode(path)), "model_load_file")
 
     def logits(self, tokens, start_pos: int):
         import numpy as np

@@ -91,6 +91,29 @@ def test_load_rejects_bad_images(orc, gpu):
     m.close()
 
 
+@pytest.mark.parametrize("name", ["llama", "minicpm"])
+def test_load_file_matches_load(orc, gpu, name, tmp_path):
+    """gtn_model_load_file (mapped .gten file) gives the same model as gtn_model_load from memory,
+    including the padded-row records (MiniCPM's down projection rows are not 16-byte multiples);
+    a reload replaces the weights."""
+    dims = CUSTOM[name]
+    img = gtenfile.synthetic_image(6, Q8, 5, cpu_pack(orc), dims=dims, std=0.05, gain_std=0.1)
+    other = gtenfile.synthetic_image(6, Q8, 6, cpu_pack(orc), dims=dims, std=0.05, gain_std=0.1)
+    path = tmp_path / "m.gten"
+    img.tofile(path)
+    prompt = np.random.default_rng(8).integers(0, dims[0], 11).astype(np.int32)
+    a = G.Model(G.CUSTOM, Q8, 40, dims=dims)
+    a.load(img)
+    b = G.Model(G.CUSTOM, Q8, 40, dims=dims)
+    b.load(other)
+    b.load_file(str(path))
+    assert np.array_equal(a.generate(prompt, 6), b.generate(prompt, 6))
+    with pytest.raises(G.GtenError):
+        b.load_file(str(tmp_path / "missing.gten"))
+    a.close()
+    b.close()
+
+
 GOLDEN = os.path.join(HERE, "golden", "greedy_tokens.json")
 
 
