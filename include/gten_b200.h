@@ -214,6 +214,22 @@ int gtn_model_generate_batch(gtn_model* m, const int32_t* prompts, int batch, in
  * the device; gtn_model_check reports violations. */
 int gtn_model_generate_device(gtn_model* m, const int32_t* prompt, int n_prompt, int n_gen, int32_t* out_tokens);
 
+/* Continuous batching over the model's max_batch slots (greedy; Q8/Q4 models of the TinyLlama,
+ * Zephyr and MiniCPM families). The reference decodes one sequence per greedy_sample call
+ * (sampler.cpp:11-53); here sequences of any prompt length join and leave a running batch:
+ *   gtn_slot_start   prefills a prompt (host int32) into a free slot, returns the slot and the
+ *                    first greedy id; fails when every slot is busy;
+ *   gtn_slots_step   one decode step of every busy slot (one captured CUDA graph over all slots;
+ *                    idle slots are skipped on the device); ids (host, max_batch entries) receive
+ *                    each busy slot's next id, -1 for idle slots; a slot whose last token sits at
+ *                    position max_ctx - 1 must be finished first;
+ *   gtn_slot_finish  frees a slot.
+ * Every sequence gets exactly the ids it gets alone. While slots are busy, gtn_model_logits and
+ * gtn_model_generate* refuse to run (they reuse the slots' rows). Synchronous. */
+int gtn_slot_start(gtn_model* m, const int32_t* prompt, int n_prompt, int* slot, int32_t* first_id);
+int gtn_slots_step(gtn_model* m, int32_t* ids);
+int gtn_slot_finish(gtn_model* m, int slot);
+
 /* The cudaStream_t the model enqueues its work on. */
 void* gtn_model_stream(gtn_model* m);
 

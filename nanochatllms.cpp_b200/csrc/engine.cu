@@ -84,6 +84,13 @@ struct gtn_model {
     float graph_temp = 0.0f;
     int graph_topk = 0;
     int* pos_host = nullptr;  // pinned staging for position uploads
+    // continuous batching: slot s holds one sequence between gtn_slot_start and gtn_slot_finish;
+    // active[] (device, staged in active_host) tells the decode step which slots to run
+    int* active = nullptr;
+    int* active_host = nullptr;
+    std::vector<int> slot_pos;  // host: position of each active slot's last token (-1: free)
+    bool slot_mode = false;     // the captured step runs every slot under the active mask
+    bool graph_slots = false;
     // pinned staging of the model upload (allocated by the first load): one buffer, event and
     // stream per upload worker
     uint8_t* stage[8] = {};
@@ -253,6 +260,12 @@ int gtn_model_create(int kind, int wdtype, int max_ctx, int max_batch, const int
         rc |= dalloc(m.get(), &m->ygu, sizeof(float) * B * m->ldgu);
         rc |= dalloc(m.get(), &m->yd, sizeof(float) * B * m->d);
         if (rc == GTN_OK && cudaMallocHost((void**)&m->pos_host, sizeof(int) * B) != cudaSuccess) rc = GTN_ERR_OOM;
+        rc |= dalloc(m.get(), &m->active, sizeof(int) * B);
+        if (rc == GTN_OK && cudaMallocHost((void**)&m->active_host, sizeof(int) * B) != cudaSuccess) rc = GTN_ERR_OOM;
+        if (rc == GTN_OK) {
+            for (int b = 0; b < B; ++b) m->active_host[b] = 0;
+            m->slot_pos.assign(B, -1);
+        }
     }
     if (rc == GTN_OK && m->rd > 0) {
         auto tab = rope_table_host(max_ctx, m->rd);
@@ -275,6 +288,7 @@ void gtn_model_free(gtn_model* m) {
     if (m->st) cudaStreamSynchronize(m->st);
     if (m->graph) cudaGraphExecDestroy(m->graph);
     if (m->pos_host) cudaFreeHost(m->pos_host);
+    if (m->active_host) cudaFreeHost(m->active_host);
     for (int i = 0; i < 8; ++i) {
         if (m->stage[i]) cudaFreeHost(m->stage[i]);
         if (m->stage_ev[i]) cudaEventDestroy(m->stage_ev[i]);
@@ -778,9 +792,11 @@ static int decode_step(gtn_model* m, int B, bool dry) {
         e = (expr);                                           \
         if (e != cudaSuccess) return cuda_st(e, #expr);       \
     } while (0)
+    const int* act_mask = m->slot_mode ? m->active : nullptr;
     FArgs base{};
     base.B = B;
     base.pos = m->pos;
+    base.active = act_mask;
     base.adt = adt;
     base.err = err;
     for (int l = 0; l < m->nl; ++l) {
@@ -806,7 +822,7 @@ static int decode_step(gtn_model* m, int B, bool dry) {
         at.y = m->yqkv; at.ys = m->ldqkv; at.bq = Ly.bq; at.bk = Ly.bk; at.bv = Ly.bv;
         at.cs = m->rope; at.half = m->rd / 2; at.kc = Ly.kc; at.vc = Ly.vc; at.kvs = m->kv_rs;
         at.khs = (long)m->max_ctx * m->kv_rs; at.seq_stride = (long)Ly.nkv * at.khs;
-        at.out = m->datt; at.os = row_bytes(adt, m->max_q); at.err = err;
+        at.out = m->datt; at.os = row_bytes(adt, m->max_q); at.err = err; at.active = act_mask;
         const size_t asm_ = fattn_smem(m->max_ctx, adt, dh);
         if (dry) {
             SK(ensure_smem(k_fattn, asm_));
@@ -846,7 +862,8 @@ static int decode_step(gtn_model* m, int B, bool dry) {
             SK(launch_topk_sample(st, m->logits, m->n_vocab, m->s_temp, m->s_topk, m->s_mt, sample_dst(m, err)));
         else
             SK(launch_pdl(k_fargmax, dim3(B), dim3(1024), 0, st, (const float*)m->logits, (long)m->n_vocab,
-                          m->n_vocab, m->tok, m->gen, (long)m->max_ctx + 1, m->pos, m->max_ctx + 1, err));
+                          m->n_vocab, m->tok, m->gen, (long)m->max_ctx + 1, m->pos, m->max_ctx + 1, err, act_mask,
+                          m->slot_mode ? m->next : (int32_t*)nullptr));
     }
 #undef SK
     return GTN_OK;
@@ -855,7 +872,7 @@ static int decode_step(gtn_model* m, int B, bool dry) {
 // Captures decode_step(B) into a CUDA graph (once per B) and launches it.
 static int run_step(gtn_model* m, int B) {
     if (!m->graph || m->graph_B != B || m->graph_mt != m->s_mt || m->graph_temp != m->s_temp ||
-        m->graph_topk != m->s_topk) {
+        m->graph_topk != m->s_topk || m->graph_slots != m->slot_mode) {
         if (m->graph) {
             cudaGraphExecDestroy(m->graph);
             m->graph = nullptr;
@@ -876,6 +893,7 @@ static int run_step(gtn_model* m, int B) {
         cudaGraphDestroy(g);
         ECHK(ei, "graph instantiate");
         m->graph_B = B;
+        m->graph_slots = m->slot_mode;
         m->graph_mt = m->s_mt;
         m->graph_temp = m->s_temp;
         m->graph_topk = m->s_topk;
@@ -899,6 +917,7 @@ static int set_positions(gtn_model* m, int B, int p) {
 // the last row's logits), the greedy pick, then n_gen-1 fused decode steps replayed from a CUDA
 // graph. The generated ids land in m->gen[b*max_ctx + n_prompt + i].
 static int generate_fused(gtn_model* m, int B, int n_prompt, int n_gen) {
+    m->slot_mode = false;
     for (int b = 0; b < B; ++b) {
         const int rc = forward(m, b, n_prompt, 0);
         if (rc != GTN_OK) return rc;
@@ -912,7 +931,7 @@ static int generate_fused(gtn_model* m, int B, int n_prompt, int n_gen) {
     } else {
         ECHK(launch_pdl(k_fargmax, dim3(B), dim3(1024), 0, m->st, (const float*)m->logits, (long)m->n_vocab,
                         m->n_vocab, m->tok, m->gen, (long)m->max_ctx + 1, m->pos, m->max_ctx + 1,
-                        device_error_word()),
+                        device_error_word(), (const int*)nullptr, (int32_t*)nullptr),
              "first token");
     }
     for (int i = 1; i < n_gen; ++i) {
@@ -949,6 +968,13 @@ static int generate_dev(gtn_model* m, int n_prompt, int n_gen, int32_t* out) {
     return GTN_OK;
 }
 
+// Sequences started with gtn_slot_start and not finished own their slots' KV rows and positions.
+static bool slots_busy(const gtn_model* m) {
+    for (int p : m->slot_pos)
+        if (p >= 0) return true;
+    return false;
+}
+
 }  // namespace gtn
 
 extern "C" {
@@ -956,6 +982,7 @@ extern "C" {
 int gtn_model_logits(gtn_model* m, const int32_t* tokens, int n_tokens, int start_pos, float* logits) {
     if (!m || !m->loaded || !tokens || !logits) return fail(GTN_ERR_ARG, "model_logits: arguments");
     if (n_tokens > m->max_ctx) return fail(GTN_ERR_ARG, "model_logits: %d tokens exceed max_ctx %d", n_tokens, m->max_ctx);
+    if (slots_busy(m)) return fail(GTN_ERR_ARG, "model_logits: slots are in use (gtn_slot_finish them first)");
     if (start_pos < 0 || start_pos >= n_tokens) return fail(GTN_ERR_ARG, "model_logits: start_pos");
     for (int i = 0; i < n_tokens; ++i)
         if (tokens[i] < 0 || tokens[i] >= m->n_vocab) return fail(GTN_ERR_ARG, "model_logits: token id %d", tokens[i]);
@@ -971,6 +998,7 @@ int gtn_model_generate(gtn_model* m, const int32_t* prompt, int n_prompt, int n_
     if (!m || !m->loaded || !prompt || !out_tokens || n_prompt <= 0 || n_gen <= 0)
         return fail(GTN_ERR_ARG, "model_generate: arguments");
     if (n_prompt + n_gen - 1 > m->max_ctx) return fail(GTN_ERR_ARG, "model_generate: exceeds max_ctx");
+    if (slots_busy(m)) return fail(GTN_ERR_ARG, "model_generate: slots are in use (gtn_slot_finish them first)");
     for (int i = 0; i < n_prompt; ++i)
         if (prompt[i] < 0 || prompt[i] >= m->n_vocab) return fail(GTN_ERR_ARG, "model_generate: token id %d", prompt[i]);
     ECHK(cudaMemcpyAsync(m->tok, prompt, sizeof(int32_t) * n_prompt, cudaMemcpyHostToDevice, m->st), "prompt");
@@ -1016,6 +1044,7 @@ int gtn_model_generate_batch(gtn_model* m, const int32_t* prompts, int batch, in
         return fail(GTN_ERR_ARG, "model_generate_batch: arguments");
     if (batch > m->max_batch) return fail(GTN_ERR_ARG, "model_generate_batch: batch %d > max_batch %d", batch, m->max_batch);
     if (n_prompt + n_gen - 1 > m->max_ctx) return fail(GTN_ERR_ARG, "model_generate_batch: exceeds max_ctx");
+    if (slots_busy(m)) return fail(GTN_ERR_ARG, "model_generate_batch: slots are in use");
     if (!m->fused) return fail(GTN_ERR_ARG, "model_generate_batch: needs Q8/Q4 weights of the TinyLlama, Zephyr or MiniCPM family");
     for (long i = 0; i < (long)batch * n_prompt; ++i)
         if (prompts[i] < 0 || prompts[i] >= m->n_vocab) return fail(GTN_ERR_ARG, "model_generate_batch: token id %d", prompts[i]);
@@ -1036,8 +1065,80 @@ int gtn_model_generate_device(gtn_model* m, const int32_t* prompt, int n_prompt,
     if (!m || !m->loaded || !prompt || !out_tokens || n_prompt <= 0 || n_gen <= 0)
         return fail(GTN_ERR_ARG, "model_generate_device: arguments");
     if (n_prompt + n_gen - 1 > m->max_ctx) return fail(GTN_ERR_ARG, "model_generate_device: exceeds max_ctx");
+    if (slots_busy(m)) return fail(GTN_ERR_ARG, "model_generate_device: slots are in use");
     ECHK(cudaMemcpyAsync(m->tok, prompt, sizeof(int32_t) * n_prompt, cudaMemcpyDeviceToDevice, m->st), "prompt");
     return generate_dev(m, n_prompt, n_gen, out_tokens);
+}
+
+int gtn_slot_start(gtn_model* m, const int32_t* prompt, int n_prompt, int* slot, int32_t* first_id) {
+    if (!m || !m->loaded || !prompt || n_prompt <= 0 || !slot) return fail(GTN_ERR_ARG, "slot_start: arguments");
+    if (!m->fused) return fail(GTN_ERR_ARG, "slot_start: needs Q8/Q4 weights of the TinyLlama, Zephyr or MiniCPM family");
+    if (n_prompt > m->max_ctx) return fail(GTN_ERR_ARG, "slot_start: %d prompt tokens exceed max_ctx %d", n_prompt, m->max_ctx);
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= m->n_vocab) return fail(GTN_ERR_ARG, "slot_start: token id %d", prompt[i]);
+    int s = -1;
+    for (int b = 0; b < m->max_batch && s < 0; ++b)
+        if (m->slot_pos[b] < 0) s = b;
+    if (s < 0) return fail(GTN_ERR_ARG, "slot_start: all %d slots are busy", m->max_batch);
+    const long ts = m->max_ctx + 1;
+    ECHK(cudaMemcpyAsync(m->tok + (long)s * ts, prompt, sizeof(int32_t) * n_prompt, cudaMemcpyHostToDevice, m->st),
+         "slot_start: prompt");
+    int rc = forward(m, s, n_prompt, 0);  // the prompt's KV rows of slot s and its last logits
+    if (rc != GTN_OK) return rc;
+    m->pos_host[s] = n_prompt - 1;
+    ECHK(cudaMemcpyAsync(m->pos + s, m->pos_host + s, sizeof(int), cudaMemcpyHostToDevice, m->st), "slot_start");
+    ECHK(launch_pdl(k_fargmax, dim3(1), dim3(1024), 0, m->st, (const float*)(m->logits + (long)s * m->n_vocab),
+                    (long)m->n_vocab, m->n_vocab, m->tok + (long)s * ts, m->gen + (long)s * ts, ts, m->pos + s,
+                    m->max_ctx + 1, device_error_word(), (const int*)nullptr, m->next + s),
+         "slot_start: first token");
+    int32_t id = 0;
+    ECHK(cudaMemcpyAsync(&id, m->next + s, sizeof(int32_t), cudaMemcpyDeviceToHost, m->st), "slot_start");
+    ECHK(cudaStreamSynchronize(m->st), "slot_start");
+    rc = check_dev_err();
+    if (rc != GTN_OK) return rc;
+    m->slot_pos[s] = n_prompt;
+    *slot = s;
+    if (first_id) *first_id = id;
+    return GTN_OK;
+}
+
+int gtn_slots_step(gtn_model* m, int32_t* ids) {
+    if (!m || !m->loaded || !ids) return fail(GTN_ERR_ARG, "slots_step: arguments");
+    if (!m->fused) return fail(GTN_ERR_ARG, "slots_step: needs Q8/Q4 weights of the TinyLlama, Zephyr or MiniCPM family");
+    int nact = 0;
+    for (int b = 0; b < m->max_batch; ++b) {
+        const int p = m->slot_pos[b];
+        m->active_host[b] = p >= 0;
+        if (p < 0) continue;
+        ++nact;
+        if (p >= m->max_ctx) return fail(GTN_ERR_ARG, "slots_step: slot %d has reached max_ctx %d", b, m->max_ctx);
+    }
+    for (int b = 0; b < m->max_batch; ++b) ids[b] = -1;
+    if (nact == 0) return GTN_OK;
+    ECHK(cudaMemcpyAsync(m->active, m->active_host, sizeof(int) * m->max_batch, cudaMemcpyHostToDevice, m->st),
+         "slots_step: mask");
+    m->slot_mode = true;
+    int rc = run_step(m, m->max_batch);
+    if (rc != GTN_OK) return rc;
+    ECHK(cudaMemcpyAsync(m->pos_host, m->next, sizeof(int32_t) * m->max_batch, cudaMemcpyDeviceToHost, m->st),
+         "slots_step: ids");
+    ECHK(cudaStreamSynchronize(m->st), "slots_step");
+    rc = check_dev_err();
+    if (rc != GTN_OK) return rc;
+    for (int b = 0; b < m->max_batch; ++b) {
+        if (m->slot_pos[b] < 0) continue;
+        ids[b] = m->pos_host[b];
+        ++m->slot_pos[b];
+    }
+    return GTN_OK;
+}
+
+int gtn_slot_finish(gtn_model* m, int slot) {
+    if (!m || slot < 0 || slot >= m->max_batch) return fail(GTN_ERR_ARG, "slot_finish: slot %d", slot);
+    if (m->slot_pos[slot] < 0) return fail(GTN_ERR_ARG, "slot_finish: slot %d is not in use", slot);
+    m->slot_pos[slot] = -1;
+    m->active_host[slot] = 0;
+    return GTN_OK;
 }
 
 void* gtn_model_stream(gtn_model* m) { return m ? (void*)m->st : nullptr; }

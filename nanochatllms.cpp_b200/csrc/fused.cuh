@@ -52,6 +52,7 @@ enum { PRO_COPY = 0, PRO_RESNORM = 1, PRO_SWIGLU = 2 };
 struct FArgs {
     int B;              // sequences in this launch (rows of the activation)
     const int* pos;     // [B] absolute position of each sequence's new token
+    const int* active;  // [B] 0: an idle slot, skipped (its rows are not used); null: all active
     int adt;            // activation dtype (Q8 / F16)
     int K;              // activation width (GEMV input)
     // PRO_COPY: activation rows in global memory
@@ -450,6 +451,8 @@ __device__ __forceinline__ float resnorm_block(const FArgs& a, int blk, int lane
 }
 
 static __global__ void __launch_bounds__(PCL_THREADS) k_prep_cl(const FArgs a, uint8_t* act, long act_s) {
+    // an idle slot: the whole cluster (one sequence) leaves before its first cluster barrier
+    if (a.active && !__ldcg(a.active + blockIdx.y)) return;
     namespace cg = cooperative_groups;
     cg::cluster_group cl = cg::this_cluster();
     extern __shared__ float sv[];  // the row at global element indices, then K ints of scratch
@@ -584,6 +587,7 @@ static __global__ void __launch_bounds__(1024) k_prep_swiglu(const FArgs a, uint
 struct AArgs {
     int adt, q_heads, kv_heads, d;          // d = head size (64)
     const int* pos;                          // [B]
+    const int* active;                       // [B] 0: idle slot (no cache write), or null
     const float* y; long ys;                 // stacked q|k|v fp32 rows
     const uint16_t *bq, *bk, *bv;            // Zephyr biases (or null)
     const float2* cs; int half;              // RoPE table [pos][half] (cos, sin), half = rd/2
@@ -608,6 +612,7 @@ static __global__ void __launch_bounds__(ATT_THREADS) k_fattn(const AArgs a) {
     __shared__ __align__(8) uint64_t bars[2];
     __shared__ int abort_flag;
     const int h = blockIdx.x, b = blockIdx.y;
+    if (a.active && !__ldcg(a.active + b)) return;  // an idle slot: no cache row, no output
     const int group = a.q_heads / a.kv_heads, g = h / group;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int d = a.d, nbh = d / GTN_QBLK;
@@ -676,9 +681,11 @@ static __global__ void __launch_bounds__(ATT_THREADS) k_fattn(const AArgs a) {
 inline size_t fattn_smem(int n, int adt, int d) { return attn_smem(n, adt, d); }
 
 // Greedy pick per sequence (sampler.cpp:30-41) + the decode loop's bookkeeping: the id becomes the
-// input token of the next position and is recorded; the position advances. grid B; block 1024.
+// input token of the next position and is recorded (and copied to next[b] if next is set); the
+// position advances. Idle slots (active[b] == 0) are skipped. grid B; block 1024.
 static __global__ void k_fargmax(const float* logits, long ls, int n, int32_t* tok, int32_t* gen, long tok_s,
-                                 int* pos, int max_ctx, unsigned int* err) {
+                                 int* pos, int max_ctx, unsigned int* err, const int* active, int32_t* next) {
+    if (active && !__ldcg(active + blockIdx.x)) return;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     __shared__ float bv[1024];
     __shared__ int bi[1024];
@@ -704,6 +711,7 @@ static __global__ void k_fargmax(const float* logits, long ls, int n, int32_t* t
     }
     if (t == 0) {
         const int id = bi[0] == 0x7fffffff ? 0 : bi[0];
+        if (next) next[b] = id;
         const int p = pos[b];
         if (p + 1 < max_ctx) {
             tok[(long)b * tok_s + p + 1] = id;

@@ -55,6 +55,9 @@ def lib() -> C.CDLL:
         L.gtn_model_n_vocab.argtypes = [C.c_void_p]
         L.gtn_model_load.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t]
         L.gtn_model_load_file.argtypes = [C.c_void_p, C.c_char_p]
+        L.gtn_slot_start.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int32)]
+        L.gtn_slots_step.argtypes = [C.c_void_p, C.c_void_p]
+        L.gtn_slot_finish.argtypes = [C.c_void_p, C.c_int]
         L.gtn_model_logits.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
         L.gtn_model_generate.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
         L.gtn_model_generate_device.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
@@ -263,6 +266,8 @@ class Model:
         if dims is not None:
             arr = (C.c_int32 * 7)(*dims)
         _check(lib().gtn_model_create(kind, wdtype, max_ctx, max_batch, arr, C.byref(self._h)), "model_create")
+        self.max_batch = max_batch
+        self.max_ctx = max_ctx
         self.n_vocab = lib().gtn_model_n_vocab(self._h)
 
     def load(self, image) -> None:
@@ -298,6 +303,25 @@ class Model:
         _check(lib().gtn_model_generate_topk(self._h, p.ctypes.data, p.size, n_gen, C.c_float(temp), top_k, rng._h,
                                              out.ctypes.data), "model_generate_topk")
         return out
+
+    # ---- continuous batching (gtn_slot_*)
+    def slot_start(self, prompt):
+        """Prefills prompt into a free slot; returns (slot, first greedy id)."""
+        import numpy as np
+        p = np.ascontiguousarray(prompt, np.int32)
+        slot, first = C.c_int(), C.c_int32()
+        _check(lib().gtn_slot_start(self._h, p.ctypes.data, p.size, C.byref(slot), C.byref(first)), "slot_start")
+        return slot.value, first.value
+
+    def slots_step(self):
+        """One decode step of every busy slot; returns max_batch ids (-1 for idle slots)."""
+        import numpy as np
+        out = np.empty(self.max_batch, np.int32)
+        _check(lib().gtn_slots_step(self._h, out.ctypes.data), "slots_step")
+        return out
+
+    def slot_finish(self, slot: int) -> None:
+        _check(lib().gtn_slot_finish(self._h, slot), "slot_finish")
 
     def generate_batch(self, prompts, n_gen: int):
         """prompts: [batch, n_prompt] int32 (host); returns [batch, n_gen] greedy ids."""

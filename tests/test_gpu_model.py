@@ -114,6 +114,58 @@ def test_load_file_matches_load(orc, gpu, name, tmp_path):
     b.close()
 
 
+@pytest.mark.parametrize("name", list(CUSTOM))
+@pytest.mark.parametrize("wdt", [Q8, Q4])
+def test_continuous_batching_matches_single_sequences(orc, gpu, name, wdt):
+    """Eleven requests of mixed prompt lengths and lengths of generation through 4 slots: requests
+    join the running batch as slots free up; each must get exactly the oracle's single-sequence
+    greedy ids."""
+    from gten_b200.serve import ContinuousBatcher
+    from oracle.oracle import OracleModel
+    dims = CUSTOM[name]
+    img = gtenfile.synthetic_image(6, wdt, 41, cpu_pack(orc), dims=dims, std=0.05, gain_std=0.1)
+    rng = np.random.default_rng(wdt * 7 + len(name))
+    m = G.Model(G.CUSTOM, wdt, 48, max_batch=4, dims=dims)
+    m.load(img)
+    b = ContinuousBatcher(m)
+    reqs = {}
+    for i in range(11):
+        p = rng.integers(0, dims[0], int(rng.integers(2, 28))).astype(np.int32)
+        n = int(rng.integers(1, 48 - p.size + 2)) if i % 3 else 1 + i
+        reqs[i] = (p, n)
+        b.submit(i, p, n)
+    res = b.run()
+    assert b.steps < sum(n for _, n in reqs.values())  # the steps were shared
+    for i, (p, n) in reqs.items():
+        om = OracleModel(orc, 6, wdt, 2 * (p.size + n), img, dims=dims)
+        assert res[i] == om.greedy(p, n).tolist(), f"request {i}"
+    m.close()
+
+
+def test_slot_api_errors(orc, gpu):
+    dims = CUSTOM["llama"]
+    img = gtenfile.synthetic_image(6, Q8, 2, cpu_pack(orc), dims=dims)
+    m = G.Model(G.CUSTOM, Q8, 16, max_batch=2, dims=dims)
+    m.load(img)
+    assert (m.slots_step() == -1).all()  # no busy slot: nothing runs
+    s0, _ = m.slot_start(np.arange(15, dtype=np.int32))
+    s1, _ = m.slot_start(np.array([1, 2], np.int32))
+    with pytest.raises(G.GtenError, match="busy"):
+        m.slot_start(np.array([3], np.int32))
+    with pytest.raises(G.GtenError, match="in use"):
+        m.generate(np.array([1, 2, 3], np.int32), 2)  # the slots own the rows
+    ids = m.slots_step()  # slot s0 processes position 15
+    assert ids[s0] >= 0 and ids[s1] >= 0
+    with pytest.raises(G.GtenError, match="max_ctx"):
+        m.slots_step()  # slot s0's last token now sits at position 16
+    m.slot_finish(s0)
+    with pytest.raises(G.GtenError):
+        m.slot_finish(s0)
+    m.slot_finish(s1)
+    assert m.generate(np.array([1, 2, 3], np.int32), 2).size == 2
+    m.close()
+
+
 GOLDEN = os.path.join(HERE, "golden", "greedy_tokens.json")
 
 
