@@ -374,6 +374,53 @@ def run_batch(args, rank, world, local):
     return res
 
 
+def run_serve(args):
+    """Continuous batching on TinyLlama: R requests, prompt lengths uniform in [16, 128] and new
+    tokens uniform in [32, 256] (seeded), through --slots slots (gten_b200.serve); then the same
+    requests one after another through gtn_model_generate (the reference's one-sequence loop).
+    Wall-clock over each whole run (both synchronous), generated tokens / s."""
+    import numpy as np
+    import torch
+
+    import gten_b200 as G
+    from gten_b200 import gtenfile
+    from gten_b200.serve import ContinuousBatcher
+    rng = np.random.default_rng(7)
+    reqs = [(rng.integers(0, 32000, int(rng.integers(16, 129))).astype(np.int32), int(rng.integers(32, 257)))
+            for _ in range(args.serve)]
+    max_ctx = 128 + 256
+    m = G.Model(G.TINYLLAMA, args.wdtype, max_ctx, max_batch=args.slots)
+    m.load(gtenfile.synthetic_image_device(G.TINYLLAMA, args.wdtype, SEED))
+    # warm-up: capture the slot step and the single-sequence step
+    b = ContinuousBatcher(m)
+    for i in range(min(args.slots, len(reqs))):
+        b.submit(i, reqs[i][0], 8)
+    b.run()
+    m.generate(reqs[0][0], 8)
+    torch.cuda.synchronize()
+    total = sum(n for _, n in reqs)
+    b = ContinuousBatcher(m)
+    for i, (p, n) in enumerate(reqs):
+        b.submit(i, p, n)
+    t0 = time.perf_counter()
+    res = b.run()
+    t_cb = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    same = 0
+    for i, (p, n) in enumerate(reqs):
+        same += int(np.array_equal(m.generate(p, n), res[i]))
+    t_seq = time.perf_counter() - t0
+    m.close()
+    return {"metric": "served tok/s (continuous batching)", "value": round(total / t_cb, 1), "unit": "tok/s",
+            "requests": len(reqs), "slots": args.slots, "generated_tokens": total,
+            "steps": b.steps, "mean_busy_slots": round(b.busy_slot_steps / max(b.steps, 1), 2),
+            "wall_s": round(t_cb, 3),
+            "sequential": {"value": round(total / t_seq, 1), "unit": "tok/s", "wall_s": round(t_seq, 3)},
+            "ids_equal_to_sequential": same,
+            "config": {"workload": f"TinyLlama-1.1B {WDT_NAMES[args.wdtype].upper()}, prompts U[16,128], "
+                                   f"new tokens U[32,256], greedy", "data": "synthetic"}}
+
+
 def run_load(args):
     """Model upload throughput: a TinyLlama image (host memory) through gtn_model_load, and the same
     bytes from a file (written first, so it is in the page cache) through gtn_model_load_file."""
@@ -465,6 +512,10 @@ def main():
     ap.add_argument("--batch", type=int, default=1,
                     help="global batch of sequences sharded over the ranks (default 1: the headline bs1 request)")
     ap.add_argument("--model", default="tinyllama", choices=sorted(BATCH_MODELS), help="with --batch > 1")
+    ap.add_argument("--serve", type=int, default=0, metavar="R",
+                    help="continuous batching: R requests of mixed prompt / generation lengths through "
+                         "--slots slots, against the same requests one at a time")
+    ap.add_argument("--slots", type=int, default=16, help="with --serve: decode slots (max_batch)")
     ap.add_argument("--load", action="store_true",
                     help="only time the model upload (gtn_model_load from host memory, gtn_model_load_file "
                          "from a file in the page cache)")
@@ -487,6 +538,9 @@ def main():
         return
     if args.load:
         print(json.dumps(run_load(args)), flush=True)
+        return
+    if args.serve:
+        print(json.dumps(run_serve(args)), flush=True)
         return
     if args.gemv_only:
         import torch
