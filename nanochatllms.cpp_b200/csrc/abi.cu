@@ -290,7 +290,25 @@ static cudaError_t launch_gm3(const uint8_t* X, long xs, int M, const uint8_t* W
                       ws, N, K, X, xs, M, Y, ldy, p.R, p.MT, p.MC, device_error_word());
 }
 
+// k_gemm_tc: 16-byte aligned weight rows, K a multiple of 32 * TC_G, at least TC_MIN_M rows.
+static bool tc_fits(const uint8_t* W, long ws, int M, int wdt, int K) {
+    if (M < TC_MIN_M || (wdt != GTN_Q8 && wdt != GTN_Q4) || K % GTN_QBLK) return false;
+    const int nb = K / GTN_QBLK;
+    return nb > 0 && nb % TC_G == 0 && ((reinterpret_cast<uintptr_t>(W) & 15) | (uintptr_t)(ws & 15)) == 0;
+}
+
+template <int WDT>
+static cudaError_t launch_tc(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y,
+                             long ldy, cudaStream_t st, bool dry) {
+    constexpr size_t smem = tc_smem<WDT>();
+    const cudaError_t e = ensure_smem(k_gemm_tc<WDT>, smem);
+    if (e != cudaSuccess || dry) return e;
+    return launch_pdl(k_gemm_tc<WDT>, dim3((N + TC_NT - 1) / TC_NT, (M + TC_MT - 1) / TC_MT), dim3(TC_THREADS), smem,
+                      st, W, ws, N, K, X, xs, M, Y, ldy, device_error_word());
+}
+
 bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K) {
+    if (tc_fits(W, ws, M, wdt, K)) return true;
     GM3Plan gp{};
     if (wdt == GTN_Q8) return gm3_plan<GTN_Q8>(W, ws, M, K, &gp);
     if (wdt == GTN_Q4) return gm3_plan<GTN_Q4>(W, ws, M, K, &gp);
@@ -299,6 +317,9 @@ bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K) {
 
 cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
                    long ldy, cudaStream_t st, bool dry) {
+    if (tc_fits(W, ws, M, wdt, K))
+        return wdt == GTN_Q8 ? launch_tc<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, st, dry)
+                             : launch_tc<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, st, dry);
     GM3Plan gp{};
     if (wdt == GTN_Q8 && gm3_plan<GTN_Q8>(W, ws, M, K, &gp))
         return launch_gm3<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, gp, st, dry);
@@ -310,6 +331,7 @@ cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, 
 static cudaError_t matmul_tma(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K,
                               float* Y, long ldy, cudaStream_t st) {
     if (gemv_q_fits(M, wdt, K)) return gemv_q(X, xs, M, W, ws, wdt, N, K, Y, ldy, st, false);
+    if (tc_fits(W, ws, M, wdt, K)) return gemm_q(X, xs, M, W, ws, wdt, N, K, Y, ldy, st, false);
     GM3Plan gp{};
     if (wdt == GTN_Q8 && gm3_plan<GTN_Q8>(W, ws, M, K, &gp)) return launch_gm3<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, gp, st);
     if (wdt == GTN_Q4 && gm3_plan<GTN_Q4>(W, ws, M, K, &gp)) return launch_gm3<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, gp, st);

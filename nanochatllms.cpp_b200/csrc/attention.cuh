@@ -36,7 +36,7 @@ __device__ __forceinline__ float head_dot(const uint8_t* q, const uint8_t* k, in
 #pragma unroll
                 for (int c = 0; c < GTN_QBLK; c += 8)
                     L += (int)x[c + 2 * l] * y[c + 2 * l] + (int)x[c + 2 * l + 1] * y[c + 2 * l + 1];
-                const float p = (float)L * s;
+                const float p = lane_sum_f32(L) * s;
                 acc[l] = acc[l] + p;
             }
         }
@@ -203,7 +203,7 @@ __device__ __forceinline__ float att_dot(const uint8_t* kr, const uint8_t* qraw,
             const float s = qp[b * 4].da * h2f(ld_u16(kb));
 #pragma unroll
             for (int l = 0; l < 4; ++l) {
-                const float pr = (float)q8_block_lane_dot(kb, l, qp[b * 4 + l]) * s;
+                const float pr = lane_sum_f32(q8_block_lane_dot(kb, l, qp[b * 4 + l])) * s;
                 acc[l] = acc[l] + pr;
             }
         }
@@ -235,7 +235,7 @@ __device__ __forceinline__ float att_dot_q8x2(const uint8_t* kr, const LanePrep*
             const int w0 = gv3_pair(w, ob + 2 + 2 * l, ob + 10 + 2 * l);
             const int w1 = gv3_pair(w, ob + 18 + 2 * l, ob + 26 + 2 * l);
             const LanePrep& a = qp[b * 4 + l];
-            const float pr = (float)dp4a(w0, a.a0, dp4a(w1, a.a1, 0)) * s;
+            const float pr = lane_sum_f32(dp4a(w0, a.a0, dp4a(w1, a.a1, 0))) * s;
             acc[l] = acc[l] + pr;
         }
     }

@@ -127,4 +127,11 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
+// float(L) for |L| < 2^22 (every block lane sum: at most 8 * 128 * 128 in magnitude), bit-identical
+// to the conversion instruction but on the full-rate integer and fp32 pipes: L + 0x4B400000 read as a
+// float is 1.5 * 2^23 + L exactly (the binade [2^23, 2^24) has unit spacing), and subtracting
+// 1.5 * 2^23 is exact. The conversion instruction issues at a fraction of the fp32 rate, and the
+// block epilogues convert one lane sum per 8 multiply-adds.
+__device__ __forceinline__ float lane_sum_f32(int L) { return __int_as_float(L + 0x4B400000) - 12582912.0f; }
+
 }  // namespace gtn

@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(NW * 32) k_fgemv(const FArgs a) {
                         const LanePrep av = prep[((size_t)m * nb + b0 + b) * 4 + l];
                         const int L = WDT == GTN_Q8 ? q8_block_lane_dot(p, l, av) : q4_block_lane_dot(p, l, av);
                         const float sc = av.da * dw;
-                        const float pr = (float)L * sc;
+                        const float pr = lane_sum_f32(L) * sc;
                         acc[m] = acc[m] + pr;
                     }
                 }

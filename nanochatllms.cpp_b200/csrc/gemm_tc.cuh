@@ -1,0 +1,399 @@
+// Exact Q8/Q4 GEMM on the 5th-generation tensor cores (tcgen05) for M >= 16 activation rows:
+// prefill and batched decode steps.
+//
+// Reference: ops.cpp:292-490 (vec_dot_product_q8, vec_dot_product_q8_q4) inside matmul_2d_impl
+// (ops.cpp:579-636). The reference keeps 4 fp32 lanes per dot product; lane l owns the elements
+// k of every 32-element block with (k % 8) / 2 == l, its int32 sum L over those 8 products is
+// converted to fp32, multiplied by fp32(da) * fp32(dw) and added to the lane, blocks in order;
+// the result is (L0 + L1) + (L2 + L3).
+//
+// Split of the work:
+//   * tensor cores: the exact integer lane sums. Q8 values (-128..127) and Q4 values (nibble - 7)
+//     are exact in fp16, every product is an integer below 2^15 and a lane sum of 8 of them stays
+//     below 2^18, so kind::f16 with fp32 accumulation returns L exactly. To get one lane per
+//     accumulator row, the activation tile is expanded 4x: row r = l * 32 + m of A' holds row m
+//     of the activations masked to lane l's elements (zeros elsewhere). One block (K = 32) is two
+//     MMAs (K = 16 each) into its own TMEM region of 128 lanes x 64 columns; D[l*32+m][n] = L.
+//   * CUDA cores: the reference's fp32 epilogue. Thread (warp w, lane m) reads TMEM lane quarter
+//     l = w % 4 (its own accumulator rows) and owns the chains (m, l, n) of 32 weight rows n; per
+//     block it computes s = da * dw, p = L * s and acc = acc + p, blocks in order, so every
+//     chain is the reference's. The four lane chains of an output meet in shared memory at the
+//     end for (L0 + L1) + (L2 + L3).
+//
+// Data movement: weight rows arrive raw (34/18-byte blocks, which are not TMA-tileable) by 1-D
+// bulk copies of 8 blocks per row into a 3-stage ring; the CUDA cores convert them into the
+// canonical K-major fp16 tile (8-row x 16-byte core matrices, no swizzle) the MMA reads, and the
+// activations into A' (only each row's lane words are written; the zeros are written once). Four
+// groups of 2 blocks are in flight (tile, TMEM and scale slots); converter warps, the MMA issue and
+// epilogue warps run as separate roles. Every wait is bounded (about 2 s of device time); on expiry
+// the kernel flags the device error word, waits (bounded) for its own copies and MMAs, frees its
+// TMEM and returns.
+#pragma once
+#include "common.cuh"
+
+namespace gtn {
+
+constexpr int TC_EPI_WARPS = 8;                  // epilogue warps: warp w reads TMEM lane quarter w % 4
+constexpr int TC_CONV_WARPS = 4;                 // converter warps (thread 0 also issues MMAs and copies)
+constexpr int TC_CONV_THREADS = 32 * TC_CONV_WARPS;
+constexpr int TC_THREADS = 32 * (TC_EPI_WARPS + TC_CONV_WARPS);
+constexpr int TC_MT = 32;                        // activation rows per CTA (x 4 lanes = 128 MMA rows)
+constexpr int TC_NT = 64;                        // weight rows per CTA (MMA N)
+constexpr int TC_G = 2;                          // blocks per group (one commit)
+constexpr int TC_S = 4;                          // groups in flight (tile / TMEM / scale slots)
+constexpr int TC_KB = 8;                         // blocks per raw weight chunk (one bulk copy per row)
+constexpr int TC_RS = 3;                         // raw chunk stages
+constexpr int TC_TMEM_COLS = TC_S * TC_G * TC_NT;  // 512 columns: the whole TMEM (one CTA per SM)
+constexpr int TC_ATILE = 128 * 64;               // expanded activation tile of one block: 128 rows x 32 fp16
+constexpr int TC_BTILE = TC_NT * 64;             // weight tile of one block: 64 rows x 32 fp16
+constexpr int TC_COMB_STRIDE = 65;               // floats per (lane, row) in the final combine (bank spread)
+
+template <int WDT>
+__host__ __device__ constexpr int tc_rstride() {
+    return ((TC_KB * (WDT == GTN_Q8 ? GTN_Q8_BYTES : GTN_Q4_BYTES) + 15) / 16) * 16;
+}
+template <int WDT>
+__host__ __device__ constexpr size_t tc_smem() {
+    return 1024 + (size_t)TC_S * TC_G * (TC_ATILE + TC_BTILE) + (size_t)TC_RS * TC_NT * tc_rstride<WDT>() +
+           (size_t)TC_S * TC_G * (TC_MT + TC_NT) * sizeof(float);
+}
+static_assert((size_t)4 * TC_MT * TC_COMB_STRIDE * sizeof(float) <= (size_t)TC_S * TC_G * TC_ATILE,
+              "the combine buffer reuses the activation tiles");
+static_assert(TC_TMEM_COLS <= 512, "TMEM has 512 columns");
+static_assert(TC_KB % TC_G == 0, "groups never straddle raw chunks");
+
+// Shared-memory matrix descriptor (tcgen05): K-major, no swizzle; LBO = bytes between the two
+// 16-byte K chunks of a core-matrix row group, SBO = bytes between 8-row groups; version 1.
+__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// Instruction descriptor: kind::f16, A = B = fp16, D = fp32, both K-major, M = 128, N = TC_NT.
+constexpr uint32_t TC_IDESC = (1u << 4) | ((uint32_t)(TC_NT >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(TC_IDESC), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Barrier 1 over the converter warps, returning the AND of every thread's `ok` (the same value in
+// all of them, so the converters always leave their loop together).
+__device__ __forceinline__ bool conv_bar_and(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 1, %2, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)ok), "n"(TC_CONV_THREADS)
+        : "memory");
+    return r != 0;
+}
+
+// Bounded mbarrier wait: at most about TC_WAIT_NS of device time (%globaltimer), then the device
+// error word is flagged and false returned.
+constexpr uint64_t TC_WAIT_NS = 2000000000ull;
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t phase, unsigned int* err) {
+    if (mbar_try_wait(bar, phase)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0; it < GTN_WAIT_LIMIT; ++it) {
+        if (mbar_try_wait(bar, phase)) return true;
+        if ((it & 255u) == 255u && globaltimer_ns() - t0 > TC_WAIT_NS) break;
+    }
+    if (err) atomicOr(err, GTN_DEVERR_TIMEOUT);
+    return false;
+}
+
+// 32 consecutive TMEM columns of this warp's lane quarter (one lane per thread), waited for.
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
+        "tcgen05.wait::ld.sync.aligned;\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// Four int8 (as bytes b0..b3 of x, each biased by `bias` so that it is 0..255) -> two fp16 pairs
+// of (byte - sub): 1024 + byte has the fp16 bits 0x6400 | byte, and subtracting 1024 + bias in fp16
+// is exact (both operands lie in [1024, 1280)).
+__device__ __forceinline__ uint2 tc_bytes_to_f16x4(uint32_t x, uint32_t sub2) {
+    const uint32_t lo = __byte_perm(x, 0x64646464u, 0x4140), hi = __byte_perm(x, 0x64646464u, 0x4342);
+    const __half2 s = *reinterpret_cast<const __half2*>(&sub2);
+    const __half2 a = __hsub2(*reinterpret_cast<const __half2*>(&lo), s);
+    const __half2 b = __hsub2(*reinterpret_cast<const __half2*>(&hi), s);
+    return make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+}
+
+// Y[m, n] (fp32, row stride y_stride) = dot(X[m, :], W[n, :]) for Q8 activations X and Q8/Q4
+// weights W, bit-identical to the reference. W: 16-byte aligned base and row stride, rows readable
+// up to the next 16-byte boundary; K / 32 a multiple of TC_G. grid (ceil(N / 64), ceil(M / 32)),
+// block TC_THREADS, dynamic shared memory tc_smem<WDT>(); one CTA per SM (it holds all of TMEM).
+//
+// Roles, synchronised only by mbarriers (no block-wide barrier inside the main loop):
+//   converter warps 8-11, group g in slot s = g % TC_S: wait until the epilogue released slot s
+//     (tmem_empty, group g - TC_S), write the activation lane words and the weight tile of the
+//     group's blocks, then barrier 1 among themselves; their thread 0 issues the group's MMAs
+//     into TMEM slot s and commits them to mma_done[s], and refills the raw weight ring.
+//   epilogue warps 0-7: wait mma_done[s], read the lane sums from TMEM, run the fp32 chains,
+//     release slot s (tmem_empty[s], 256 arrivals).
+template <int WDT>
+__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const uint8_t* __restrict__ W, long w_stride, int N, int K,
+                                                           const uint8_t* __restrict__ X, long x_stride, int M,
+                                                           float* __restrict__ Y, long y_stride, unsigned int* err) {
+    constexpr int BB = WDT == GTN_Q8 ? GTN_Q8_BYTES : GTN_Q4_BYTES;
+    constexpr int RSTR = tc_rstride<WDT>();
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem);  // [TC_RS]
+    uint64_t* mma_done = raw_full + TC_RS;                    // [TC_S]
+    uint64_t* tmem_empty = mma_done + TC_S;                   // [TC_S]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + TC_S);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    uint8_t* atile = smem + 1024;                             // [TC_S * TC_G][TC_ATILE]
+    uint8_t* btile = atile + TC_S * TC_G * TC_ATILE;          // [TC_S * TC_G][TC_BTILE]
+    uint8_t* raw = btile + TC_S * TC_G * TC_BTILE;            // [TC_RS][TC_NT][RSTR]
+    float* da_s = reinterpret_cast<float*>(raw + (size_t)TC_RS * TC_NT * RSTR);  // [TC_S][TC_G][TC_MT]
+    float* dw_s = da_s + TC_S * TC_G * TC_MT;                                    // [TC_S][TC_G][TC_NT]
+    float* comb = reinterpret_cast<float*>(atile);  // [4][TC_MT][TC_COMB_STRIDE], after the last MMA
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * TC_NT, nr = min(TC_NT, N - n0);
+    const int m0 = blockIdx.y * TC_MT, mr = min(TC_MT, M - m0);
+    const int nb = K / GTN_QBLK, ngroups = nb / TC_G, nchunks = (nb + TC_KB - 1) / TC_KB;
+    constexpr int CW0 = TC_EPI_WARPS;  // first converter warp
+
+    // raw chunk c (blocks [c*KB, c*KB + KB)) of the nr weight rows into stage c % TC_RS; one warp
+    auto issue_chunk = [&](int c) {
+        uint64_t* bar = &raw_full[c % TC_RS];
+        const int nblk = min(TC_KB, nb - c * TC_KB);
+        const uint32_t bytes = (uint32_t)((nblk * BB + 15) & ~15);
+        if (lane == 0) mbar_arrive_expect_tx(bar, bytes * (uint32_t)nr);
+        __syncwarp();
+        uint8_t* dst = raw + (size_t)(c % TC_RS) * TC_NT * RSTR;
+        for (int r = lane; r < nr; r += 32)
+            bulk_g2s(dst + (size_t)r * RSTR, W + (size_t)(n0 + r) * w_stride + (size_t)c * TC_KB * BB, bytes, bar);
+    };
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TC_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 32) {
+        for (int s = 0; s < TC_RS; ++s) mbar_init(&raw_full[s], 1);
+        for (int s = 0; s < TC_S; ++s) {
+            mbar_init(&mma_done[s], 1);
+            mbar_init(&tmem_empty[s], 32 * TC_EPI_WARPS);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    // the expanded activation tiles: zeros everywhere but the lane words written per block
+    for (int i = tid; i < TC_S * TC_G * TC_ATILE / 16; i += TC_THREADS)
+        reinterpret_cast<uint4*>(atile)[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (warp == CW0)
+        for (int c = 0; c < min(TC_RS, nchunks); ++c) issue_chunk(c);  // weights: independent of the previous kernel
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    float acc[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
+    int g_issued = 0, chunks_issued = min(TC_RS, nchunks);
+
+    if (warp >= CW0) {
+        // ---- converters (and the MMA / copy issue on converter warp 0) ----
+        const int ct = tid - 32 * CW0;
+        // activation lane words of group g: unit u -> (lane l, row m, chunk c, block)
+        auto act_word = [&](int g, int u) -> uint32_t {
+            const int l = u & 3, m = ((u >> 2) & 7) | (((u >> 7) & 3) << 3), c = (u >> 5) & 3, blk = u >> 9;
+            if (m >= mr) return 0u;
+            return (uint32_t)ld_u16(X + (long)(m0 + m) * x_stride + (long)(g * TC_G + blk) * GTN_Q8_BYTES + 2 + 8 * c +
+                                    2 * l);
+        };
+        auto act_scale = [&](int g) -> float {
+            const int m = ct % TC_MT, blk = ct / TC_MT;
+            return m < mr ? h2f(ld_u16(X + (long)(m0 + m) * x_stride + (long)(g * TC_G + blk) * GTN_Q8_BYTES)) : 0.0f;
+        };
+        constexpr int AU = TC_G * TC_MT * 16 / TC_CONV_THREADS;  // activation words per thread per group
+        constexpr int WU = TC_G * TC_NT * 8 / TC_CONV_THREADS;   // weight 4-element units per thread per group
+        uint32_t apf[AU];
+        float dapf = 0.0f;
+#pragma unroll
+        for (int i = 0; i < AU; ++i) apf[i] = act_word(0, ct + TC_CONV_THREADS * i);
+        if (ct < TC_G * TC_MT) dapf = act_scale(0);
+        for (int g = 0; g < ngroups; ++g) {
+            const int s = g % TC_S, chunk = (g * TC_G) / TC_KB, stage = chunk % TC_RS;
+            bool ok = *abort_flag == 0;
+            if (ok && g >= TC_S) ok = tc_wait(&tmem_empty[s], (uint32_t)(g / TC_S - 1) & 1u, err);
+            if (ok) {
+#pragma unroll
+                for (int i = 0; i < AU; ++i) {
+                    const int u = ct + TC_CONV_THREADS * i;
+                    const int l = u & 3, m = ((u >> 2) & 7) | (((u >> 7) & 3) << 3), c = (u >> 5) & 3, blk = u >> 9;
+                    const int r = l * 32 + m;
+                    const uint2 h = tc_bytes_to_f16x4(apf[i] ^ 0x8080u, 0x64806480u);  // (q + 128) - 1152
+                    *reinterpret_cast<uint32_t*>(atile + (size_t)(s * TC_G + blk) * TC_ATILE + (r >> 3) * 512 +
+                                                 c * 128 + (r & 7) * 16 + l * 4) = h.x;
+                }
+                if (ct < TC_G * TC_MT) da_s[s * TC_G * TC_MT + ct] = dapf;
+                if (g + 1 < ngroups) {  // the next group's activations, in flight meanwhile
+#pragma unroll
+                    for (int i = 0; i < AU; ++i) apf[i] = act_word(g + 1, ct + TC_CONV_THREADS * i);
+                    if (ct < TC_G * TC_MT) dapf = act_scale(g + 1);
+                }
+                ok = tc_wait(&raw_full[stage], (uint32_t)(chunk / TC_RS) & 1u, err);
+            }
+            if (ok) {
+                const uint8_t* rs = raw + (size_t)stage * TC_NT * RSTR;
+#pragma unroll
+                for (int i = 0; i < WU; ++i) {
+                    const int u = ct + TC_CONV_THREADS * i;
+                    const int kq = (u & 1) | (((u >> 4) & 3) << 1), n = ((u >> 1) & 7) | (((u >> 6) & 7) << 3);
+                    const int blk = u >> 9;
+                    uint2 h = make_uint2(0u, 0u);
+                    if (n < nr) {
+                        const uint8_t* bp = rs + (size_t)n * RSTR + (size_t)((g * TC_G + blk) % TC_KB) * BB + 2;
+                        if (WDT == GTN_Q8) {
+                            const uint32_t v = (uint32_t)ld_u16(bp + 4 * kq) | ((uint32_t)ld_u16(bp + 4 * kq + 2) << 16);
+                            h = tc_bytes_to_f16x4(v ^ 0x80808080u, 0x64806480u);  // (q + 128) - 1152
+                        } else {
+                            const int kb = 4 * (kq & 3);
+                            const uint32_t v = (uint32_t)ld_u16(bp + kb) | ((uint32_t)ld_u16(bp + kb + 2) << 16);
+                            const uint32_t nib = kq < 4 ? (v >> 4) & 0x0F0F0F0Fu : v & 0x0F0F0F0Fu;
+                            h = tc_bytes_to_f16x4(nib, 0x64076407u);  // nibble - 7
+                        }
+                    }
+                    *reinterpret_cast<uint2*>(btile + (size_t)(s * TC_G + blk) * TC_BTILE + (n >> 3) * 512 +
+                                              (kq >> 1) * 128 + (n & 7) * 16 + (kq & 1) * 8) = h;
+                }
+                for (int i = ct; i < TC_G * TC_NT; i += TC_CONV_THREADS) {
+                    const int blk = i / TC_NT, n = i % TC_NT;
+                    dw_s[s * TC_G * TC_NT + i] =
+                        n < nr ? h2f(ld_u16(rs + (size_t)n * RSTR + (size_t)((g * TC_G + blk) % TC_KB) * BB)) : 0.0f;
+                }
+                fence_async_smem();  // generic-proxy tile writes -> visible to the tensor cores
+            }
+            if (!conv_bar_and(ok)) {
+                *abort_flag = 1;
+                break;
+            }
+            if (warp == CW0) {
+                if (lane == 0) {
+                    tc_fence_after();
+#pragma unroll
+                    for (int blk = 0; blk < TC_G; ++blk) {
+                        const int t = s * TC_G + blk;
+                        const uint32_t a = smem_u32(atile + (size_t)t * TC_ATILE);
+                        const uint32_t b = smem_u32(btile + (size_t)t * TC_BTILE);
+                        const uint32_t d = tmem + (uint32_t)(t * TC_NT);
+                        tc_mma(d, tc_desc(a, 128, 512), tc_desc(b, 128, 512), 0u);
+                        tc_mma(d, tc_desc(a + 256, 128, 512), tc_desc(b + 256, 128, 512), 1u);
+                    }
+                    tc_commit(&mma_done[s]);
+                }
+                __syncwarp();
+                // this group ended its raw chunk: refill the stage with the chunk TC_RS ahead
+                if (((g + 1) * TC_G % TC_KB == 0 || g + 1 == ngroups) && chunk + TC_RS < nchunks) {
+                    issue_chunk(chunk + TC_RS);
+                    chunks_issued = chunk + TC_RS + 1;
+                }
+            }
+            g_issued = g + 1;
+        }
+    } else {
+        // ---- epilogue: thread (quarter q = reference lane l, column half, row m = lane) ----
+        const int q = warp & 3, half = warp >> 2;
+        for (int g = 0; g < ngroups; ++g) {
+            const int s = g % TC_S;
+            if (*abort_flag != 0 || !tc_wait(&mma_done[s], (uint32_t)(g / TC_S) & 1u, err)) {
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll 1
+            for (int blk = 0; blk < TC_G; ++blk) {
+                const int t = s * TC_G + blk;
+                float v[32];
+                tc_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * TC_NT + half * 32), v);
+                const float da = da_s[t * TC_MT + lane];
+                const float4* dw4 = reinterpret_cast<const float4*>(dw_s + t * TC_NT + half * 32);
+#pragma unroll
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    const float4 w = dw4[j4];
+                    const float s0 = da * w.x, s1 = da * w.y, s2 = da * w.z, s3 = da * w.w;
+                    const float p0 = v[4 * j4] * s0, p1 = v[4 * j4 + 1] * s1;
+                    const float p2 = v[4 * j4 + 2] * s2, p3 = v[4 * j4 + 3] * s3;
+                    acc[4 * j4] = acc[4 * j4] + p0;
+                    acc[4 * j4 + 1] = acc[4 * j4 + 1] + p1;
+                    acc[4 * j4 + 2] = acc[4 * j4 + 2] + p2;
+                    acc[4 * j4 + 3] = acc[4 * j4 + 3] + p3;
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tmem_empty[s]);
+        }
+    }
+    __syncthreads();
+    const bool ok = *abort_flag == 0;
+    if (ok) {
+        // (L0 + L1) + (L2 + L3): the four lane chains of each output meet in shared memory
+        if (warp < TC_EPI_WARPS) {
+            const int q = warp & 3, half = warp >> 2;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) comb[(q * TC_MT + lane) * TC_COMB_STRIDE + half * 32 + j] = acc[j];
+        }
+        __syncthreads();
+        for (int i = tid; i < TC_MT * TC_NT; i += TC_THREADS) {
+            const int m = i / TC_NT, n = i % TC_NT;
+            if (m < mr && n < nr) {
+                const float c0 = comb[(0 * TC_MT + m) * TC_COMB_STRIDE + n], c1 = comb[(1 * TC_MT + m) * TC_COMB_STRIDE + n];
+                const float c2 = comb[(2 * TC_MT + m) * TC_COMB_STRIDE + n], c3 = comb[(3 * TC_MT + m) * TC_COMB_STRIDE + n];
+                Y[(long)(m0 + m) * y_stride + n0 + n] = (c0 + c1) + (c2 + c3);
+            }
+        }
+    } else if (tid == 32 * CW0) {
+        // an expired wait: let this CTA's MMAs and copies finish (bounded) before its TMEM and
+        // shared memory are released; each slot / stage has at most one outstanding phase
+        for (int g2 = max(0, g_issued - TC_S); g2 < g_issued; ++g2)
+            tc_wait(&mma_done[g2 % TC_S], (uint32_t)(g2 / TC_S) & 1u, err);
+        for (int c = max(0, chunks_issued - TC_RS); c < chunks_issued; ++c)
+            tc_wait(&raw_full[c % TC_RS], (uint32_t)(c / TC_RS) & 1u, err);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+}
+
+}  // namespace gtn

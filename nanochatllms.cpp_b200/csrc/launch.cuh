@@ -7,6 +7,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "gemm_tc.cuh"
 #include "matmul.cuh"
 #include "rowops.cuh"
 
@@ -116,8 +117,10 @@ bool gemv_q_fits(int M, int wdt, int K);
 cudaError_t gemv_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
                    long ldy, cudaStream_t st, bool dry);
 
-// Exact GEMM (k_gemm3) for M >= 2 activation rows of Q8 against Q8 or Q4 weights (16-byte aligned
-// weight rows, same `padded` precondition); `dry` only configures shared memory.
+// Exact GEMM for M >= 2 activation rows of Q8 against Q8 or Q4 weights (16-byte aligned weight
+// rows, same `padded` precondition): the tensor-core kernel k_gemm_tc from TC_MIN_M rows on, else
+// k_gemm3 on the CUDA cores; `dry` only configures shared memory.
+constexpr int TC_MIN_M = 128;
 bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K);
 cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
                    long ldy, cudaStream_t st, bool dry);

@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(NW * 32) k_mm_q(const uint8_t* __restrict__ W,
                         const LanePrep a = prep[((size_t)m * nb + b0 + b) * 4 + l];
                         const int L = WDT == GTN_Q8 ? q8_block_lane_dot(p, l, a) : q4_block_lane_dot(p, l, a);
                         const float sc = a.da * dw;
-                        const float pr = (float)L * sc;
+                        const float pr = lane_sum_f32(L) * sc;
                         acc[m] = acc[m] + pr;
                     }
                 }
@@ -420,7 +420,7 @@ __global__ void __launch_bounds__(GV2_THREADS) k_gemv2(const uint8_t* __restrict
                             const LanePrep av = prep[((size_t)m * nb + b) * 4 + l];
                             const int L = WDT == GTN_Q8 ? q8_block_lane_dot(p, l, av) : q4_block_lane_dot(p, l, av);
                             const float sc = av.da * dw;
-                            prod[((size_t)(m * R + r) * 4 + l) * pstr + b] = (float)L * sc;
+                            prod[((size_t)(m * R + r) * 4 + l) * pstr + b] = lane_sum_f32(L) * sc;
                         }
                     }
                 }
@@ -607,7 +607,7 @@ __global__ void __launch_bounds__(GV3_THREADS, 2) k_gemv3(const uint8_t* __restr
                             const int hi = (wb >> 4) & 0x0f0f0f0f, lo = wb & 0x0f0f0f0f;
                             L = dp4a(hi, a0[k * 4 + l], dp4a(lo, a1[k * 4 + l], 0)) - 7 * asum[k * 4 + l];
                         }
-                        o[l][k] = (float)L * sc;
+                        o[l][k] = lane_sum_f32(L) * sc;
                     }
                 }
 #pragma unroll
@@ -787,7 +787,7 @@ __global__ void __launch_bounds__(GV3_THREADS, 2) k_gemm3(const uint8_t* __restr
                         const int2 av = pa[o2];
                         int L = dp4a(wl0[k * 4 + l], av.x, dp4a(wl1[k * 4 + l], av.y, 0));
                         if (WDT == GTN_Q4) L -= 7 * ps[o2];
-                        o[l][k] = (float)L * sc;
+                        o[l][k] = lane_sum_f32(L) * sc;
                     }
                 }
 #pragma unroll
@@ -881,7 +881,7 @@ __global__ void k_mm_rows_plain(const uint8_t* __restrict__ W, long w_stride, in
             const float da = h2f((uint16_t)(xb[0] | (xb[1] << 8)));
             const float dw = h2f((uint16_t)(wb[0] | (wb[1] << 8)));
             const float sc = da * dw;
-            const float pr = (float)L * sc;
+            const float pr = lane_sum_f32(L) * sc;
             acc = acc + pr;
         }
     }
