@@ -5,6 +5,7 @@
 #include <cstdarg>
 #include <map>
 #include <mutex>
+#include <tuple>
 
 #include "launch.cuh"
 
@@ -134,10 +135,10 @@ static cudaError_t launch_plain(const uint8_t* X, long xs, int M, const uint8_t*
 }
 
 static cudaError_t matmul_tma(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K,
-                              float* Y, long ldy, cudaStream_t st);
+                              float* Y, long ldy, cudaStream_t st, const TcScratch& tc);
 
 cudaError_t matmul_f32(const uint8_t* X, long xs, int xdt, int M, const uint8_t* W, long ws, int wdt, int N, int K,
-                       float* Y, long ldy, cudaStream_t st, bool padded) {
+                       float* Y, long ldy, cudaStream_t st, bool padded, const TcScratch& tc) {
     (void)xdt;
     auto plain = [&](int row0, int nrows) -> cudaError_t {
         if (wdt == GTN_Q8) return launch_plain<GTN_Q8>(X, xs, M, W, ws, row0, nrows, K, Y, ldy, st);
@@ -152,13 +153,13 @@ cudaError_t matmul_f32(const uint8_t* X, long xs, int xdt, int M, const uint8_t*
         if ((end & 15) != 0 || (ws & 15) != 0) {
             // every row but the last reads at most into the following row; the last row goes plain
             if (N > 1) {
-                const cudaError_t e = matmul_tma(X, xs, M, W, ws, wdt, N - 1, K, Y, ldy, st);
+                const cudaError_t e = matmul_tma(X, xs, M, W, ws, wdt, N - 1, K, Y, ldy, st, tc);
                 if (e != cudaSuccess) return e;
             }
             return plain(N - 1, 1);
         }
     }
-    return matmul_tma(X, xs, M, W, ws, wdt, N, K, Y, ldy, st);
+    return matmul_tma(X, xs, M, W, ws, wdt, N, K, Y, ldy, st, tc);
 }
 
 static int sm_count() {
@@ -290,25 +291,88 @@ static cudaError_t launch_gm3(const uint8_t* X, long xs, int M, const uint8_t* W
                       ws, N, K, X, xs, M, Y, ldy, p.R, p.MT, p.MC, device_error_word());
 }
 
-// k_gemm_tc: 16-byte aligned weight rows, K a multiple of 32 * TC_G, at least TC_MIN_M rows.
-static bool tc_fits(const uint8_t* W, long ws, int M, int wdt, int K) {
-    if (M < TC_MIN_M || (wdt != GTN_Q8 && wdt != GTN_Q4) || K % GTN_QBLK) return false;
+// ---- tensor-core GEMM (k_gemm_tc) -----------------------------------------------------------
+// cuTensorMapEncodeTiled, reached through the runtime's driver entry point.
+typedef CUresult (*TmapEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static TmapEncodeFn tmap_encode_fn() {
+    static TmapEncodeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<TmapEncodeFn>(p);
+    });
+    return fn;
+}
+
+// A weight matrix (N rows, row stride ws bytes) as a 2-D uint16 tensor [N][ws / 2] whose box is
+// 64 rows x rstr bytes (8 blocks); rows past N and bytes past the row stride read as zeros. The
+// map holds only the address and shape, so it is cached by them.
+static bool weight_tmap(const uint8_t* W, long ws, int N, int rstr, CUtensorMap* out) {
+    static std::mutex mu;
+    static std::map<std::tuple<uintptr_t, long, int, int>, CUtensorMap> cache;
+    std::lock_guard<std::mutex> lk(mu);
+    const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(W), ws, N, rstr);
+    const auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return true;
+    }
+    const TmapEncodeFn fn = tmap_encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)(ws / 2), (cuuint64_t)N};
+    const cuuint64_t strides[1] = {(cuuint64_t)ws};
+    const cuuint32_t box[2] = {(cuuint32_t)(rstr / 2), (cuuint32_t)TC_NT};
+    const cuuint32_t es[2] = {1, 1};
+    CUtensorMap m;
+    if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint8_t*>(W), dims, strides, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    if (cache.size() >= 4096) cache.clear();
+    cache.emplace(key, m);
+    *out = m;
+    return true;
+}
+
+// k_gemm_tc: at least TC_MIN_M rows, 16-byte aligned weight rows of at least one raw chunk (K >= 256),
+// K a multiple of 32 * TC_G, and scratch for one 32-row activation image.
+bool tc_fits(const uint8_t* W, long ws, int M, int wdt, int K, const TcScratch& tc) {
+    if (M < TC_MIN_M || (wdt != GTN_Q8 && wdt != GTN_Q4) || K % GTN_QBLK || !tc.p) return false;
     const int nb = K / GTN_QBLK;
-    return nb > 0 && nb % TC_G == 0 && ((reinterpret_cast<uintptr_t>(W) & 15) | (uintptr_t)(ws & 15)) == 0;
+    const long rstr = wdt == GTN_Q8 ? tc_rstride<GTN_Q8>() : tc_rstride<GTN_Q4>();
+    return nb % TC_G == 0 && ws >= rstr && tc.bytes >= tc_aimg_bytes(TC_MT, K) &&
+           ((reinterpret_cast<uintptr_t>(W) & 15) | (uintptr_t)(ws & 15) | (reinterpret_cast<uintptr_t>(tc.p) & 15)) == 0;
 }
 
 template <int WDT>
 static cudaError_t launch_tc(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y,
-                             long ldy, cudaStream_t st, bool dry) {
+                             long ldy, const TcScratch& tc, cudaStream_t st, bool dry) {
     constexpr size_t smem = tc_smem<WDT>();
-    const cudaError_t e = ensure_smem(k_gemm_tc<WDT>, smem);
-    if (e != cudaSuccess || dry) return e;
-    return launch_pdl(k_gemm_tc<WDT>, dim3((N + TC_NT - 1) / TC_NT, (M + TC_MT - 1) / TC_MT), dim3(TC_THREADS), smem,
-                      st, W, ws, N, K, X, xs, M, Y, ldy, device_error_word());
+    cudaError_t e = ensure_smem(k_gemm_tc<WDT>, smem);
+    if (e != cudaSuccess) return e;
+    CUtensorMap map;
+    if (!weight_tmap(W, ws, N, tc_rstride<WDT>(), &map)) return cudaErrorInvalidValue;
+    if (dry) return cudaSuccess;
+    const int nb = K / GTN_QBLK;
+    const int cap = (int)(tc.bytes / ((size_t)nb * TC_AIMG)) * TC_MT;  // rows per pass
+    for (int r0 = 0; r0 < M; r0 += cap) {
+        const int mm = std::min(cap, M - r0), tiles = (mm + TC_MT - 1) / TC_MT;
+        e = launch_pdl(k_tc_expand, dim3(nb, tiles), dim3(128), 0, st, X + (long)r0 * xs, xs, mm, K, tc.p);
+        if (e != cudaSuccess) return e;
+        e = launch_pdl(k_gemm_tc<WDT>, dim3((N + TC_NT - 1) / TC_NT, tiles), dim3(TC_THREADS), smem, st, map, N, K,
+                       (const uint8_t*)tc.p, mm, Y + (long)r0 * ldy, ldy, device_error_word());
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
-bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K) {
-    if (tc_fits(W, ws, M, wdt, K)) return true;
+bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K, const TcScratch& tc) {
+    if (tc_fits(W, ws, M, wdt, K, tc)) return true;
     GM3Plan gp{};
     if (wdt == GTN_Q8) return gm3_plan<GTN_Q8>(W, ws, M, K, &gp);
     if (wdt == GTN_Q4) return gm3_plan<GTN_Q4>(W, ws, M, K, &gp);
@@ -316,10 +380,10 @@ bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K) {
 }
 
 cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
-                   long ldy, cudaStream_t st, bool dry) {
-    if (tc_fits(W, ws, M, wdt, K))
-        return wdt == GTN_Q8 ? launch_tc<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, st, dry)
-                             : launch_tc<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, st, dry);
+                   long ldy, cudaStream_t st, bool dry, const TcScratch& tc) {
+    if (tc_fits(W, ws, M, wdt, K, tc))
+        return wdt == GTN_Q8 ? launch_tc<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, tc, st, dry)
+                             : launch_tc<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, tc, st, dry);
     GM3Plan gp{};
     if (wdt == GTN_Q8 && gm3_plan<GTN_Q8>(W, ws, M, K, &gp))
         return launch_gm3<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, gp, st, dry);
@@ -329,9 +393,9 @@ cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, 
 }
 
 static cudaError_t matmul_tma(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K,
-                              float* Y, long ldy, cudaStream_t st) {
+                              float* Y, long ldy, cudaStream_t st, const TcScratch& tc) {
     if (gemv_q_fits(M, wdt, K)) return gemv_q(X, xs, M, W, ws, wdt, N, K, Y, ldy, st, false);
-    if (tc_fits(W, ws, M, wdt, K)) return gemm_q(X, xs, M, W, ws, wdt, N, K, Y, ldy, st, false);
+    if (tc_fits(W, ws, M, wdt, K, tc)) return gemm_q(X, xs, M, W, ws, wdt, N, K, Y, ldy, st, false, tc);
     GM3Plan gp{};
     if (wdt == GTN_Q8 && gm3_plan<GTN_Q8>(W, ws, M, K, &gp)) return launch_gm3<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, gp, st);
     if (wdt == GTN_Q4 && gm3_plan<GTN_Q4>(W, ws, M, K, &gp)) return launch_gm3<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, gp, st);
@@ -522,20 +586,33 @@ int gtn_matmul_2d(const gtn_tensor* x, const gtn_tensor* w, gtn_tensor* out, int
     const uint8_t* X = (const uint8_t*)x->data + (long)start_pos * bstride(x, 0);
     const long os = out->ndim == 1 ? 0 : bstride(out, 0);
     cudaStream_t st = S(stream);
+    // the tensor-core path's expanded activation image (stream-ordered scratch, freed below)
+    TcScratch tc;
+    if (q && M >= TC_MIN_M && K % GTN_QBLK == 0) {
+        tc.bytes = tc_aimg_bytes(M, K);
+        if (cudaMallocAsync((void**)&tc.p, tc.bytes, st) != cudaSuccess) {
+            cudaGetLastError();
+            tc = TcScratch();  // the CUDA-core kernels need no scratch
+        }
+    }
+    cudaError_t e;
     if (out->dtype == GTN_F32) {
         float* Y = (float*)((uint8_t*)out->data + (long)start_pos * os);
-        return cuda_status(matmul_f32(X, bstride(x, 0), x->dtype, M, (const uint8_t*)w->data, bstride(w, 0),
-                                      w->dtype, N, K, Y, out->ndim == 1 ? 0 : N, st, false),
-                           "matmul_2d");
+        e = matmul_f32(X, bstride(x, 0), x->dtype, M, (const uint8_t*)w->data, bstride(w, 0), w->dtype, N, K, Y,
+                       out->ndim == 1 ? 0 : N, st, false, tc);
+    } else {
+        float* Y = nullptr;
+        e = cudaMallocAsync((void**)&Y, sizeof(float) * (size_t)M * N, st);
+        if (e == cudaSuccess) {
+            e = matmul_f32(X, bstride(x, 0), x->dtype, M, (const uint8_t*)w->data, bstride(w, 0), w->dtype, N, K, Y, N,
+                           st, false, tc);
+            if (e == cudaSuccess)
+                e = launch_pdl(k_write_rows, dim3(((N + GTN_QBLK - 1) / GTN_QBLK + 3) / 4, M), dim3(128), 0, st,
+                               (const float*)Y, (long)N, (uint8_t*)out->data, os, (int)out->dtype, N, start_pos);
+            cudaFreeAsync(Y, st);
+        }
     }
-    float* Y = nullptr;
-    GTN_CHECK(cuda_status(cudaMallocAsync((void**)&Y, sizeof(float) * (size_t)M * N, st), "matmul_2d scratch"));
-    cudaError_t e = matmul_f32(X, bstride(x, 0), x->dtype, M, (const uint8_t*)w->data, bstride(w, 0), w->dtype, N,
-                               K, Y, N, st, false);
-    if (e == cudaSuccess)
-        e = launch_pdl(k_write_rows, dim3(((N + GTN_QBLK - 1) / GTN_QBLK + 3) / 4, M), dim3(128), 0, st,
-                       (const float*)Y, (long)N, (uint8_t*)out->data, os, (int)out->dtype, N, start_pos);
-    cudaFreeAsync(Y, st);
+    if (tc.p) cudaFreeAsync(tc.p, st);
     return cuda_status(e, "matmul_2d");
 }
 

@@ -58,6 +58,7 @@ struct gtn_model {
     uint8_t *kr = nullptr, *vr = nullptr;  // new K / V rows of a prefill, reference layout
     long kv_rs = 0;                        // KV cache row stride (att_kv_rs: one padded head row)
     float* y = nullptr;
+    gtn::TcScratch tcs;  // expanded activation image of the tensor-core GEMM (Q8/Q4 weights)
     float* logits = nullptr;
     int32_t* tok = nullptr;
     int32_t* next = nullptr;
@@ -230,6 +231,13 @@ int gtn_model_create(int kind, int wdtype, int max_ctx, int max_batch, const int
     rc |= dalloc(m.get(), &m->u, R * row_bytes(adt, m->max_ffn));
     const long ywidth = std::max<long>(m->max_q + 2L * m->max_kv, 2L * m->max_ffn);
     rc |= dalloc(m.get(), &m->y, sizeof(float) * R * ywidth);
+    if (m->wdt == GTN_Q8 || m->wdt == GTN_Q4) {
+        // k_gemm_tc's activation image: up to 512 rows per pass (prefill chunks, batched steps)
+        const int rows = std::min(512, std::max(m->max_rows, max_batch));
+        const int kmax = std::max(m->d, std::max(m->max_q, m->max_ffn));
+        m->tcs.bytes = gtn::tc_aimg_bytes(rows, kmax);
+        rc |= dalloc(m.get(), &m->tcs.p, m->tcs.bytes);
+    }
     rc |= dalloc(m.get(), &m->logits, sizeof(float) * (size_t)m->n_vocab * max_batch);
     // token ids per sequence: max_ctx + 1 slots (the last generated id is recorded, never fed back)
     rc |= dalloc(m.get(), &m->tok, sizeof(int32_t) * (size_t)(max_ctx + 1) * max_batch);
@@ -633,7 +641,7 @@ static int forward(gtn_model* m, int seq, int n, int sp) {
         uint8_t* kr = m->kr;
         uint8_t* vr = m->vr;
         GK(norm_rows(m, m->x, m->a, Ly.n1w, Ly.n1b, M, st));
-        GK(matmul_f32(m->a, rd_, adt, M, Ly.wqkv, Ly.rs_d, m->wdt, nqkv, d, m->y, nqkv, st));
+        GK(matmul_f32(m->a, rd_, adt, M, Ly.wqkv, Ly.rs_d, m->wdt, nqkv, d, m->y, nqkv, st, true, m->tcs));
         GK(write_cols(m->y, nqkv, 0, qd, m->q, rq, adt, M, st));
         GK(write_cols(m->y, nqkv, qd, kvd, kr, rkv, adt, M, st));
         GK(write_cols(m->y, nqkv, qd + kvd, kvd, vr, rkv, adt, M, st));
@@ -670,17 +678,17 @@ static int forward(gtn_model* m, int seq, int n, int sp) {
         GK(launch_pdl(k_attn, dim3(Ly.nh, M), dim3(ATT_THREADS), asmem, st, (const uint8_t*)(m->q - (long)sp * rq),
                       rq, (const uint8_t*)kc, m->kv_rs, khs, (const uint8_t*)vc, m->kv_rs, khs,
                       m->att - (long)sp * rq, rq, adt, n, sp, Ly.nh, Ly.nkv, dh, device_error_word()));
-        GK(matmul_f32(m->att, rq, adt, M, Ly.wo, Ly.rs_q, m->wdt, d, qd, m->y, d, st));
+        GK(matmul_f32(m->att, rq, adt, M, Ly.wo, Ly.rs_q, m->wdt, d, qd, m->y, d, st, true, m->tcs));
         GK(write_cols(m->y, d, 0, d, m->o, rd_, adt, M, st));
         if (m->family == 2) GK(rows_op(ROP_SCALE, m->o, rd_, nullptr, 0, m->o, rd_, adt, d, M, depth, nullptr, st));
         GK(rows_op(ROP_ADD, m->x, rd_, m->o, rd_, m->h, rd_, adt, d, M, 0.0f, nullptr, st));
         GK(norm_rows(m, m->h, m->a, Ly.n2w, Ly.n2b, M, st));
-        GK(matmul_f32(m->a, rd_, adt, M, Ly.wgu, Ly.rs_d, m->wdt, 2 * Ly.nffn, d, m->y, 2L * Ly.nffn, st));
+        GK(matmul_f32(m->a, rd_, adt, M, Ly.wgu, Ly.rs_d, m->wdt, 2 * Ly.nffn, d, m->y, 2L * Ly.nffn, st, true, m->tcs));
         GK(write_cols(m->y, 2L * Ly.nffn, 0, Ly.nffn, m->g, rf, adt, M, st));
         GK(write_cols(m->y, 2L * Ly.nffn, Ly.nffn, Ly.nffn, m->u, rf, adt, M, st));
         GK(rows_op(ROP_SILU, m->g, rf, nullptr, 0, m->g, rf, adt, Ly.nffn, M, 0.0f, nullptr, st));
         GK(rows_op(ROP_MUL, m->g, rf, m->u, rf, m->g, rf, adt, Ly.nffn, M, 0.0f, nullptr, st));
-        GK(matmul_f32(m->g, rf, adt, M, Ly.wd, Ly.rs_f, m->wdt, d, Ly.nffn, m->y, d, st));
+        GK(matmul_f32(m->g, rf, adt, M, Ly.wd, Ly.rs_f, m->wdt, d, Ly.nffn, m->y, d, st, true, m->tcs));
         GK(write_cols(m->y, d, 0, d, m->o, rd_, adt, M, st));
         if (m->family == 2) GK(rows_op(ROP_SCALE, m->o, rd_, nullptr, 0, m->o, rd_, adt, d, M, depth, nullptr, st));
         GK(rows_op(ROP_ADD, m->h, rd_, m->o, rd_, m->x, rd_, adt, d, M, 0.0f, nullptr, st));
@@ -758,9 +766,9 @@ static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) 
         if (!dry) ++g_step_kernels;
         return gemv_q(g.xin, g.xin_s, g.B, g.W, g.ws, m->wdt, g.N, g.K, g.Y, g.ldy, m->st, dry);
     }
-    if (gemm_q_fits(g.W, g.ws, g.B, m->wdt, g.K)) {  // batches of 5 or more sequences
-        if (!dry) ++g_step_kernels;
-        return gemm_q(g.xin, g.xin_s, g.B, g.W, g.ws, m->wdt, g.N, g.K, g.Y, g.ldy, m->st, dry);
+    if (gemm_q_fits(g.W, g.ws, g.B, m->wdt, g.K, m->tcs)) {  // batches of 5 or more sequences
+        if (!dry) g_step_kernels += tc_fits(g.W, g.ws, g.B, m->wdt, g.K, m->tcs) ? 2 : 1;
+        return gemm_q(g.xin, g.xin_s, g.B, g.W, g.ws, m->wdt, g.N, g.K, g.Y, g.ldy, m->st, dry, m->tcs);
     }
     if (m->wdt == GTN_Q8) return fg_mt<GTN_Q8, PRO_COPY>(g, m->st, dry);
     return fg_mt<GTN_Q4, PRO_COPY>(g, m->st, dry);

@@ -1,4 +1,4 @@
-// Exact Q8/Q4 GEMM on the 5th-generation tensor cores (tcgen05) for M >= 16 activation rows:
+// Exact Q8/Q4 GEMM on the 5th-generation tensor cores (tcgen05) for M >= 32 activation rows:
 // prefill and batched decode steps.
 //
 // Reference: ops.cpp:292-490 (vec_dot_product_q8, vec_dot_product_q8_q4) inside matmul_2d_impl
@@ -20,47 +20,62 @@
 //     chain is the reference's. The four lane chains of an output meet in shared memory at the
 //     end for (L0 + L1) + (L2 + L3).
 //
-// Data movement: weight rows arrive raw (34/18-byte blocks, which are not TMA-tileable) by 1-D
-// bulk copies of 8 blocks per row into a 3-stage ring; the CUDA cores convert them into the
-// canonical K-major fp16 tile (8-row x 16-byte core matrices, no swizzle) the MMA reads, and the
-// activations into A' (only each row's lane words are written; the zeros are written once). Four
-// groups of 2 blocks are in flight (tile, TMEM and scale slots); converter warps, the MMA issue and
-// epilogue warps run as separate roles. Every wait is bounded (about 2 s of device time); on expiry
-// the kernel flags the device error word, waits (bounded) for its own copies and MMAs, frees its
-// TMEM and returns.
+// Data movement:
+//   * activations: a pre-pass (k_tc_expand) writes, per 32-row tile and block, the expanded A'
+//     tile in the MMA's canonical K-major fp16 layout (8-row x 16-byte core matrices, no swizzle)
+//     followed by the 32 activation scales: 8320 bytes that the GEMM fetches with one bulk copy
+//     (the image is small and stays in L2; every CTA of a row tile reads the same image);
+//   * weights: raw rows (34/18-byte blocks, 16-byte aligned row stride) through a 2-D TMA tensor
+//     map, one copy per 64 rows x 8 blocks into a 3-stage ring; each converter thread turns one
+//     (row, block) into the four 16-byte K-chunk rows of the canonical fp16 tile (aligned word
+//     loads, byte permutes and one exact fp16 subtraction per pair).
+// Four groups of 2 blocks are in flight (tile, TMEM and scale slots). Roles: a producer warp
+// (copies), converter warps (weight tiles; their thread 0 issues the MMAs), epilogue warps. Every
+// wait is bounded (about 2 s of device time); on expiry the kernel flags the device error word,
+// waits (bounded) for its own copies and MMAs, frees its TMEM and returns.
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace gtn {
 
 constexpr int TC_EPI_WARPS = 8;                  // epilogue warps: warp w reads TMEM lane quarter w % 4
-constexpr int TC_CONV_WARPS = 4;                 // converter warps (thread 0 also issues MMAs and copies)
+constexpr int TC_CONV_WARPS = 4;                 // converter warps (thread 0 also issues the MMAs)
 constexpr int TC_CONV_THREADS = 32 * TC_CONV_WARPS;
-constexpr int TC_THREADS = 32 * (TC_EPI_WARPS + TC_CONV_WARPS);
+constexpr int TC_PROD_WARP = TC_EPI_WARPS + TC_CONV_WARPS;  // producer warp (copies)
+constexpr int TC_THREADS = 32 * (TC_PROD_WARP + 1);
 constexpr int TC_MT = 32;                        // activation rows per CTA (x 4 lanes = 128 MMA rows)
 constexpr int TC_NT = 64;                        // weight rows per CTA (MMA N)
 constexpr int TC_G = 2;                          // blocks per group (one commit)
 constexpr int TC_S = 4;                          // groups in flight (tile / TMEM / scale slots)
-constexpr int TC_KB = 8;                         // blocks per raw weight chunk (one bulk copy per row)
+constexpr int TC_KB = 8;                         // blocks per raw weight chunk (one TMA copy)
 constexpr int TC_RS = 3;                         // raw chunk stages
 constexpr int TC_TMEM_COLS = TC_S * TC_G * TC_NT;  // 512 columns: the whole TMEM (one CTA per SM)
 constexpr int TC_ATILE = 128 * 64;               // expanded activation tile of one block: 128 rows x 32 fp16
+constexpr int TC_AIMG = TC_ATILE + TC_MT * 4;    // + the 32 activation scales (fp32): one bulk copy
 constexpr int TC_BTILE = TC_NT * 64;             // weight tile of one block: 64 rows x 32 fp16
 constexpr int TC_COMB_STRIDE = 65;               // floats per (lane, row) in the final combine (bank spread)
 
+// Bytes of the expanded activation image of M rows and K columns (k_tc_expand's output).
+__host__ __device__ inline size_t tc_aimg_bytes(int M, int K) {
+    return (size_t)((M + TC_MT - 1) / TC_MT) * (size_t)(K / GTN_QBLK) * TC_AIMG;
+}
 template <int WDT>
-__host__ __device__ constexpr int tc_rstride() {
-    return ((TC_KB * (WDT == GTN_Q8 ? GTN_Q8_BYTES : GTN_Q4_BYTES) + 15) / 16) * 16;
+__host__ __device__ constexpr int tc_rstride() {  // raw chunk row: 8 blocks (272 / 144 bytes)
+    return TC_KB * (WDT == GTN_Q8 ? GTN_Q8_BYTES : GTN_Q4_BYTES);
 }
 template <int WDT>
 __host__ __device__ constexpr size_t tc_smem() {
-    return 1024 + (size_t)TC_S * TC_G * (TC_ATILE + TC_BTILE) + (size_t)TC_RS * TC_NT * tc_rstride<WDT>() +
-           (size_t)TC_S * TC_G * (TC_MT + TC_NT) * sizeof(float);
+    return 1024 + (size_t)TC_S * TC_G * (TC_AIMG + TC_BTILE) + (size_t)TC_RS * TC_NT * tc_rstride<WDT>() +
+           (size_t)TC_S * TC_G * TC_NT * sizeof(float) + 64;
 }
-static_assert((size_t)4 * TC_MT * TC_COMB_STRIDE * sizeof(float) <= (size_t)TC_S * TC_G * TC_ATILE,
+static_assert(tc_rstride<GTN_Q8>() % 16 == 0 && tc_rstride<GTN_Q4>() % 16 == 0, "TMA boxes are 16-byte rows");
+static_assert((size_t)4 * TC_MT * TC_COMB_STRIDE * sizeof(float) <= (size_t)TC_S * TC_G * TC_AIMG,
               "the combine buffer reuses the activation tiles");
 static_assert(TC_TMEM_COLS <= 512, "TMEM has 512 columns");
 static_assert(TC_KB % TC_G == 0, "groups never straddle raw chunks");
+static_assert(TC_G * TC_NT == TC_CONV_THREADS, "one (block, row) pair per converter thread");
 
 // Shared-memory matrix descriptor (tcgen05): K-major, no swizzle; LBO = bytes between the two
 // 16-byte K chunks of a core-matrix row group, SBO = bytes between 8-row groups; version 1.
@@ -147,35 +162,92 @@ __device__ __forceinline__ uint2 tc_bytes_to_f16x4(uint32_t x, uint32_t sub2) {
     return make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
 }
 
-// Y[m, n] (fp32, row stride y_stride) = dot(X[m, :], W[n, :]) for Q8 activations X and Q8/Q4
-// weights W, bit-identical to the reference. W: 16-byte aligned base and row stride, rows readable
-// up to the next 16-byte boundary; K / 32 a multiple of TC_G. grid (ceil(N / 64), ceil(M / 32)),
-// block TC_THREADS, dynamic shared memory tc_smem<WDT>(); one CTA per SM (it holds all of TMEM).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+// 2-D TMA tile load (no multicast) of box (x, y) of `map` into shared memory, counted on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Expanded activation image for k_gemm_tc: for each 32-row tile t and block b, at
+// img + (t * nb + b) * TC_AIMG, the A' tile (row r = l * 32 + m holds the lane-l elements of
+// activation row m as fp16, zeros elsewhere; canonical K-major layout) and the 32 row scales as
+// fp32 (0 for rows past M). X: Q8 rows, stride x_stride. grid (nb, ceil(M / 32)), block 128.
+static __global__ void __launch_bounds__(128) k_tc_expand(const uint8_t* __restrict__ X, long x_stride, int M, int K,
+                                                         uint8_t* __restrict__ img) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int b = blockIdx.x, t = blockIdx.y, nb = K / GTN_QBLK;
+    const int m0 = t * TC_MT, mr = min(TC_MT, M - m0);
+    uint8_t* tile = img + ((size_t)t * nb + b) * TC_AIMG;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int u = threadIdx.x + 128 * i;  // 16-byte core row: chunk c, A' row r
+        const int c = u & 3, r = u >> 2, l = r >> 5, m = r & 31;
+        uint32_t w = 0u;
+        if (m < mr) {
+            const uint32_t v = ld_u16(X + (long)(m0 + m) * x_stride + (long)b * GTN_Q8_BYTES + 2 + 8 * c + 2 * l);
+            w = tc_bytes_to_f16x4(v ^ 0x8080u, 0x64806480u).x;  // (q + 128) - 1152
+        }
+        uint4 o = make_uint4(0u, 0u, 0u, 0u);
+        if (l == 0) o.x = w;
+        if (l == 1) o.y = w;
+        if (l == 2) o.z = w;
+        if (l == 3) o.w = w;
+        *reinterpret_cast<uint4*>(tile + (r >> 3) * 512 + c * 128 + (r & 7) * 16) = o;
+    }
+    if (threadIdx.x < TC_MT) {
+        const int m = threadIdx.x;
+        reinterpret_cast<float*>(tile + TC_ATILE)[m] =
+            m < mr ? h2f(ld_u16(X + (long)(m0 + m) * x_stride + (long)b * GTN_Q8_BYTES)) : 0.0f;
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+}
+
+// Y[m, n] (fp32, row stride y_stride) = dot(X[m, :], W[n, :]) for Q8 activations and Q8/Q4
+// weights, bit-identical to the reference. `img`: k_tc_expand's image of X (M rows). `wmap`: the
+// weight matrix as a 2-D uint16 tensor (inner extent w_stride / 2, N rows, row stride w_stride),
+// box (tc_rstride / 2, 64); rows past N read as zeros. K / 32 a multiple of TC_G.
+// grid (ceil(N / 64), ceil(M / 32)), block TC_THREADS, dynamic shared memory tc_smem<WDT>();
+// one CTA per SM (it holds all of TMEM).
 //
 // Roles, synchronised only by mbarriers (no block-wide barrier inside the main loop):
-//   converter warps 8-11, group g in slot s = g % TC_S: wait until the epilogue released slot s
-//     (tmem_empty, group g - TC_S), write the activation lane words and the weight tile of the
-//     group's blocks, then barrier 1 among themselves; their thread 0 issues the group's MMAs
-//     into TMEM slot s and commits them to mma_done[s], and refills the raw weight ring.
-//   epilogue warps 0-7: wait mma_done[s], read the lane sums from TMEM, run the fp32 chains,
-//     release slot s (tmem_empty[s], 256 arrivals).
+//   producer warp: weight chunks (raw_full / raw_empty ring) and the A' images of group g into
+//     slot s = g % TC_S once the epilogue released the slot (tmem_empty of group g - TC_S);
+//   converter warps: wait for the slot and the raw chunk, write the weight tile and scales, barrier
+//     1 among themselves; their thread 0 releases finished raw chunks, waits for the A' images and
+//     issues the group's MMAs into TMEM slot s, committed to mma_done[s];
+//   epilogue warps: wait mma_done[s], read the lane sums from TMEM, run the fp32 chains, release
+//     slot s (tmem_empty[s], 256 arrivals).
 template <int WDT>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const uint8_t* __restrict__ W, long w_stride, int N, int K,
-                                                           const uint8_t* __restrict__ X, long x_stride, int M,
+__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap wmap, int N, int K,
+                                                           const uint8_t* __restrict__ img, int M,
                                                            float* __restrict__ Y, long y_stride, unsigned int* err) {
     constexpr int BB = WDT == GTN_Q8 ? GTN_Q8_BYTES : GTN_Q4_BYTES;
     constexpr int RSTR = tc_rstride<WDT>();
+    constexpr uint32_t CHUNK_BYTES = (uint32_t)RSTR * TC_NT;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem);  // [TC_RS]
-    uint64_t* mma_done = raw_full + TC_RS;                    // [TC_S]
+    uint64_t* raw_empty = raw_full + TC_RS;                   // [TC_RS]
+    uint64_t* a_full = raw_empty + TC_RS;                     // [TC_S]
+    uint64_t* mma_done = a_full + TC_S;                       // [TC_S]
     uint64_t* tmem_empty = mma_done + TC_S;                   // [TC_S]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + TC_S);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    uint8_t* atile = smem + 1024;                             // [TC_S * TC_G][TC_ATILE]
-    uint8_t* btile = atile + TC_S * TC_G * TC_ATILE;          // [TC_S * TC_G][TC_BTILE]
+    uint8_t* atile = smem + 1024;                             // [TC_S * TC_G][TC_AIMG]
+    uint8_t* btile = atile + TC_S * TC_G * TC_AIMG;           // [TC_S * TC_G][TC_BTILE]
     uint8_t* raw = btile + TC_S * TC_G * TC_BTILE;            // [TC_RS][TC_NT][RSTR]
-    float* da_s = reinterpret_cast<float*>(raw + (size_t)TC_RS * TC_NT * RSTR);  // [TC_S][TC_G][TC_MT]
-    float* dw_s = da_s + TC_S * TC_G * TC_MT;                                    // [TC_S][TC_G][TC_NT]
+    float* dw_s = reinterpret_cast<float*>(raw + (size_t)TC_RS * TC_NT * RSTR);  // [TC_S][TC_G][TC_NT]
     float* comb = reinterpret_cast<float*>(atile);  // [4][TC_MT][TC_COMB_STRIDE], after the last MMA
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -184,18 +256,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const uint8_t* __rest
     const int nb = K / GTN_QBLK, ngroups = nb / TC_G, nchunks = (nb + TC_KB - 1) / TC_KB;
     constexpr int CW0 = TC_EPI_WARPS;  // first converter warp
 
-    // raw chunk c (blocks [c*KB, c*KB + KB)) of the nr weight rows into stage c % TC_RS; one warp
-    auto issue_chunk = [&](int c) {
-        uint64_t* bar = &raw_full[c % TC_RS];
-        const int nblk = min(TC_KB, nb - c * TC_KB);
-        const uint32_t bytes = (uint32_t)((nblk * BB + 15) & ~15);
-        if (lane == 0) mbar_arrive_expect_tx(bar, bytes * (uint32_t)nr);
-        __syncwarp();
-        uint8_t* dst = raw + (size_t)(c % TC_RS) * TC_NT * RSTR;
-        for (int r = lane; r < nr; r += 32)
-            bulk_g2s(dst + (size_t)r * RSTR, W + (size_t)(n0 + r) * w_stride + (size_t)c * TC_KB * BB, bytes, bar);
-    };
-
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(TC_TMEM_COLS)
@@ -203,130 +263,147 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const uint8_t* __rest
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 32) {
-        for (int s = 0; s < TC_RS; ++s) mbar_init(&raw_full[s], 1);
+        for (int s = 0; s < TC_RS; ++s) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], 1);
+        }
         for (int s = 0; s < TC_S; ++s) {
+            mbar_init(&a_full[s], 1);
             mbar_init(&mma_done[s], 1);
             mbar_init(&tmem_empty[s], 32 * TC_EPI_WARPS);
         }
         *abort_flag = 0;
         fence_mbar_init();
     }
-    // the expanded activation tiles: zeros everywhere but the lane words written per block
-    for (int i = tid; i < TC_S * TC_G * TC_ATILE / 16; i += TC_THREADS)
-        reinterpret_cast<uint4*>(atile)[i] = make_uint4(0u, 0u, 0u, 0u);
-    fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    if (warp == CW0)
-        for (int c = 0; c < min(TC_RS, nchunks); ++c) issue_chunk(c);  // weights: independent of the previous kernel
-    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     float acc[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-    int g_issued = 0, chunks_issued = min(TC_RS, nchunks);
+    int g_issued = 0;                // converter thread 0: groups whose MMAs were issued
+    int a_issued = 0, w_issued = 0;  // producer: groups of A' images and weight chunks issued
 
-    if (warp >= CW0) {
-        // ---- converters (and the MMA / copy issue on converter warp 0) ----
+    if (warp == TC_PROD_WARP) {
+        // ---- producer (one thread) ----
+        if (lane == 0) {
+            for (int c = 0; c < min(TC_RS, nchunks); ++c) {  // weights: independent of the previous kernel
+                mbar_arrive_expect_tx(&raw_full[c], CHUNK_BYTES);
+                tma_load_2d(raw + (size_t)c * TC_NT * RSTR, &wmap, c * (RSTR / 2), n0, &raw_full[c]);
+            }
+            w_issued = min(TC_RS, nchunks);
+            asm volatile("griddepcontrol.wait;" ::: "memory");  // the A' image comes from the pre-pass
+            const uint8_t* aimg = img + (size_t)blockIdx.y * nb * TC_AIMG;
+            uint64_t t0 = globaltimer_ns();
+            while (a_issued < ngroups || w_issued < nchunks) {
+                bool progressed = false;
+                if (a_issued < ngroups) {
+                    const int g = a_issued, s = g % TC_S;
+                    if (g < TC_S || mbar_test(&tmem_empty[s], (uint32_t)(g / TC_S - 1) & 1u)) {
+                        mbar_arrive_expect_tx(&a_full[s], (uint32_t)(TC_G * TC_AIMG));
+                        for (int blk = 0; blk < TC_G; ++blk)
+                            bulk_g2s(atile + (size_t)(s * TC_G + blk) * TC_AIMG,
+                                     aimg + (size_t)(g * TC_G + blk) * TC_AIMG, (uint32_t)TC_AIMG, &a_full[s]);
+                        ++a_issued;
+                        progressed = true;
+                    }
+                }
+                if (w_issued < nchunks) {
+                    const int c = w_issued, st = c % TC_RS;
+                    if (mbar_test(&raw_empty[st], (uint32_t)(c / TC_RS - 1) & 1u)) {
+                        mbar_arrive_expect_tx(&raw_full[st], CHUNK_BYTES);
+                        tma_load_2d(raw + (size_t)st * TC_NT * RSTR, &wmap, c * (RSTR / 2), n0, &raw_full[st]);
+                        ++w_issued;
+                        progressed = true;
+                    }
+                }
+                if (progressed) {
+                    t0 = globaltimer_ns();
+                } else if (*abort_flag != 0 || globaltimer_ns() - t0 > TC_WAIT_NS) {
+                    *abort_flag = 1;
+                    if (err) atomicOr(err, GTN_DEVERR_TIMEOUT);
+                    break;
+                } else {
+                    __nanosleep(64);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp >= CW0) {
+        // ---- converters: thread -> (block blk of the group, weight row n); the whole 32-element
+        // block is read as aligned words (the block data starts 2 bytes past a word boundary in even
+        // blocks) and written as the four 16-byte K-chunk rows of the fp16 tile. Thread 0 also
+        // releases finished raw chunks and issues the MMAs. ----
         const int ct = tid - 32 * CW0;
-        // activation lane words of group g: unit u -> (lane l, row m, chunk c, block)
-        auto act_word = [&](int g, int u) -> uint32_t {
-            const int l = u & 3, m = ((u >> 2) & 7) | (((u >> 7) & 3) << 3), c = (u >> 5) & 3, blk = u >> 9;
-            if (m >= mr) return 0u;
-            return (uint32_t)ld_u16(X + (long)(m0 + m) * x_stride + (long)(g * TC_G + blk) * GTN_Q8_BYTES + 2 + 8 * c +
-                                    2 * l);
-        };
-        auto act_scale = [&](int g) -> float {
-            const int m = ct % TC_MT, blk = ct / TC_MT;
-            return m < mr ? h2f(ld_u16(X + (long)(m0 + m) * x_stride + (long)(g * TC_G + blk) * GTN_Q8_BYTES)) : 0.0f;
-        };
-        constexpr int AU = TC_G * TC_MT * 16 / TC_CONV_THREADS;  // activation words per thread per group
-        constexpr int WU = TC_G * TC_NT * 8 / TC_CONV_THREADS;   // weight 4-element units per thread per group
-        uint32_t apf[AU];
-        float dapf = 0.0f;
-#pragma unroll
-        for (int i = 0; i < AU; ++i) apf[i] = act_word(0, ct + TC_CONV_THREADS * i);
-        if (ct < TC_G * TC_MT) dapf = act_scale(0);
+        const int blk = ct / TC_NT, n = ct % TC_NT;
         for (int g = 0; g < ngroups; ++g) {
             const int s = g % TC_S, chunk = (g * TC_G) / TC_KB, stage = chunk % TC_RS;
             bool ok = *abort_flag == 0;
             if (ok && g >= TC_S) ok = tc_wait(&tmem_empty[s], (uint32_t)(g / TC_S - 1) & 1u, err);
+            if (ok) ok = tc_wait(&raw_full[stage], (uint32_t)(chunk / TC_RS) & 1u, err);
             if (ok) {
+                const int boff = ((g * TC_G + blk) % TC_KB) * BB;  // block offset in the raw row
+                const uint8_t* row = raw + (size_t)stage * TC_NT * RSTR + (size_t)n * RSTR;
+                const int sh = ((boff + 2) & 3) * 8;                // 16 (even blocks) or 0 bits
+                const uint32_t* wp = reinterpret_cast<const uint32_t*>(row + ((boff + 2) & ~3));
+                uint8_t* dst = btile + (size_t)(s * TC_G + blk) * TC_BTILE + (n >> 3) * 512 + (n & 7) * 16;
+                if (WDT == GTN_Q8) {
+                    uint32_t w[9], d[8];
 #pragma unroll
-                for (int i = 0; i < AU; ++i) {
-                    const int u = ct + TC_CONV_THREADS * i;
-                    const int l = u & 3, m = ((u >> 2) & 7) | (((u >> 7) & 3) << 3), c = (u >> 5) & 3, blk = u >> 9;
-                    const int r = l * 32 + m;
-                    const uint2 h = tc_bytes_to_f16x4(apf[i] ^ 0x8080u, 0x64806480u);  // (q + 128) - 1152
-                    *reinterpret_cast<uint32_t*>(atile + (size_t)(s * TC_G + blk) * TC_ATILE + (r >> 3) * 512 +
-                                                 c * 128 + (r & 7) * 16 + l * 4) = h.x;
-                }
-                if (ct < TC_G * TC_MT) da_s[s * TC_G * TC_MT + ct] = dapf;
-                if (g + 1 < ngroups) {  // the next group's activations, in flight meanwhile
+                    for (int i = 0; i < 9; ++i) w[i] = wp[i];
 #pragma unroll
-                    for (int i = 0; i < AU; ++i) apf[i] = act_word(g + 1, ct + TC_CONV_THREADS * i);
-                    if (ct < TC_G * TC_MT) dapf = act_scale(g + 1);
-                }
-                ok = tc_wait(&raw_full[stage], (uint32_t)(chunk / TC_RS) & 1u, err);
-            }
-            if (ok) {
-                const uint8_t* rs = raw + (size_t)stage * TC_NT * RSTR;
+                    for (int i = 0; i < 8; ++i) d[i] = __funnelshift_r(w[i], w[i + 1], sh) ^ 0x80808080u;
 #pragma unroll
-                for (int i = 0; i < WU; ++i) {
-                    const int u = ct + TC_CONV_THREADS * i;
-                    const int kq = (u & 1) | (((u >> 4) & 3) << 1), n = ((u >> 1) & 7) | (((u >> 6) & 7) << 3);
-                    const int blk = u >> 9;
-                    uint2 h = make_uint2(0u, 0u);
-                    if (n < nr) {
-                        const uint8_t* bp = rs + (size_t)n * RSTR + (size_t)((g * TC_G + blk) % TC_KB) * BB + 2;
-                        if (WDT == GTN_Q8) {
-                            const uint32_t v = (uint32_t)ld_u16(bp + 4 * kq) | ((uint32_t)ld_u16(bp + 4 * kq + 2) << 16);
-                            h = tc_bytes_to_f16x4(v ^ 0x80808080u, 0x64806480u);  // (q + 128) - 1152
-                        } else {
-                            const int kb = 4 * (kq & 3);
-                            const uint32_t v = (uint32_t)ld_u16(bp + kb) | ((uint32_t)ld_u16(bp + kb + 2) << 16);
-                            const uint32_t nib = kq < 4 ? (v >> 4) & 0x0F0F0F0Fu : v & 0x0F0F0F0Fu;
-                            h = tc_bytes_to_f16x4(nib, 0x64076407u);  // nibble - 7
-                        }
+                    for (int c = 0; c < 4; ++c) {  // K chunk c: elements 8c .. 8c+7
+                        const uint2 lo = tc_bytes_to_f16x4(d[2 * c], 0x64806480u);  // (q + 128) - 1152
+                        const uint2 hi = tc_bytes_to_f16x4(d[2 * c + 1], 0x64806480u);
+                        *reinterpret_cast<uint4*>(dst + c * 128) = make_uint4(lo.x, lo.y, hi.x, hi.y);
                     }
-                    *reinterpret_cast<uint2*>(btile + (size_t)(s * TC_G + blk) * TC_BTILE + (n >> 3) * 512 +
-                                              (kq >> 1) * 128 + (n & 7) * 16 + (kq & 1) * 8) = h;
+                } else {
+                    uint32_t w[5], d[4];
+#pragma unroll
+                    for (int i = 0; i < 5; ++i) w[i] = wp[i];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) d[i] = __funnelshift_r(w[i], w[i + 1], sh);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {  // elements 8c..8c+7: high nibbles (c < 2) or low nibbles
+                        const uint32_t b0 = d[2 * (c & 1)], b1 = d[2 * (c & 1) + 1];
+                        const uint32_t q0 = c < 2 ? (b0 >> 4) & 0x0F0F0F0Fu : b0 & 0x0F0F0F0Fu;
+                        const uint32_t q1 = c < 2 ? (b1 >> 4) & 0x0F0F0F0Fu : b1 & 0x0F0F0F0Fu;
+                        const uint2 lo = tc_bytes_to_f16x4(q0, 0x64076407u);  // nibble - 7
+                        const uint2 hi = tc_bytes_to_f16x4(q1, 0x64076407u);
+                        *reinterpret_cast<uint4*>(dst + c * 128) = make_uint4(lo.x, lo.y, hi.x, hi.y);
+                    }
                 }
-                for (int i = ct; i < TC_G * TC_NT; i += TC_CONV_THREADS) {
-                    const int blk = i / TC_NT, n = i % TC_NT;
-                    dw_s[s * TC_G * TC_NT + i] =
-                        n < nr ? h2f(ld_u16(rs + (size_t)n * RSTR + (size_t)((g * TC_G + blk) % TC_KB) * BB)) : 0.0f;
-                }
+                dw_s[s * TC_G * TC_NT + ct] = h2f(ld_u16(row + boff));  // rows past N are zeros (scale 0)
                 fence_async_smem();  // generic-proxy tile writes -> visible to the tensor cores
             }
             if (!conv_bar_and(ok)) {
                 *abort_flag = 1;
                 break;
             }
-            if (warp == CW0) {
-                if (lane == 0) {
+            if (ct == 0) {
+                if ((g + 1) * TC_G % TC_KB == 0 || g + 1 == ngroups) mbar_arrive(&raw_empty[stage]);  // chunk done
+                if (!tc_wait(&a_full[s], (uint32_t)(g / TC_S) & 1u, err)) {
+                    *abort_flag = 1;
+                } else {
                     tc_fence_after();
 #pragma unroll
-                    for (int blk = 0; blk < TC_G; ++blk) {
-                        const int t = s * TC_G + blk;
-                        const uint32_t a = smem_u32(atile + (size_t)t * TC_ATILE);
+                    for (int b2 = 0; b2 < TC_G; ++b2) {
+                        const int t = s * TC_G + b2;
+                        const uint32_t a = smem_u32(atile + (size_t)t * TC_AIMG);
                         const uint32_t b = smem_u32(btile + (size_t)t * TC_BTILE);
                         const uint32_t d = tmem + (uint32_t)(t * TC_NT);
                         tc_mma(d, tc_desc(a, 128, 512), tc_desc(b, 128, 512), 0u);
                         tc_mma(d, tc_desc(a + 256, 128, 512), tc_desc(b + 256, 128, 512), 1u);
                     }
                     tc_commit(&mma_done[s]);
-                }
-                __syncwarp();
-                // this group ended its raw chunk: refill the stage with the chunk TC_RS ahead
-                if (((g + 1) * TC_G % TC_KB == 0 || g + 1 == ngroups) && chunk + TC_RS < nchunks) {
-                    issue_chunk(chunk + TC_RS);
-                    chunks_issued = chunk + TC_RS + 1;
+                    g_issued = g + 1;
                 }
             }
-            g_issued = g + 1;
+            __syncwarp();  // reconverge converter warp 0 before the next barrier
         }
     } else {
         // ---- epilogue: thread (quarter q = reference lane l, column half, row m = lane) ----
@@ -339,11 +416,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const uint8_t* __rest
             }
             tc_fence_after();
 #pragma unroll 1
-            for (int blk = 0; blk < TC_G; ++blk) {
-                const int t = s * TC_G + blk;
+            for (int b2 = 0; b2 < TC_G; ++b2) {
+                const int t = s * TC_G + b2;
                 float v[32];
                 tc_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * TC_NT + half * 32), v);
-                const float da = da_s[t * TC_MT + lane];
+                const float da = reinterpret_cast<const float*>(atile + (size_t)t * TC_AIMG + TC_ATILE)[lane];
                 const float4* dw4 = reinterpret_cast<const float4*>(dw_s + t * TC_NT + half * 32);
 #pragma unroll
                 for (int j4 = 0; j4 < 8; ++j4) {
@@ -379,13 +456,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const uint8_t* __rest
                 Y[(long)(m0 + m) * y_stride + n0 + n] = (c0 + c1) + (c2 + c3);
             }
         }
-    } else if (tid == 32 * CW0) {
+    } else {
         // an expired wait: let this CTA's MMAs and copies finish (bounded) before its TMEM and
         // shared memory are released; each slot / stage has at most one outstanding phase
-        for (int g2 = max(0, g_issued - TC_S); g2 < g_issued; ++g2)
-            tc_wait(&mma_done[g2 % TC_S], (uint32_t)(g2 / TC_S) & 1u, err);
-        for (int c = max(0, chunks_issued - TC_RS); c < chunks_issued; ++c)
-            tc_wait(&raw_full[c % TC_RS], (uint32_t)(c / TC_RS) & 1u, err);
+        if (tid == 32 * CW0)
+            for (int g2 = max(0, g_issued - TC_S); g2 < g_issued; ++g2)
+                tc_wait(&mma_done[g2 % TC_S], (uint32_t)(g2 / TC_S) & 1u, err);
+        if (tid == 32 * TC_PROD_WARP) {
+            for (int g2 = max(0, a_issued - TC_S); g2 < a_issued; ++g2)
+                tc_wait(&a_full[g2 % TC_S], (uint32_t)(g2 / TC_S) & 1u, err);
+            for (int c = max(0, w_issued - TC_RS); c < w_issued; ++c)
+                tc_wait(&raw_full[c % TC_RS], (uint32_t)(c / TC_RS) & 1u, err);
+        }
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();

@@ -106,8 +106,16 @@ unsigned int take_device_error();
 // `padded`: W is 16-byte aligned and its allocation extends at least 16 bytes past the last row
 // (the engine's arena guarantees it). Otherwise rows whose TMA tiles could leave the buffer are
 // computed by the plain-load kernel, so no byte outside W is ever read.
+// `tc`: device scratch for the tensor-core GEMM's expanded activation image (k_tc_expand); without
+// it (or when it holds less than one 32-row tile) the CUDA-core kernels run. Larger M are done in
+// passes of as many row tiles as the scratch holds.
+struct TcScratch {
+    uint8_t* p = nullptr;
+    size_t bytes = 0;
+};
 cudaError_t matmul_f32(const uint8_t* X, long x_stride, int xdt, int M, const uint8_t* W, long w_stride, int wdt,
-                       int N, int K, float* Y, long ldy, cudaStream_t st, bool padded = true);
+                       int N, int K, float* Y, long ldy, cudaStream_t st, bool padded = true,
+                       const TcScratch& tc = TcScratch());
 
 // Two-phase GEMV (k_gemv2) for M <= 4 activation rows of Q8 against Q8 or Q4 weights, with the
 // same `padded` precondition on W as matmul_f32. `dry` only configures shared memory (so that a
@@ -118,12 +126,15 @@ cudaError_t gemv_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, 
                    long ldy, cudaStream_t st, bool dry);
 
 // Exact GEMM for M >= 2 activation rows of Q8 against Q8 or Q4 weights (16-byte aligned weight
-// rows, same `padded` precondition): the tensor-core kernel k_gemm_tc from TC_MIN_M rows on, else
-// k_gemm3 on the CUDA cores; `dry` only configures shared memory.
-constexpr int TC_MIN_M = 128;
-bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K);
+// rows, same `padded` precondition): the tensor-core kernel k_gemm_tc from TC_MIN_M rows on when
+// `tc` scratch is given, else k_gemm3 on the CUDA cores; `dry` only configures shared memory and
+// prepares the weight tensor map (so that a later launch can be captured into a CUDA graph).
+constexpr int TC_MIN_M = 32;
+bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K, const TcScratch& tc = TcScratch());
 cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
-                   long ldy, cudaStream_t st, bool dry);
+                   long ldy, cudaStream_t st, bool dry, const TcScratch& tc = TcScratch());
+// Whether matmul_f32 / gemm_q take the tensor-core path for this shape given scratch `tc`.
+bool tc_fits(const uint8_t* W, long ws, int M, int wdt, int K, const TcScratch& tc);
 
 // Host table of (cos, sin) for positions [0, npos) and j < rd/2, as rotary_emb_impl computes them
 // (ops.cpp:791-812): theta = m * powf(10000, -((2j)/rd)), then cosf / sinf.

@@ -23,7 +23,7 @@ def dev_out(nbytes, device, fill=None):
 @pytest.mark.parametrize("wdt", [Q8, Q4, F16])
 @pytest.mark.parametrize("M,K,N", [(1, 2048, 256), (1, 2048, 2048), (1, 5632, 2048), (3, 256, 96), (16, 2048, 64),
                                    (9, 5760, 64), (64, 2304, 96), (1, 2048, 32003), (1, 2048, 40),
-                                   # tensor-core GEMM (M >= 16): partial row / column tiles, one raw
+                                   # tensor-core GEMM (M >= 32): partial row / column tiles, one raw
                                    # chunk, ring wrap-around (K = 5632: 22 chunks)
                                    (16, 256, 64), (33, 2048, 96), (100, 5632, 160), (128, 2304, 256),
                                    (47, 256, 32)])
