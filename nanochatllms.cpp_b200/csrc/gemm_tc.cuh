@@ -29,9 +29,8 @@
 //     map, one copy per 64 rows x 8 blocks into a 3-stage ring; each converter thread turns one
 //     (row, block) into the four 16-byte K-chunk rows of the canonical fp16 tile (aligned word
 //     loads, byte permutes and one exact fp16 subtraction per pair).
-// Four groups of 2 blocks are in flight (tile, TMEM and scale slots). Roles: a producer warp
-// (copies), converter warps (weight tiles; their thread 0 issues the MMAs), epilogue warps. Every
-// wait is bounded (about 2 s of device time); on expiry the kernel flags the device error word,
+// Two groups of 4 blocks are in flight (tile, TMEM and scale slots). Roles: a producer warp
+// (copies), converter warps (weight tiles), an MMA warp, epilogue warps. Every wait is bounded (about 2 s of device time); on expiry the kernel flags the device error word,
 // waits (bounded) for its own copies and MMAs, frees its TMEM and returns.
 #pragma once
 #include <cuda.h>
@@ -41,14 +40,15 @@
 namespace gtn {
 
 constexpr int TC_EPI_WARPS = 8;                  // epilogue warps: warp w reads TMEM lane quarter w % 4
-constexpr int TC_CONV_WARPS = 4;                 // converter warps (thread 0 also issues the MMAs)
+constexpr int TC_CONV_WARPS = 8;                 // converter warps: one (block, weight row) per thread
 constexpr int TC_CONV_THREADS = 32 * TC_CONV_WARPS;
 constexpr int TC_PROD_WARP = TC_EPI_WARPS + TC_CONV_WARPS;  // producer warp (copies)
-constexpr int TC_THREADS = 32 * (TC_PROD_WARP + 1);
+constexpr int TC_MMA_WARP = TC_PROD_WARP + 1;               // MMA issue warp
+constexpr int TC_THREADS = 32 * (TC_MMA_WARP + 1);
 constexpr int TC_MT = 32;                        // activation rows per CTA (x 4 lanes = 128 MMA rows)
 constexpr int TC_NT = 64;                        // weight rows per CTA (MMA N)
-constexpr int TC_G = 2;                          // blocks per group (one commit)
-constexpr int TC_S = 4;                          // groups in flight (tile / TMEM / scale slots)
+constexpr int TC_G = 4;                          // blocks per group (one commit)
+constexpr int TC_S = 2;                          // groups in flight (tile / TMEM / scale slots)
 constexpr int TC_KB = 8;                         // blocks per raw weight chunk (one TMA copy)
 constexpr int TC_RS = 3;                         // raw chunk stages
 constexpr int TC_TMEM_COLS = TC_S * TC_G * TC_NT;  // 512 columns: the whole TMEM (one CTA per SM)
@@ -103,18 +103,6 @@ __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.a
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-// Barrier 1 over the converter warps, returning the AND of every thread's `ok` (the same value in
-// all of them, so the converters always leave their loop together).
-__device__ __forceinline__ bool conv_bar_and(bool ok) {
-    uint32_t r;
-    asm volatile(
-        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 1, %2, q;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(r)
-        : "r"((uint32_t)ok), "n"(TC_CONV_THREADS)
-        : "memory");
-    return r != 0;
-}
-
 // Bounded mbarrier wait: at most about TC_WAIT_NS of device time (%globaltimer), then the device
 // error word is flagged and false returned.
 constexpr uint64_t TC_WAIT_NS = 2000000000ull;
@@ -224,9 +212,10 @@ static __global__ void __launch_bounds__(128) k_tc_expand(const uint8_t* __restr
 // Roles, synchronised only by mbarriers (no block-wide barrier inside the main loop):
 //   producer warp: weight chunks (raw_full / raw_empty ring) and the A' images of group g into
 //     slot s = g % TC_S once the epilogue released the slot (tmem_empty of group g - TC_S);
-//   converter warps: wait for the slot and the raw chunk, write the weight tile and scales, barrier
-//     1 among themselves; their thread 0 releases finished raw chunks, waits for the A' images and
-//     issues the group's MMAs into TMEM slot s, committed to mma_done[s];
+//   converter warps: wait for the slot and the raw chunk, write the weight tile and scales, arrive
+//     on b_full[s] (and on raw_empty once a chunk's last group is converted);
+//   MMA warp: waits for b_full[s] and a_full[s], issues the group's MMAs into TMEM slot s and
+//     commits them to mma_done[s];
 //   epilogue warps: wait mma_done[s], read the lane sums from TMEM, run the fp32 chains, release
 //     slot s (tmem_empty[s], 256 arrivals).
 template <int WDT>
@@ -240,7 +229,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem);  // [TC_RS]
     uint64_t* raw_empty = raw_full + TC_RS;                   // [TC_RS]
     uint64_t* a_full = raw_empty + TC_RS;                     // [TC_S]
-    uint64_t* mma_done = a_full + TC_S;                       // [TC_S]
+    uint64_t* b_full = a_full + TC_S;                         // [TC_S]
+    uint64_t* mma_done = b_full + TC_S;                       // [TC_S]
     uint64_t* tmem_empty = mma_done + TC_S;                   // [TC_S]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + TC_S);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -265,10 +255,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     if (tid == 32) {
         for (int s = 0; s < TC_RS; ++s) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], 1);
+            mbar_init(&raw_empty[s], TC_CONV_THREADS);
         }
         for (int s = 0; s < TC_S; ++s) {
             mbar_init(&a_full[s], 1);
+            mbar_init(&b_full[s], TC_CONV_THREADS);
             mbar_init(&mma_done[s], 1);
             mbar_init(&tmem_empty[s], 32 * TC_EPI_WARPS);
         }
@@ -283,7 +274,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     float acc[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-    int g_issued = 0;                // converter thread 0: groups whose MMAs were issued
+    int g_issued = 0;                // MMA warp: groups whose MMAs were issued
     int a_issued = 0, w_issued = 0;  // producer: groups of A' images and weight chunks issued
 
     if (warp == TC_PROD_WARP) {
@@ -331,11 +322,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
             }
         }
         __syncwarp();
-    } else if (warp >= CW0) {
+    } else if (warp >= CW0 && warp < CW0 + TC_CONV_WARPS) {
         // ---- converters: thread -> (block blk of the group, weight row n); the whole 32-element
         // block is read as aligned words (the block data starts 2 bytes past a word boundary in even
-        // blocks) and written as the four 16-byte K-chunk rows of the fp16 tile. Thread 0 also
-        // releases finished raw chunks and issues the MMAs. ----
+        // blocks) and written as the four 16-byte K-chunk rows of the fp16 tile ----
         const int ct = tid - 32 * CW0;
         const int blk = ct / TC_NT, n = ct % TC_NT;
         for (int g = 0; g < ngroups; ++g) {
@@ -380,31 +370,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
                 dw_s[s * TC_G * TC_NT + ct] = h2f(ld_u16(row + boff));  // rows past N are zeros (scale 0)
                 fence_async_smem();  // generic-proxy tile writes -> visible to the tensor cores
             }
-            if (!conv_bar_and(ok)) {
+            if (!ok) {
                 *abort_flag = 1;
                 break;
             }
-            if (ct == 0) {
-                if ((g + 1) * TC_G % TC_KB == 0 || g + 1 == ngroups) mbar_arrive(&raw_empty[stage]);  // chunk done
-                if (!tc_wait(&a_full[s], (uint32_t)(g / TC_S) & 1u, err)) {
-                    *abort_flag = 1;
-                } else {
-                    tc_fence_after();
-#pragma unroll
-                    for (int b2 = 0; b2 < TC_G; ++b2) {
-                        const int t = s * TC_G + b2;
-                        const uint32_t a = smem_u32(atile + (size_t)t * TC_AIMG);
-                        const uint32_t b = smem_u32(btile + (size_t)t * TC_BTILE);
-                        const uint32_t d = tmem + (uint32_t)(t * TC_NT);
-                        tc_mma(d, tc_desc(a, 128, 512), tc_desc(b, 128, 512), 0u);
-                        tc_mma(d, tc_desc(a + 256, 128, 512), tc_desc(b + 256, 128, 512), 1u);
-                    }
-                    tc_commit(&mma_done[s]);
-                    g_issued = g + 1;
-                }
-            }
-            __syncwarp();  // reconverge converter warp 0 before the next barrier
+            mbar_arrive(&b_full[s]);
+            if ((g + 1) * TC_G % TC_KB == 0 || g + 1 == ngroups) mbar_arrive(&raw_empty[stage]);  // chunk done
         }
+    } else if (warp == TC_MMA_WARP) {
+        // ---- MMA issue (one thread) ----
+        if (lane == 0) {
+            for (int g = 0; g < ngroups; ++g) {
+                const int s = g % TC_S;
+                const uint32_t ph = (uint32_t)(g / TC_S) & 1u;
+                if (*abort_flag != 0 || !tc_wait(&b_full[s], ph, err) || !tc_wait(&a_full[s], ph, err)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int b2 = 0; b2 < TC_G; ++b2) {
+                    const int t = s * TC_G + b2;
+                    const uint32_t a = smem_u32(atile + (size_t)t * TC_AIMG);
+                    const uint32_t b = smem_u32(btile + (size_t)t * TC_BTILE);
+                    const uint32_t d = tmem + (uint32_t)(t * TC_NT);
+                    tc_mma(d, tc_desc(a, 128, 512), tc_desc(b, 128, 512), 0u);
+                    tc_mma(d, tc_desc(a + 256, 128, 512), tc_desc(b + 256, 128, 512), 1u);
+                }
+                tc_commit(&mma_done[s]);
+                g_issued = g + 1;
+            }
+        }
+        __syncwarp();
     } else {
         // ---- epilogue: thread (quarter q = reference lane l, column half, row m = lane) ----
         const int q = warp & 3, half = warp >> 2;
@@ -459,7 +456,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     } else {
         // an expired wait: let this CTA's MMAs and copies finish (bounded) before its TMEM and
         // shared memory are released; each slot / stage has at most one outstanding phase
-        if (tid == 32 * CW0)
+        if (tid == 32 * TC_MMA_WARP)
             for (int g2 = max(0, g_issued - TC_S); g2 < g_issued; ++g2)
                 tc_wait(&mma_done[g2 % TC_S], (uint32_t)(g2 / TC_S) & 1u, err);
         if (tid == 32 * TC_PROD_WARP) {
