@@ -202,6 +202,65 @@ def gemv_roofline(G, torch, wdt: int, device, hbm_peak: float, only: str | None 
     return dom, out
 
 
+def gemm_sweep(G, torch, wdt: int, device, M: int, only: str | None = None):
+    """Live timing of the exact quantized GEMM with M activation rows on TinyLlama's weight shapes:
+    gtn_matmul_2d (the tcgen05 kernel from 32 rows on) and, for comparison, gtn_matmul_2d_noalloc,
+    which has no scratch for the activation image and so runs the CUDA-core GEMM. Rotating weight
+    copies larger than L2. cells = M*N*K/8 lane sums; the CUDA-core bound of the exact epilogue is
+    SMs x 128 lanes x the SM clock / 3 ordered fp32 operations per lane sum."""
+    import ctypes as C
+    from gten_b200 import row_bytes
+    shapes = [(2560, 2048, "qkv"), (2048, 2048, "o"), (11264, 2048, "gate_up"), (2048, 5632, "down")]
+    if only:
+        shapes = [s for s in shapes if s[2] == only]
+    props = torch.cuda.get_device_properties(device)
+    bound = props.multi_processor_count * 128 * 1.965e9 / 3
+    stream = torch.cuda.current_stream()
+    out = {}
+    for N, K, name in shapes:
+        wb = N * row_bytes(wdt, K)
+        ncopy = max(2, int(300e6 // wb) + 1)
+        ws = [torch.randint(0, 255, (wb,), dtype=torch.uint8, device=device) for _ in range(ncopy)]
+        bb = 34 if wdt == 3 else 18
+        for w in ws:  # valid fp16 deltas (1/1024) in every block
+            w.view(-1, bb)[:, 0] = 0x00
+            w.view(-1, bb)[:, 1] = 0x14
+        xq = torch.randint(0, 255, (M * row_bytes(3, K),), dtype=torch.uint8, device=device)
+        xq.view(-1, 34)[:, 0] = 0x00
+        xq.view(-1, 34)[:, 1] = 0x14
+        y = torch.empty(M * N, dtype=torch.float32, device=device)
+        X, Y = G.GT(xq, 3, (M, K)), G.GT(y, 2, (M, N))
+
+        def tc(i):
+            G.matmul_2d(X, G.GT(ws[i % ncopy], wdt, (N, K)), Y)
+
+        def cc(i):
+            rc = G.lib().gtn_matmul_2d_noalloc(C.byref(X.desc()), C.byref(G.GT(ws[i % ncopy], wdt, (N, K)).desc()),
+                                               C.byref(Y.desc()), 0, C.c_void_p(stream.cuda_stream))
+            assert rc == 0, G.lib().gtn_last_error()
+
+        res = {"N": N, "K": K, "M": M}
+        for key, fn in (("tc", tc), ("cuda_cores", cc)):
+            for i in range(3):
+                fn(i)
+            reps = 2 * ncopy
+            torch.cuda.synchronize()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+            for i in range(reps):
+                fn(i)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            t = ev0.elapsed_time(ev1) / reps * 1e-3
+            cells = M * N * K / 8
+            res[key] = {"us": round(t * 1e6, 2), "T_cells_s": round(cells / t / 1e12, 3),
+                        "frac_of_epilogue_bound": round(cells / t / bound, 3)}
+        out[name] = res
+        del ws
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, rank, world, local):
     import numpy as np
     import torch
@@ -505,6 +564,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--wdtype", type=int, default=3, choices=[1, 3, 4], help="1 fp16, 3 q8, 4 q4")
+    ap.add_argument("--gemm-only", action="store_true",
+                    help="only time the exact GEMM (tensor cores vs CUDA cores) on TinyLlama shapes")
+    ap.add_argument("--gemm-m", type=int, default=128, help="with --gemm-only: activation rows")
     ap.add_argument("--gemv-only", action="store_true",
                     help="only the exact GEMV sweep on TinyLlama's shapes (M=1), e.g. for profiling")
     ap.add_argument("--gemv-shape", default=None, choices=["qkv", "o", "gate_up", "down", "lm_head"],
@@ -541,6 +603,13 @@ def main():
         return
     if args.serve:
         print(json.dumps(run_serve(args)), flush=True)
+        return
+    if args.gemm_only:
+        import torch
+
+        import gten_b200 as G
+        sweep = gemm_sweep(G, torch, args.wdtype, torch.device("cuda", 0), args.gemm_m, args.gemv_shape)
+        print(json.dumps({"gemm_sweep": sweep, "wdtype": WDT_NAMES[args.wdtype]}), flush=True)
         return
     if args.gemv_only:
         import torch

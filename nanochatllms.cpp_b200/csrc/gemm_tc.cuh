@@ -122,21 +122,23 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t phase, unsigned 
     return false;
 }
 
-// 32 consecutive TMEM columns of this warp's lane quarter (one lane per thread), waited for.
-__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
+// 16 consecutive TMEM columns of this warp's lane quarter (one lane per thread), not waited for:
+// the registers are valid after tc_wait_ld, which names them as in-out operands so that no use
+// is scheduled before the wait.
+#define TC_R16(a) "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]), \
+    "=r"(a[8]), "=r"(a[9]), "=r"(a[10]), "=r"(a[11]), "=r"(a[12]), "=r"(a[13]), "=r"(a[14]), "=r"(a[15])
+#define TC_RW16(a) "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]), \
+    "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15])
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
-        "tcgen05.wait::ld.sync.aligned;\n"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];\n"
+        : TC_R16(r)
         : "r"(taddr)
         : "memory");
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+__device__ __forceinline__ void tc_wait_ld(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" : TC_RW16(r) : : "memory");
 }
 
 // Four int8 (as bytes b0..b3 of x, each biased by `bias` so that it is 0..255) -> two fp16 pairs
@@ -412,24 +414,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
                 break;
             }
             tc_fence_after();
-#pragma unroll 1
-            for (int b2 = 0; b2 < TC_G; ++b2) {
-                const int t = s * TC_G + b2;
-                float v[32];
-                tc_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * TC_NT + half * 32), v);
-                const float da = reinterpret_cast<const float*>(atile + (size_t)t * TC_AIMG + TC_ATILE)[lane];
-                const float4* dw4 = reinterpret_cast<const float4*>(dw_s + t * TC_NT + half * 32);
+            // 16-column chunks i = 2 * block + column half: the TMEM load of chunk i + 1 is in
+            // flight while chunk i is accumulated
+            const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s * TC_G * TC_NT + half * 32);
+            uint32_t va[16], vb[16];
+            tc_ld16(tq, va);
+            tc_wait_ld(va);
 #pragma unroll
-                for (int j4 = 0; j4 < 8; ++j4) {
+            for (int i = 0; i < 2 * TC_G; ++i) {
+                uint32_t(&cur)[16] = (i & 1) ? vb : va;
+                uint32_t(&nxt)[16] = (i & 1) ? va : vb;
+                if (i + 1 < 2 * TC_G) tc_ld16(tq + (uint32_t)(((i + 1) >> 1) * TC_NT + ((i + 1) & 1) * 16), nxt);
+                const int t = s * TC_G + (i >> 1);
+                const float da = reinterpret_cast<const float*>(atile + (size_t)t * TC_AIMG + TC_ATILE)[lane];
+                const float4* dw4 = reinterpret_cast<const float4*>(dw_s + t * TC_NT + half * 32 + (i & 1) * 16);
+#pragma unroll
+                for (int j4 = 0; j4 < 4; ++j4) {
                     const float4 w = dw4[j4];
+                    const int j = (i & 1) * 16 + 4 * j4;
                     const float s0 = da * w.x, s1 = da * w.y, s2 = da * w.z, s3 = da * w.w;
-                    const float p0 = v[4 * j4] * s0, p1 = v[4 * j4 + 1] * s1;
-                    const float p2 = v[4 * j4 + 2] * s2, p3 = v[4 * j4 + 3] * s3;
-                    acc[4 * j4] = acc[4 * j4] + p0;
-                    acc[4 * j4 + 1] = acc[4 * j4 + 1] + p1;
-                    acc[4 * j4 + 2] = acc[4 * j4 + 2] + p2;
-                    acc[4 * j4 + 3] = acc[4 * j4 + 3] + p3;
+                    const float p0 = __uint_as_float(cur[4 * j4]) * s0, p1 = __uint_as_float(cur[4 * j4 + 1]) * s1;
+                    const float p2 = __uint_as_float(cur[4 * j4 + 2]) * s2, p3 = __uint_as_float(cur[4 * j4 + 3]) * s3;
+                    acc[j] = acc[j] + p0;
+                    acc[j + 1] = acc[j + 1] + p1;
+                    acc[j + 2] = acc[j + 2] + p2;
+                    acc[j + 3] = acc[j + 3] + p3;
                 }
+                if (i + 1 < 2 * TC_G) tc_wait_ld(nxt);
             }
             tc_fence_before();
             mbar_arrive(&tmem_empty[s]);
