@@ -310,13 +310,13 @@ static TmapEncodeFn tmap_encode_fn() {
 }
 
 // A weight matrix (N rows, row stride ws bytes) as a 2-D uint16 tensor [N][ws / 2] whose box is
-// 64 rows x rstr bytes (8 blocks); rows past N and bytes past the row stride read as zeros. The
+// nt rows x rstr bytes (8 blocks); rows past N and bytes past the row stride read as zeros. The
 // map holds only the address and shape, so it is cached by them.
-static bool weight_tmap(const uint8_t* W, long ws, int N, int rstr, CUtensorMap* out) {
+static bool weight_tmap(const uint8_t* W, long ws, int N, int rstr, int nt, CUtensorMap* out) {
     static std::mutex mu;
-    static std::map<std::tuple<uintptr_t, long, int, int>, CUtensorMap> cache;
+    static std::map<std::tuple<uintptr_t, long, int, int, int>, CUtensorMap> cache;
     std::lock_guard<std::mutex> lk(mu);
-    const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(W), ws, N, rstr);
+    const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(W), ws, N, rstr, nt);
     const auto it = cache.find(key);
     if (it != cache.end()) {
         *out = it->second;
@@ -326,7 +326,7 @@ static bool weight_tmap(const uint8_t* W, long ws, int N, int rstr, CUtensorMap*
     if (!fn) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)(ws / 2), (cuuint64_t)N};
     const cuuint64_t strides[1] = {(cuuint64_t)ws};
-    const cuuint32_t box[2] = {(cuuint32_t)(rstr / 2), (cuuint32_t)TC_NT};
+    const cuuint32_t box[2] = {(cuuint32_t)(rstr / 2), (cuuint32_t)nt};
     const cuuint32_t es[2] = {1, 1};
     CUtensorMap m;
     if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint8_t*>(W), dims, strides, box, es,
@@ -349,14 +349,14 @@ bool tc_fits(const uint8_t* W, long ws, int M, int wdt, int K, const TcScratch& 
            ((reinterpret_cast<uintptr_t>(W) & 15) | (uintptr_t)(ws & 15) | (reinterpret_cast<uintptr_t>(tc.p) & 15)) == 0;
 }
 
-template <int WDT>
-static cudaError_t launch_tc(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y,
-                             long ldy, const TcScratch& tc, cudaStream_t st, bool dry) {
-    constexpr size_t smem = tc_smem<WDT>();
-    cudaError_t e = ensure_smem(k_gemm_tc<WDT>, smem);
+template <int WDT, int NT>
+static cudaError_t launch_tc_nt(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y,
+                                long ldy, const TcScratch& tc, cudaStream_t st, bool dry) {
+    constexpr size_t smem = tc_smem<WDT, NT>();
+    cudaError_t e = ensure_smem(k_gemm_tc<WDT, NT>, smem);
     if (e != cudaSuccess) return e;
     CUtensorMap map;
-    if (!weight_tmap(W, ws, N, tc_rstride<WDT>(), &map)) return cudaErrorInvalidValue;
+    if (!weight_tmap(W, ws, N, tc_rstride<WDT>(), NT, &map)) return cudaErrorInvalidValue;
     if (dry) return cudaSuccess;
     const int nb = K / GTN_QBLK;
     const int cap = (int)(tc.bytes / ((size_t)nb * TC_AIMG)) * TC_MT;  // rows per pass
@@ -364,11 +364,26 @@ static cudaError_t launch_tc(const uint8_t* X, long xs, int M, const uint8_t* W,
         const int mm = std::min(cap, M - r0), tiles = (mm + TC_MT - 1) / TC_MT;
         e = launch_pdl(k_tc_expand, dim3(nb, tiles), dim3(128), 0, st, X + (long)r0 * xs, xs, mm, K, tc.p);
         if (e != cudaSuccess) return e;
-        e = launch_pdl(k_gemm_tc<WDT>, dim3((N + TC_NT - 1) / TC_NT, tiles), dim3(TC_THREADS), smem, st, map, N, K,
-                       (const uint8_t*)tc.p, mm, Y + (long)r0 * ldy, ldy, device_error_word());
+        e = launch_pdl(k_gemm_tc<WDT, NT>, dim3((N + NT - 1) / NT, tiles), dim3(TcTile<NT>::THREADS), smem, st, map,
+                       N, K, (const uint8_t*)tc.p, mm, Y + (long)r0 * ldy, ldy, device_error_word());
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+// 64-row or 32-row weight tiles, by the waves of one-CTA-per-SM grids: a 32-row CTA takes about
+// 0.71 of a 64-row CTA's time (measured on 2048 x 5632 at 64 rows: 43.9 vs 61.6 us), so the smaller
+// tile wins when 1.4 x its waves stay below the 64-row waves (e.g. 64 CTAs -> 128, one wave each;
+// not 80 -> 160, which needs a second wave).
+template <int WDT>
+static cudaError_t launch_tc(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y,
+                             long ldy, const TcScratch& tc, cudaStream_t st, bool dry) {
+    const int nb = K / GTN_QBLK;
+    const int cap = (int)(tc.bytes / ((size_t)nb * TC_AIMG)) * TC_MT;
+    const long tiles = (std::min(M, cap) + TC_MT - 1) / TC_MT, sms = sm_count();
+    const long waves64 = ((N + 63) / 64 * tiles + sms - 1) / sms, waves32 = ((N + 31) / 32 * tiles + sms - 1) / sms;
+    if (10 * waves32 < 14 * waves64) return launch_tc_nt<WDT, 32>(X, xs, M, W, ws, N, K, Y, ldy, tc, st, dry);
+    return launch_tc_nt<WDT, 64>(X, xs, M, W, ws, N, K, Y, ldy, tc, st, dry);
 }
 
 bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K, const TcScratch& tc) {

@@ -13,9 +13,9 @@
 //     below 2^18, so kind::f16 with fp32 accumulation returns L exactly. To get one lane per
 //     accumulator row, the activation tile is expanded 4x: row r = l * 32 + m of A' holds row m
 //     of the activations masked to lane l's elements (zeros elsewhere). One block (K = 32) is two
-//     MMAs (K = 16 each) into its own TMEM region of 128 lanes x 64 columns; D[l*32+m][n] = L.
+//     MMAs (K = 16 each) into its own TMEM region of 128 lanes x NT columns; D[l*32+m][n] = L.
 //   * CUDA cores: the reference's fp32 epilogue. Thread (warp w, lane m) reads TMEM lane quarter
-//     l = w % 4 (its own accumulator rows) and owns the chains (m, l, n) of 32 weight rows n; per
+//     l = w % 4 (its own accumulator rows) and owns the chains (m, l, n) of NT/2 weight rows n; per
 //     block it computes s = da * dw, p = L * s and acc = acc + p, blocks in order, so every
 //     chain is the reference's. The four lane chains of an output meet in shared memory at the
 //     end for (L0 + L1) + (L2 + L3).
@@ -26,10 +26,10 @@
 //     followed by the 32 activation scales: 8320 bytes that the GEMM fetches with one bulk copy
 //     (the image is small and stays in L2; every CTA of a row tile reads the same image);
 //   * weights: raw rows (34/18-byte blocks, 16-byte aligned row stride) through a 2-D TMA tensor
-//     map, one copy per 64 rows x 8 blocks into a 3-stage ring; each converter thread turns one
+//     map, one copy per NT rows x 8 blocks into a 3-stage ring; each converter thread turns one
 //     (row, block) into the four 16-byte K-chunk rows of the canonical fp16 tile (aligned word
 //     loads, byte permutes and one exact fp16 subtraction per pair).
-// Two groups of 4 blocks are in flight (tile, TMEM and scale slots). Roles: a producer warp
+// 512 / (4 NT) groups of 4 blocks are in flight (tile, TMEM and scale slots; all of TMEM). Roles: a producer warp
 // (copies), converter warps (weight tiles), an MMA warp, epilogue warps. Every wait is bounded (about 2 s of device time); on expiry the kernel flags the device error word,
 // waits (bounded) for its own copies and MMAs, frees its TMEM and returns.
 #pragma once
@@ -40,22 +40,31 @@
 namespace gtn {
 
 constexpr int TC_EPI_WARPS = 8;                  // epilogue warps: warp w reads TMEM lane quarter w % 4
-constexpr int TC_CONV_WARPS = 8;                 // converter warps: one (block, weight row) per thread
-constexpr int TC_CONV_THREADS = 32 * TC_CONV_WARPS;
-constexpr int TC_PROD_WARP = TC_EPI_WARPS + TC_CONV_WARPS;  // producer warp (copies)
-constexpr int TC_MMA_WARP = TC_PROD_WARP + 1;               // MMA issue warp
-constexpr int TC_THREADS = 32 * (TC_MMA_WARP + 1);
 constexpr int TC_MT = 32;                        // activation rows per CTA (x 4 lanes = 128 MMA rows)
-constexpr int TC_NT = 64;                        // weight rows per CTA (MMA N)
 constexpr int TC_G = 4;                          // blocks per group (one commit)
-constexpr int TC_S = 2;                          // groups in flight (tile / TMEM / scale slots)
 constexpr int TC_KB = 8;                         // blocks per raw weight chunk (one TMA copy)
 constexpr int TC_RS = 3;                         // raw chunk stages
-constexpr int TC_TMEM_COLS = TC_S * TC_G * TC_NT;  // 512 columns: the whole TMEM (one CTA per SM)
+constexpr int TC_TMEM_COLS = 512;                // the whole TMEM (one CTA per SM)
 constexpr int TC_ATILE = 128 * 64;               // expanded activation tile of one block: 128 rows x 32 fp16
 constexpr int TC_AIMG = TC_ATILE + TC_MT * 4;    // + the 32 activation scales (fp32): one bulk copy
-constexpr int TC_BTILE = TC_NT * 64;             // weight tile of one block: 64 rows x 32 fp16
 constexpr int TC_COMB_STRIDE = 65;               // floats per (lane, row) in the final combine (bank spread)
+
+// Tile of one CTA: NT weight rows (the MMA's N) — 64, or 32 when a grid of 64-row tiles would leave
+// SMs idle. The slots in flight fill TMEM; converter threads cover one (block, weight row) each.
+template <int NT>
+struct TcTile {
+    static constexpr int S = TC_TMEM_COLS / (TC_G * NT);  // groups in flight (tile / TMEM / scale slots)
+    static constexpr int CONV_WARPS = TC_G * NT / 32;
+    static constexpr int CONV_THREADS = 32 * CONV_WARPS;
+    static constexpr int PROD_WARP = TC_EPI_WARPS + CONV_WARPS;  // producer warp (copies)
+    static constexpr int MMA_WARP = PROD_WARP + 1;               // MMA issue warp
+    static constexpr int THREADS = 32 * (MMA_WARP + 1);
+    static constexpr int BTILE = NT * 64;  // weight tile of one block: NT rows x 32 fp16
+    static constexpr int COLS = NT / 2;    // epilogue columns per thread (two threads per row and lane)
+    // instruction descriptor: kind::f16, A = B = fp16, D = fp32, both K-major, M = 128, N = NT
+    static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+    static_assert(NT == 32 || NT == 64, "32- or 64-row tiles");
+};
 
 // Bytes of the expanded activation image of M rows and K columns (k_tc_expand's output).
 __host__ __device__ inline size_t tc_aimg_bytes(int M, int K) {
@@ -65,17 +74,16 @@ template <int WDT>
 __host__ __device__ constexpr int tc_rstride() {  // raw chunk row: 8 blocks (272 / 144 bytes)
     return TC_KB * (WDT == GTN_Q8 ? GTN_Q8_BYTES : GTN_Q4_BYTES);
 }
-template <int WDT>
+template <int WDT, int NT>
 __host__ __device__ constexpr size_t tc_smem() {
-    return 1024 + (size_t)TC_S * TC_G * (TC_AIMG + TC_BTILE) + (size_t)TC_RS * TC_NT * tc_rstride<WDT>() +
-           (size_t)TC_S * TC_G * TC_NT * sizeof(float) + 64;
+    return 1024 + (size_t)TcTile<NT>::S * TC_G * (TC_AIMG + TcTile<NT>::BTILE) +
+           (size_t)TC_RS * NT * tc_rstride<WDT>() + (size_t)TcTile<NT>::S * TC_G * NT * sizeof(float) + 64;
 }
 static_assert(tc_rstride<GTN_Q8>() % 16 == 0 && tc_rstride<GTN_Q4>() % 16 == 0, "TMA boxes are 16-byte rows");
-static_assert((size_t)4 * TC_MT * TC_COMB_STRIDE * sizeof(float) <= (size_t)TC_S * TC_G * TC_AIMG,
+static_assert((size_t)4 * TC_MT * TC_COMB_STRIDE * sizeof(float) <= (size_t)2 * TC_G * TC_AIMG,
               "the combine buffer reuses the activation tiles");
-static_assert(TC_TMEM_COLS <= 512, "TMEM has 512 columns");
+static_assert(tc_smem<GTN_Q8, 32>() <= 227 * 1024 && tc_smem<GTN_Q8, 64>() <= 227 * 1024, "shared memory");
 static_assert(TC_KB % TC_G == 0, "groups never straddle raw chunks");
-static_assert(TC_G * TC_NT == TC_CONV_THREADS, "one (block, row) pair per converter thread");
 
 // Shared-memory matrix descriptor (tcgen05): K-major, no swizzle; LBO = bytes between the two
 // 16-byte K chunks of a core-matrix row group, SBO = bytes between 8-row groups; version 1.
@@ -83,14 +91,11 @@ __device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, uint32_t lbo, uint32
     return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
-// Instruction descriptor: kind::f16, A = B = fp16, D = fp32, both K-major, M = 128, N = TC_NT.
-constexpr uint32_t TC_IDESC = (1u << 4) | ((uint32_t)(TC_NT >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t accumulate) {
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
-        "l"(a), "l"(b), "r"(TC_IDESC), "r"(accumulate)
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
@@ -207,43 +212,44 @@ static __global__ void __launch_bounds__(128) k_tc_expand(const uint8_t* __restr
 // Y[m, n] (fp32, row stride y_stride) = dot(X[m, :], W[n, :]) for Q8 activations and Q8/Q4
 // weights, bit-identical to the reference. `img`: k_tc_expand's image of X (M rows). `wmap`: the
 // weight matrix as a 2-D uint16 tensor (inner extent w_stride / 2, N rows, row stride w_stride),
-// box (tc_rstride / 2, 64); rows past N read as zeros. K / 32 a multiple of TC_G.
-// grid (ceil(N / 64), ceil(M / 32)), block TC_THREADS, dynamic shared memory tc_smem<WDT>();
+// box (tc_rstride / 2, NT); rows past N read as zeros. K / 32 a multiple of TC_G.
+// grid (ceil(N / NT), ceil(M / 32)), block TcTile<NT>::THREADS, dynamic shared memory tc_smem<WDT, NT>();
 // one CTA per SM (it holds all of TMEM).
 //
 // Roles, synchronised only by mbarriers (no block-wide barrier inside the main loop):
 //   producer warp: weight chunks (raw_full / raw_empty ring) and the A' images of group g into
-//     slot s = g % TC_S once the epilogue released the slot (tmem_empty of group g - TC_S);
+//     slot s = g % T::S once the epilogue released the slot (tmem_empty of group g - T::S);
 //   converter warps: wait for the slot and the raw chunk, write the weight tile and scales, arrive
 //     on b_full[s] (and on raw_empty once a chunk's last group is converted);
 //   MMA warp: waits for b_full[s] and a_full[s], issues the group's MMAs into TMEM slot s and
 //     commits them to mma_done[s];
 //   epilogue warps: wait mma_done[s], read the lane sums from TMEM, run the fp32 chains, release
 //     slot s (tmem_empty[s], 256 arrivals).
-template <int WDT>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap wmap, int N, int K,
+template <int WDT, int NT>
+__global__ void __launch_bounds__(TcTile<NT>::THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap wmap, int N, int K,
                                                            const uint8_t* __restrict__ img, int M,
                                                            float* __restrict__ Y, long y_stride, unsigned int* err) {
+    using T = TcTile<NT>;
     constexpr int BB = WDT == GTN_Q8 ? GTN_Q8_BYTES : GTN_Q4_BYTES;
     constexpr int RSTR = tc_rstride<WDT>();
-    constexpr uint32_t CHUNK_BYTES = (uint32_t)RSTR * TC_NT;
+    constexpr uint32_t CHUNK_BYTES = (uint32_t)RSTR * NT;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem);  // [TC_RS]
     uint64_t* raw_empty = raw_full + TC_RS;                   // [TC_RS]
-    uint64_t* a_full = raw_empty + TC_RS;                     // [TC_S]
-    uint64_t* b_full = a_full + TC_S;                         // [TC_S]
-    uint64_t* mma_done = b_full + TC_S;                       // [TC_S]
-    uint64_t* tmem_empty = mma_done + TC_S;                   // [TC_S]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + TC_S);
+    uint64_t* a_full = raw_empty + TC_RS;                     // [T::S]
+    uint64_t* b_full = a_full + T::S;                         // [T::S]
+    uint64_t* mma_done = b_full + T::S;                       // [T::S]
+    uint64_t* tmem_empty = mma_done + T::S;                   // [T::S]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + T::S);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    uint8_t* atile = smem + 1024;                             // [TC_S * TC_G][TC_AIMG]
-    uint8_t* btile = atile + TC_S * TC_G * TC_AIMG;           // [TC_S * TC_G][TC_BTILE]
-    uint8_t* raw = btile + TC_S * TC_G * TC_BTILE;            // [TC_RS][TC_NT][RSTR]
-    float* dw_s = reinterpret_cast<float*>(raw + (size_t)TC_RS * TC_NT * RSTR);  // [TC_S][TC_G][TC_NT]
+    uint8_t* atile = smem + 1024;                             // [T::S * TC_G][TC_AIMG]
+    uint8_t* btile = atile + T::S * TC_G * TC_AIMG;           // [T::S * TC_G][T::BTILE]
+    uint8_t* raw = btile + T::S * TC_G * T::BTILE;            // [TC_RS][NT][RSTR]
+    float* dw_s = reinterpret_cast<float*>(raw + (size_t)TC_RS * NT * RSTR);  // [T::S][TC_G][NT]
     float* comb = reinterpret_cast<float*>(atile);  // [4][TC_MT][TC_COMB_STRIDE], after the last MMA
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * TC_NT, nr = min(TC_NT, N - n0);
+    const int n0 = blockIdx.x * NT, nr = min(NT, N - n0);
     const int m0 = blockIdx.y * TC_MT, mr = min(TC_MT, M - m0);
     const int nb = K / GTN_QBLK, ngroups = nb / TC_G, nchunks = (nb + TC_KB - 1) / TC_KB;
     constexpr int CW0 = TC_EPI_WARPS;  // first converter warp
@@ -257,11 +263,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     if (tid == 32) {
         for (int s = 0; s < TC_RS; ++s) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], TC_CONV_THREADS);
+            mbar_init(&raw_empty[s], T::CONV_THREADS);
         }
-        for (int s = 0; s < TC_S; ++s) {
+        for (int s = 0; s < T::S; ++s) {
             mbar_init(&a_full[s], 1);
-            mbar_init(&b_full[s], TC_CONV_THREADS);
+            mbar_init(&b_full[s], T::CONV_THREADS);
             mbar_init(&mma_done[s], 1);
             mbar_init(&tmem_empty[s], 32 * TC_EPI_WARPS);
         }
@@ -273,18 +279,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    float acc[32];
+    float acc[T::COLS];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
+    for (int j = 0; j < T::COLS; ++j) acc[j] = 0.0f;
     int g_issued = 0;                // MMA warp: groups whose MMAs were issued
     int a_issued = 0, w_issued = 0;  // producer: groups of A' images and weight chunks issued
 
-    if (warp == TC_PROD_WARP) {
+    if (warp == T::PROD_WARP) {
         // ---- producer (one thread) ----
         if (lane == 0) {
             for (int c = 0; c < min(TC_RS, nchunks); ++c) {  // weights: independent of the previous kernel
                 mbar_arrive_expect_tx(&raw_full[c], CHUNK_BYTES);
-                tma_load_2d(raw + (size_t)c * TC_NT * RSTR, &wmap, c * (RSTR / 2), n0, &raw_full[c]);
+                tma_load_2d(raw + (size_t)c * NT * RSTR, &wmap, c * (RSTR / 2), n0, &raw_full[c]);
             }
             w_issued = min(TC_RS, nchunks);
             asm volatile("griddepcontrol.wait;" ::: "memory");  // the A' image comes from the pre-pass
@@ -293,8 +299,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
             while (a_issued < ngroups || w_issued < nchunks) {
                 bool progressed = false;
                 if (a_issued < ngroups) {
-                    const int g = a_issued, s = g % TC_S;
-                    if (g < TC_S || mbar_test(&tmem_empty[s], (uint32_t)(g / TC_S - 1) & 1u)) {
+                    const int g = a_issued, s = g % T::S;
+                    if (g < T::S || mbar_test(&tmem_empty[s], (uint32_t)(g / T::S - 1) & 1u)) {
                         mbar_arrive_expect_tx(&a_full[s], (uint32_t)(TC_G * TC_AIMG));
                         for (int blk = 0; blk < TC_G; ++blk)
                             bulk_g2s(atile + (size_t)(s * TC_G + blk) * TC_AIMG,
@@ -307,7 +313,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
                     const int c = w_issued, st = c % TC_RS;
                     if (mbar_test(&raw_empty[st], (uint32_t)(c / TC_RS - 1) & 1u)) {
                         mbar_arrive_expect_tx(&raw_full[st], CHUNK_BYTES);
-                        tma_load_2d(raw + (size_t)st * TC_NT * RSTR, &wmap, c * (RSTR / 2), n0, &raw_full[st]);
+                        tma_load_2d(raw + (size_t)st * NT * RSTR, &wmap, c * (RSTR / 2), n0, &raw_full[st]);
                         ++w_issued;
                         progressed = true;
                     }
@@ -324,23 +330,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
             }
         }
         __syncwarp();
-    } else if (warp >= CW0 && warp < CW0 + TC_CONV_WARPS) {
+    } else if (warp >= CW0 && warp < CW0 + T::CONV_WARPS) {
         // ---- converters: thread -> (block blk of the group, weight row n); the whole 32-element
         // block is read as aligned words (the block data starts 2 bytes past a word boundary in even
         // blocks) and written as the four 16-byte K-chunk rows of the fp16 tile ----
         const int ct = tid - 32 * CW0;
-        const int blk = ct / TC_NT, n = ct % TC_NT;
+        const int blk = ct / NT, n = ct % NT;
         for (int g = 0; g < ngroups; ++g) {
-            const int s = g % TC_S, chunk = (g * TC_G) / TC_KB, stage = chunk % TC_RS;
+            const int s = g % T::S, chunk = (g * TC_G) / TC_KB, stage = chunk % TC_RS;
             bool ok = *abort_flag == 0;
-            if (ok && g >= TC_S) ok = tc_wait(&tmem_empty[s], (uint32_t)(g / TC_S - 1) & 1u, err);
+            if (ok && g >= T::S) ok = tc_wait(&tmem_empty[s], (uint32_t)(g / T::S - 1) & 1u, err);
             if (ok) ok = tc_wait(&raw_full[stage], (uint32_t)(chunk / TC_RS) & 1u, err);
             if (ok) {
                 const int boff = ((g * TC_G + blk) % TC_KB) * BB;  // block offset in the raw row
-                const uint8_t* row = raw + (size_t)stage * TC_NT * RSTR + (size_t)n * RSTR;
+                const uint8_t* row = raw + (size_t)stage * NT * RSTR + (size_t)n * RSTR;
                 const int sh = ((boff + 2) & 3) * 8;                // 16 (even blocks) or 0 bits
                 const uint32_t* wp = reinterpret_cast<const uint32_t*>(row + ((boff + 2) & ~3));
-                uint8_t* dst = btile + (size_t)(s * TC_G + blk) * TC_BTILE + (n >> 3) * 512 + (n & 7) * 16;
+                uint8_t* dst = btile + (size_t)(s * TC_G + blk) * T::BTILE + (n >> 3) * 512 + (n & 7) * 16;
                 if (WDT == GTN_Q8) {
                     uint32_t w[9], d[8];
 #pragma unroll
@@ -369,7 +375,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
                         *reinterpret_cast<uint4*>(dst + c * 128) = make_uint4(lo.x, lo.y, hi.x, hi.y);
                     }
                 }
-                dw_s[s * TC_G * TC_NT + ct] = h2f(ld_u16(row + boff));  // rows past N are zeros (scale 0)
+                dw_s[s * TC_G * NT + ct] = h2f(ld_u16(row + boff));  // rows past N are zeros (scale 0)
                 fence_async_smem();  // generic-proxy tile writes -> visible to the tensor cores
             }
             if (!ok) {
@@ -379,12 +385,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
             mbar_arrive(&b_full[s]);
             if ((g + 1) * TC_G % TC_KB == 0 || g + 1 == ngroups) mbar_arrive(&raw_empty[stage]);  // chunk done
         }
-    } else if (warp == TC_MMA_WARP) {
+    } else if (warp == T::MMA_WARP) {
         // ---- MMA issue (one thread) ----
         if (lane == 0) {
             for (int g = 0; g < ngroups; ++g) {
-                const int s = g % TC_S;
-                const uint32_t ph = (uint32_t)(g / TC_S) & 1u;
+                const int s = g % T::S;
+                const uint32_t ph = (uint32_t)(g / T::S) & 1u;
                 if (*abort_flag != 0 || !tc_wait(&b_full[s], ph, err) || !tc_wait(&a_full[s], ph, err)) {
                     *abort_flag = 1;
                     break;
@@ -394,10 +400,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
                 for (int b2 = 0; b2 < TC_G; ++b2) {
                     const int t = s * TC_G + b2;
                     const uint32_t a = smem_u32(atile + (size_t)t * TC_AIMG);
-                    const uint32_t b = smem_u32(btile + (size_t)t * TC_BTILE);
-                    const uint32_t d = tmem + (uint32_t)(t * TC_NT);
-                    tc_mma(d, tc_desc(a, 128, 512), tc_desc(b, 128, 512), 0u);
-                    tc_mma(d, tc_desc(a + 256, 128, 512), tc_desc(b + 256, 128, 512), 1u);
+                    const uint32_t b = smem_u32(btile + (size_t)t * T::BTILE);
+                    const uint32_t d = tmem + (uint32_t)(t * NT);
+                    tc_mma(d, tc_desc(a, 128, 512), tc_desc(b, 128, 512), T::IDESC, 0u);
+                    tc_mma(d, tc_desc(a + 256, 128, 512), tc_desc(b + 256, 128, 512), T::IDESC, 1u);
                 }
                 tc_commit(&mma_done[s]);
                 g_issued = g + 1;
@@ -408,30 +414,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         // ---- epilogue: thread (quarter q = reference lane l, column half, row m = lane) ----
         const int q = warp & 3, half = warp >> 2;
         for (int g = 0; g < ngroups; ++g) {
-            const int s = g % TC_S;
-            if (*abort_flag != 0 || !tc_wait(&mma_done[s], (uint32_t)(g / TC_S) & 1u, err)) {
+            const int s = g % T::S;
+            if (*abort_flag != 0 || !tc_wait(&mma_done[s], (uint32_t)(g / T::S) & 1u, err)) {
                 *abort_flag = 1;
                 break;
             }
             tc_fence_after();
-            // 16-column chunks i = 2 * block + column half: the TMEM load of chunk i + 1 is in
-            // flight while chunk i is accumulated
-            const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s * TC_G * TC_NT + half * 32);
+            // 16-column chunks i = CPB * block + sub: the TMEM load of chunk i + 1 is in flight while
+            // chunk i is accumulated
+            constexpr int CPB = T::COLS / 16, NCH = TC_G * CPB;
+            const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s * TC_G * NT + half * T::COLS);
             uint32_t va[16], vb[16];
             tc_ld16(tq, va);
             tc_wait_ld(va);
 #pragma unroll
-            for (int i = 0; i < 2 * TC_G; ++i) {
+            for (int i = 0; i < NCH; ++i) {
                 uint32_t(&cur)[16] = (i & 1) ? vb : va;
                 uint32_t(&nxt)[16] = (i & 1) ? va : vb;
-                if (i + 1 < 2 * TC_G) tc_ld16(tq + (uint32_t)(((i + 1) >> 1) * TC_NT + ((i + 1) & 1) * 16), nxt);
-                const int t = s * TC_G + (i >> 1);
+                if (i + 1 < NCH) tc_ld16(tq + (uint32_t)(((i + 1) / CPB) * NT + ((i + 1) % CPB) * 16), nxt);
+                const int t = s * TC_G + i / CPB, sub = i % CPB;
                 const float da = reinterpret_cast<const float*>(atile + (size_t)t * TC_AIMG + TC_ATILE)[lane];
-                const float4* dw4 = reinterpret_cast<const float4*>(dw_s + t * TC_NT + half * 32 + (i & 1) * 16);
+                const float4* dw4 = reinterpret_cast<const float4*>(dw_s + t * NT + half * T::COLS + sub * 16);
 #pragma unroll
                 for (int j4 = 0; j4 < 4; ++j4) {
                     const float4 w = dw4[j4];
-                    const int j = (i & 1) * 16 + 4 * j4;
+                    const int j = sub * 16 + 4 * j4;
                     const float s0 = da * w.x, s1 = da * w.y, s2 = da * w.z, s3 = da * w.w;
                     const float p0 = __uint_as_float(cur[4 * j4]) * s0, p1 = __uint_as_float(cur[4 * j4 + 1]) * s1;
                     const float p2 = __uint_as_float(cur[4 * j4 + 2]) * s2, p3 = __uint_as_float(cur[4 * j4 + 3]) * s3;
@@ -440,7 +447,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
                     acc[j + 2] = acc[j + 2] + p2;
                     acc[j + 3] = acc[j + 3] + p3;
                 }
-                if (i + 1 < 2 * TC_G) tc_wait_ld(nxt);
+                if (i + 1 < NCH) tc_wait_ld(nxt);
             }
             tc_fence_before();
             mbar_arrive(&tmem_empty[s]);
@@ -453,11 +460,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         if (warp < TC_EPI_WARPS) {
             const int q = warp & 3, half = warp >> 2;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) comb[(q * TC_MT + lane) * TC_COMB_STRIDE + half * 32 + j] = acc[j];
+            for (int j = 0; j < T::COLS; ++j) comb[(q * TC_MT + lane) * TC_COMB_STRIDE + half * T::COLS + j] = acc[j];
         }
         __syncthreads();
-        for (int i = tid; i < TC_MT * TC_NT; i += TC_THREADS) {
-            const int m = i / TC_NT, n = i % TC_NT;
+        for (int i = tid; i < TC_MT * NT; i += T::THREADS) {
+            const int m = i / NT, n = i % NT;
             if (m < mr && n < nr) {
                 const float c0 = comb[(0 * TC_MT + m) * TC_COMB_STRIDE + n], c1 = comb[(1 * TC_MT + m) * TC_COMB_STRIDE + n];
                 const float c2 = comb[(2 * TC_MT + m) * TC_COMB_STRIDE + n], c3 = comb[(3 * TC_MT + m) * TC_COMB_STRIDE + n];
@@ -467,12 +474,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     } else {
         // an expired wait: let this CTA's MMAs and copies finish (bounded) before its TMEM and
         // shared memory are released; each slot / stage has at most one outstanding phase
-        if (tid == 32 * TC_MMA_WARP)
-            for (int g2 = max(0, g_issued - TC_S); g2 < g_issued; ++g2)
-                tc_wait(&mma_done[g2 % TC_S], (uint32_t)(g2 / TC_S) & 1u, err);
-        if (tid == 32 * TC_PROD_WARP) {
-            for (int g2 = max(0, a_issued - TC_S); g2 < a_issued; ++g2)
-                tc_wait(&a_full[g2 % TC_S], (uint32_t)(g2 / TC_S) & 1u, err);
+        if (tid == 32 * T::MMA_WARP)
+            for (int g2 = max(0, g_issued - T::S); g2 < g_issued; ++g2)
+                tc_wait(&mma_done[g2 % T::S], (uint32_t)(g2 / T::S) & 1u, err);
+        if (tid == 32 * T::PROD_WARP) {
+            for (int g2 = max(0, a_issued - T::S); g2 < a_issued; ++g2)
+                tc_wait(&a_full[g2 % T::S], (uint32_t)(g2 / T::S) & 1u, err);
             for (int c = max(0, w_issued - TC_RS); c < w_issued; ++c)
                 tc_wait(&raw_full[c % TC_RS], (uint32_t)(c / TC_RS) & 1u, err);
         }
