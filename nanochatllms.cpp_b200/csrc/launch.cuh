@@ -129,7 +129,7 @@ cudaError_t gemv_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, 
 // rows, same `padded` precondition): the tensor-core kernel k_gemm_tc from TC_MIN_M rows on when
 // `tc` scratch is given, else k_gemm3 on the CUDA cores; `dry` only configures shared memory and
 // prepares the weight tensor map (so that a later launch can be captured into a CUDA graph).
-constexpr int TC_MIN_M = 32;
+constexpr int TC_MIN_M = 16;
 bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K, const TcScratch& tc = TcScratch());
 cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
                    long ldy, cudaStream_t st, bool dry, const TcScratch& tc = TcScratch());

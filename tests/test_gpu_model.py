@@ -57,8 +57,8 @@ def test_custom_model_matches_oracle(orc, gpu, name, wdt):
 @pytest.mark.parametrize("batch", [3, 11, 20, 40])
 def test_batched_generation_matches_single_sequences(orc, gpu, name, wdt, batch):
     """The reference has no batching: each sequence of a batch must produce exactly the ids the
-    oracle gives for it alone (batch 11 exercises a second 8-row tile of the fused GEMVs; 20 runs
-    two 16-row tiles of the CUDA-core GEMM, 40 the tensor-core GEMM with a partial second row tile)."""
+    oracle gives for it alone (batch 11 exercises a second 8-row tile of the fused GEMVs; 20 and
+    40 run the decode steps' projections on the tensor-core GEMM, 40 with a partial second row tile)."""
     from oracle.oracle import OracleModel
     dims = CUSTOM[name]
     img = gtenfile.synthetic_image(6, wdt, 77, cpu_pack(orc), dims=dims, std=0.05, gain_std=0.1)
