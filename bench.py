@@ -363,7 +363,9 @@ def run_ours(args, rank, world, local):
     return result
 
 
-BATCH_MODELS = {"tinyllama": ("TinyLlama-1.1B", 0), "minicpm": ("MiniCPM-2B", 2)}
+BATCH_MODELS = {"tinyllama": ("TinyLlama-1.1B", 0), "zephyr": ("StableLM-2-Zephyr-1.6B", 1),
+                "minicpm": ("MiniCPM-2B", 2)}
+BATCH_PROMPT = {"tinyllama": N_PROMPT, "zephyr": 512, "minicpm": 128}  # BASELINE configs[0], [2], [3]
 
 
 def run_batch(args, rank, world, local):
@@ -380,7 +382,7 @@ def run_batch(args, rank, world, local):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     name, kind = BATCH_MODELS[args.model]
-    n_prompt = 128 if args.model == "minicpm" else N_PROMPT
+    n_prompt = BATCH_PROMPT[args.model]
     start, count = shard_range(args.batch, world, rank)
     m = G.Model(kind, args.wdtype, n_prompt + N_GEN, max(1, count))
     m.load(gtenfile.synthetic_image_device(kind, args.wdtype, SEED))
