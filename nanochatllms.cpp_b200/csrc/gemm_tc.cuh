@@ -29,9 +29,10 @@
 //     map, one copy per NT rows x 8 blocks into a 3-stage ring; each converter thread turns one
 //     (row, block) into the four 16-byte K-chunk rows of the canonical fp16 tile (aligned word
 //     loads, byte permutes and one exact fp16 subtraction per pair).
-// 512 / (4 NT) groups of 4 blocks are in flight (tile, TMEM and scale slots; all of TMEM). Roles: a producer warp
-// (copies), converter warps (weight tiles), an MMA warp, epilogue warps. Every wait is bounded (about 2 s of device time); on expiry the kernel flags the device error word,
-// waits (bounded) for its own copies and MMAs, frees its TMEM and returns.
+// 512 / (4 NT) groups of 4 blocks are in flight (tile, TMEM and scale slots; all of TMEM).
+// Roles: a producer warp (copies), converter warps (weight tiles), an MMA warp, epilogue warps.
+// Every wait is bounded (about 2 s of device time); on expiry the kernel flags the device error
+// word, waits (bounded) for its own copies and MMAs, frees its TMEM and returns.
 #pragma once
 #include <cuda.h>
 
