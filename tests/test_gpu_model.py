@@ -52,6 +52,23 @@ def test_custom_model_matches_oracle(orc, gpu, name, wdt):
     m.close()
 
 
+def test_long_prefill_in_passes_matches_oracle(orc, gpu):
+    """A 520-token prefill: the engine's activation image for the tensor-core GEMM holds 512 rows,
+    so each projection runs in two passes (512 rows, then 8); logits and greedy ids must still be
+    the oracle's bit for bit."""
+    from oracle.oracle import OracleModel
+    dims = CUSTOM["llama"]
+    img = gtenfile.synthetic_image(6, Q8, 31, cpu_pack(orc), dims=dims, std=0.05, gain_std=0.1)
+    n_prompt, n_gen = 520, 4
+    max_ctx = 2 * (n_prompt + n_gen)
+    prompt = np.random.default_rng(8).integers(0, dims[0], n_prompt).astype(np.int32)
+    m = G.Model(G.CUSTOM, Q8, max_ctx, dims=dims)
+    m.load(img)
+    assert np.array_equal(m.logits(prompt, 0), OracleModel(orc, 6, Q8, max_ctx, img, dims=dims).logits(prompt, 0))
+    assert np.array_equal(m.generate(prompt, n_gen), OracleModel(orc, 6, Q8, max_ctx, img, dims=dims).greedy(prompt, n_gen))
+    m.close()
+
+
 @pytest.mark.parametrize("name", list(CUSTOM))
 @pytest.mark.parametrize("wdt", [Q8, Q4])
 @pytest.mark.parametrize("batch", [3, 11, 20, 40])
