@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(TcTile<NT>::THREADS, 1) k_gemm_tc(const __grid
     constexpr int BB = WDT == GTN_Q8 ? GTN_Q8_BYTES : GTN_Q4_BYTES;
     constexpr int RSTR = tc_rstride<WDT>();
     constexpr uint32_t CHUNK_BYTES = (uint32_t)RSTR * NT;
-    extern __shared__ __align__(1024) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];  // every TMA destination and MMA tile sits at a 128-byte multiple
     uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem);  // [TC_RS]
     uint64_t* raw_empty = raw_full + TC_RS;                   // [TC_RS]
     uint64_t* a_full = raw_empty + TC_RS;                     // [T::S]
