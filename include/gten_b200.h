@@ -171,7 +171,8 @@ enum {
  * KV capacity for `max_ctx` tokens per sequence and `max_batch` independent sequences.
  * The reference's constructor is Model(n_ctx, dtype) (tinyllama.h:52 and siblings).
  * For GTN_MODEL_CUSTOM, dims = {n_vocab, n_embd, n_layers, n_heads, n_kv_heads, n_ffn, family}
- * with family 0 = TinyLlama-like, 1 = Zephyr-like, 2 = MiniCPM-like; otherwise dims may be NULL. */
+ * with family 0 = TinyLlama-like, 1 = Zephyr-like, 2 = MiniCPM-like, 3 = OpenELM-like (QK-norm; the
+ * same head and FFN widths in every layer); otherwise dims may be NULL. */
 int gtn_model_create(int kind, int wdtype, int max_ctx, int max_batch, const int32_t* dims, gtn_model** out);
 void gtn_model_free(gtn_model* m);
 int gtn_model_n_vocab(const gtn_model* m);
@@ -204,8 +205,7 @@ int gtn_model_generate_topk(gtn_model* m, const int32_t* prompt, int n_prompt, i
 
 /* greedy_sample for `batch` independent sequences (the reference has no batching: each sequence
  * gives exactly the ids it would give alone). prompts: host [batch][n_prompt]; out_tokens: host
- * [batch][n_gen]. batch <= max_batch; Q8/Q4 models of the TinyLlama, Zephyr and MiniCPM families.
- * Synchronous. */
+ * [batch][n_gen]. batch <= max_batch; any model kind and weight dtype. Synchronous. */
 int gtn_model_generate_batch(gtn_model* m, const int32_t* prompts, int batch, int n_prompt, int n_gen,
                              int32_t* out_tokens);
 
@@ -214,8 +214,8 @@ int gtn_model_generate_batch(gtn_model* m, const int32_t* prompts, int batch, in
  * the device; gtn_model_check reports violations. */
 int gtn_model_generate_device(gtn_model* m, const int32_t* prompt, int n_prompt, int n_gen, int32_t* out_tokens);
 
-/* Continuous batching over the model's max_batch slots (greedy; Q8/Q4 models of the TinyLlama,
- * Zephyr and MiniCPM families). The reference decodes one sequence per greedy_sample call
+/* Continuous batching over the model's max_batch slots (greedy; any model kind and weight dtype).
+ * The reference decodes one sequence per greedy_sample call
  * (sampler.cpp:11-53); here sequences of any prompt length join and leave a running batch:
  *   gtn_slot_start   prefills a prompt (host int32) into a free slot, returns the slot and the
  *                    first greedy id; fails when every slot is busy;

@@ -108,7 +108,7 @@ static cudaError_t launch_mm_q(const uint8_t* X, long xs, int M, const uint8_t* 
 
 template <int NW>
 static cudaError_t launch_mm_f16(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y,
-                                 long ldy, cudaStream_t st, int mt) {
+                                 long ldy, cudaStream_t st, int mt, bool dry = false) {
     const dim3 grid((N + NW * 4 - 1) / (NW * 4), (M + mt - 1) / mt);
     const size_t smem = mm_f16_smem(NW, mt, K);
     unsigned int* err = device_error_word();
@@ -116,7 +116,7 @@ static cudaError_t launch_mm_f16(const uint8_t* X, long xs, int M, const uint8_t
 #define GTN_MMF(MTV)                                                                              \
     case MTV:                                                                                     \
         e = ensure_smem(k_mm_f16<NW, MTV>, smem);                                                 \
-        if (e != cudaSuccess) return e;                                                           \
+        if (e != cudaSuccess || dry) return e;                                                    \
         return launch_pdl(k_mm_f16<NW, MTV>, grid, dim3(NW * 32), smem, st, W, ws, N, K, X, xs, M, Y, ldy, err);
     switch (mt) {
         GTN_MMF(1)
@@ -407,6 +407,18 @@ cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, 
     return cudaErrorInvalidValue;
 }
 
+cudaError_t gemm_f16(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y, long ldy,
+                     cudaStream_t st, bool dry) {
+    const int mt = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
+    int nw = 4;
+    while (nw > 1 && (N + nw * 4 - 1) / (nw * 4) < 296) nw >>= 1;
+    int mtv = mt;
+    while (mtv > 1 && mm_f16_smem(nw, mtv, K) > 200 * 1024) mtv >>= 1;
+    if (nw == 4) return launch_mm_f16<4>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv, dry);
+    if (nw == 2) return launch_mm_f16<2>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv, dry);
+    return launch_mm_f16<1>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv, dry);
+}
+
 static cudaError_t matmul_tma(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K,
                               float* Y, long ldy, cudaStream_t st, const TcScratch& tc) {
     if (gemv_q_fits(M, wdt, K)) return gemv_q(X, xs, M, W, ws, wdt, N, K, Y, ldy, st, false);
@@ -415,15 +427,7 @@ static cudaError_t matmul_tma(const uint8_t* X, long xs, int M, const uint8_t* W
     if (wdt == GTN_Q8 && gm3_plan<GTN_Q8>(W, ws, M, K, &gp)) return launch_gm3<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, gp, st);
     if (wdt == GTN_Q4 && gm3_plan<GTN_Q4>(W, ws, M, K, &gp)) return launch_gm3<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, gp, st);
     const int mt = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
-    if (wdt == GTN_F16) {
-        int nw = 4;
-        while (nw > 1 && (N + nw * 4 - 1) / (nw * 4) < 296) nw >>= 1;
-        int mtv = mt;
-        while (mtv > 1 && mm_f16_smem(nw, mtv, K) > 200 * 1024) mtv >>= 1;
-        if (nw == 4) return launch_mm_f16<4>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv);
-        if (nw == 2) return launch_mm_f16<2>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv);
-        return launch_mm_f16<1>(X, xs, M, W, ws, N, K, Y, ldy, st, mtv);
-    }
+    if (wdt == GTN_F16) return gemm_f16(X, xs, M, W, ws, N, K, Y, ldy, st, false);
     int nw = 4;
     while (nw > 1 && (N + nw * 8 - 1) / (nw * 8) < 296) nw >>= 1;
     int mtv = mt;
@@ -571,6 +575,49 @@ static int rowop(const gtn_tensor* a, const gtn_tensor* b, gtn_tensor* out, floa
     return cuda_status(e, name);
 }
 
+namespace gtn {
+
+// ops.cpp:617-636: the argument checks of matmul_2d, shared by gtn_matmul_2d and
+// gtn_matmul_2d_noalloc (`who` prefixes the error text).
+int matmul_args(const gtn_tensor* x, const gtn_tensor* w, const gtn_tensor* out, int start_pos, const char* who,
+                MatmulArgs* a) {
+    GTN_CHECK(check_tensor(x, "x"));
+    GTN_CHECK(check_tensor(w, "w"));
+    GTN_CHECK(check_tensor(out, "out"));
+    GTN_REQUIRE(x->ndim == 2, "%s: x must be 2-D", who);
+    GTN_REQUIRE(w->ndim == 2 && w->shape[1] == x->shape[1], "%s: w must be [n_out, n_embd]", who);
+    const int n_ctx = x->shape[0], K = x->shape[1], N = w->shape[0];
+    GTN_REQUIRE(start_pos >= 0 && start_pos < n_ctx, "%s: start_pos %d out of [0, %d)", who, start_pos, n_ctx);
+    if (out->ndim == 1) {
+        GTN_REQUIRE(n_ctx - start_pos == 1, "%s: 1-D out needs exactly one new row", who);
+        GTN_REQUIRE(out->shape[0] == N, "%s: out shape", who);
+    } else {
+        GTN_REQUIRE(out->ndim == 2 && out->shape[0] == n_ctx && out->shape[1] == N, "%s: out shape", who);
+    }
+    const bool q = x->dtype == GTN_Q8 && (w->dtype == GTN_Q8 || w->dtype == GTN_Q4);
+    const bool h = x->dtype == GTN_F16 && w->dtype == GTN_F16;
+    GTN_REQUIRE(q || h, "%s: unsupported dtypes x=%d w=%d", who, x->dtype, w->dtype);
+    GTN_REQUIRE(K % GTN_QBLK == 0 || h, "%s: n_embd %d not a multiple of 32", who, K);
+    GTN_REQUIRE(out->dtype == GTN_F32 || out->dtype == x->dtype, "%s: out dtype", who);
+    a->quant = q;
+    a->M = n_ctx - start_pos;
+    a->N = N;
+    a->K = K;
+    a->X = (const uint8_t*)x->data + (long)start_pos * bstride(x, 0);
+    a->xs = bstride(x, 0);
+    a->xdt = x->dtype;
+    a->W = (const uint8_t*)w->data;
+    a->ws = bstride(w, 0);
+    a->wdt = w->dtype;
+    a->os = out->ndim == 1 ? 0 : bstride(out, 0);
+    a->odt = out->dtype;
+    a->out = (uint8_t*)out->data;
+    a->one_d = out->ndim == 1;
+    return GTN_OK;
+}
+
+}  // namespace gtn
+
 extern "C" {
 
 const char* gtn_last_error(void) { return g_last_error.c_str(); }
@@ -579,31 +626,13 @@ unsigned long long gtn_kernel_launches(void) { return g_launches.load(); }
 
 // ops.cpp:617-636
 int gtn_matmul_2d(const gtn_tensor* x, const gtn_tensor* w, gtn_tensor* out, int start_pos, void* stream) {
-    GTN_CHECK(check_tensor(x, "x"));
-    GTN_CHECK(check_tensor(w, "w"));
-    GTN_CHECK(check_tensor(out, "out"));
-    GTN_REQUIRE(x->ndim == 2, "matmul_2d: x must be 2-D");
-    GTN_REQUIRE(w->ndim == 2 && w->shape[1] == x->shape[1], "matmul_2d: w must be [n_out, n_embd]");
-    const int n_ctx = x->shape[0], K = x->shape[1], N = w->shape[0];
-    GTN_REQUIRE(start_pos >= 0 && start_pos < n_ctx, "matmul_2d: start_pos %d out of [0, %d)", start_pos, n_ctx);
-    if (out->ndim == 1) {
-        GTN_REQUIRE(n_ctx - start_pos == 1, "matmul_2d: 1-D out needs exactly one new row");
-        GTN_REQUIRE(out->shape[0] == N, "matmul_2d: out shape");
-    } else {
-        GTN_REQUIRE(out->ndim == 2 && out->shape[0] == n_ctx && out->shape[1] == N, "matmul_2d: out shape");
-    }
-    const bool q = x->dtype == GTN_Q8 && (w->dtype == GTN_Q8 || w->dtype == GTN_Q4);
-    const bool h = x->dtype == GTN_F16 && w->dtype == GTN_F16;
-    GTN_REQUIRE(q || h, "matmul_2d: unsupported dtypes x=%d w=%d", x->dtype, w->dtype);
-    GTN_REQUIRE(K % GTN_QBLK == 0 || h, "matmul_2d: n_embd %d not a multiple of 32", K);
-    GTN_REQUIRE(out->dtype == GTN_F32 || out->dtype == x->dtype, "matmul_2d: out dtype");
-    const int M = n_ctx - start_pos;
-    const uint8_t* X = (const uint8_t*)x->data + (long)start_pos * bstride(x, 0);
-    const long os = out->ndim == 1 ? 0 : bstride(out, 0);
+    MatmulArgs a;
+    GTN_CHECK(matmul_args(x, w, out, start_pos, "matmul_2d", &a));
+    const int M = a.M, N = a.N, K = a.K;
     cudaStream_t st = S(stream);
     // the tensor-core path's expanded activation image (stream-ordered scratch, freed below)
     TcScratch tc;
-    if (q && M >= TC_MIN_M && K % GTN_QBLK == 0) {
+    if (a.quant && M >= TC_MIN_M && K % GTN_QBLK == 0) {
         tc.bytes = tc_aimg_bytes(M, K);
         if (cudaMallocAsync((void**)&tc.p, tc.bytes, st) != cudaSuccess) {
             cudaGetLastError();
@@ -611,19 +640,17 @@ int gtn_matmul_2d(const gtn_tensor* x, const gtn_tensor* w, gtn_tensor* out, int
         }
     }
     cudaError_t e;
-    if (out->dtype == GTN_F32) {
-        float* Y = (float*)((uint8_t*)out->data + (long)start_pos * os);
-        e = matmul_f32(X, bstride(x, 0), x->dtype, M, (const uint8_t*)w->data, bstride(w, 0), w->dtype, N, K, Y,
-                       out->ndim == 1 ? 0 : N, st, false, tc);
+    if (a.odt == GTN_F32) {
+        float* Y = (float*)(a.out + (long)start_pos * a.os);
+        e = matmul_f32(a.X, a.xs, a.xdt, M, a.W, a.ws, a.wdt, N, K, Y, a.one_d ? 0 : N, st, false, tc);
     } else {
         float* Y = nullptr;
         e = cudaMallocAsync((void**)&Y, sizeof(float) * (size_t)M * N, st);
         if (e == cudaSuccess) {
-            e = matmul_f32(X, bstride(x, 0), x->dtype, M, (const uint8_t*)w->data, bstride(w, 0), w->dtype, N, K, Y, N,
-                           st, false, tc);
+            e = matmul_f32(a.X, a.xs, a.xdt, M, a.W, a.ws, a.wdt, N, K, Y, N, st, false, tc);
             if (e == cudaSuccess)
                 e = launch_pdl(k_write_rows, dim3(((N + GTN_QBLK - 1) / GTN_QBLK + 3) / 4, M), dim3(128), 0, st,
-                               (const float*)Y, (long)N, (uint8_t*)out->data, os, (int)out->dtype, N, start_pos);
+                               (const float*)Y, (long)N, a.out, a.os, a.odt, N, start_pos);
             cudaFreeAsync(Y, st);
         }
     }

@@ -193,7 +193,7 @@ int gtn_model_create(int kind, int wdtype, int max_ctx, int max_batch, const int
             if (!dims) return fail(GTN_ERR_ARG, "model_create: custom model needs dims");
             m->n_vocab = dims[0]; m->d = dims[1]; m->nl = dims[2]; nh = dims[3]; nkv = dims[4]; nff = dims[5];
             m->family = dims[6];
-            if (m->family < 0 || m->family > 2) return fail(GTN_ERR_ARG, "model_create: family %d", m->family);
+            if (m->family < 0 || m->family > 3) return fail(GTN_ERR_ARG, "model_create: family %d", m->family);
             if (m->family == 1) m->rope_pct = 0.25f;
             if (m->n_vocab <= 0 || m->d <= 0 || m->d % 64 || m->nl <= 0 || nh <= 0 || nkv <= 0 || nh % nkv ||
                 nff <= 0 || nff % 32)
@@ -252,7 +252,7 @@ int gtn_model_create(int kind, int wdtype, int max_ctx, int max_batch, const int
         rc |= dalloc(m.get(), &m->L[l].kc, kvb);
         rc |= dalloc(m.get(), &m->L[l].vc, kvb);
     }
-    m->fused = (m->wdt == GTN_Q8 || m->wdt == GTN_Q4) && m->family <= 2 && m->dh == 64;
+    m->fused = m->dh == 64;
     if (rc == GTN_OK && m->fused) {
         const long B = max_batch;
         m->ldqkv = m->max_q + 2L * m->max_kv;
@@ -735,8 +735,8 @@ static cudaError_t fg_mt(const FArgs& a, cudaStream_t st, bool dry) {
     return big ? fg_launch<WDT, 4, 8, PRO>(a, st, dry) : fg_launch<WDT, 1, 8, PRO>(a, st, dry);
 }
 
-// A GEMV whose activation needs a prologue (residual + norm, or SwiGLU) runs it once in k_prep
-// (one CTA per sequence) into m->act; the GEMV then copies that row.
+// A GEMV whose activation needs a prologue runs it once into m->act (residual + norm: k_prep_cl,
+// one cluster per sequence; SwiGLU: k_prep_swiglu); the GEMV then reads that row.
 static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) {
     FArgs g = a;
     if (pro != PRO_COPY) {
@@ -761,6 +761,10 @@ static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) 
         if (e != cudaSuccess) return e;
         g.xin = m->act;
         g.xin_s = m->act_s;
+    }
+    if (m->wdt == GTN_F16) {  // fp16 weights and activations: the exact 8-lane CUDA-core kernel
+        if (!dry) ++g_step_kernels;
+        return gemm_f16(g.xin, g.xin_s, g.B, g.W, g.ws, g.N, g.K, g.Y, g.ldy, m->st, dry);
     }
     if (gemv_q_fits(g.B, m->wdt, g.K)) {
         if (!dry) ++g_step_kernels;
@@ -828,6 +832,7 @@ static int decode_step(gtn_model* m, int B, bool dry) {
         AArgs at{};
         at.adt = adt; at.q_heads = Ly.nh; at.kv_heads = Ly.nkv; at.d = dh; at.pos = m->pos;
         at.y = m->yqkv; at.ys = m->ldqkv; at.bq = Ly.bq; at.bk = Ly.bk; at.bv = Ly.bv;
+        at.qnw = Ly.qnw; at.knw = Ly.knw;
         at.cs = m->rope; at.half = m->rd / 2; at.kc = Ly.kc; at.vc = Ly.vc; at.kvs = m->kv_rs;
         at.khs = (long)m->max_ctx * m->kv_rs; at.seq_stride = (long)Ly.nkv * at.khs;
         at.out = m->datt; at.os = row_bytes(adt, m->max_q); at.err = err; at.active = act_mask;
@@ -1053,7 +1058,7 @@ int gtn_model_generate_batch(gtn_model* m, const int32_t* prompts, int batch, in
     if (batch > m->max_batch) return fail(GTN_ERR_ARG, "model_generate_batch: batch %d > max_batch %d", batch, m->max_batch);
     if (n_prompt + n_gen - 1 > m->max_ctx) return fail(GTN_ERR_ARG, "model_generate_batch: exceeds max_ctx");
     if (slots_busy(m)) return fail(GTN_ERR_ARG, "model_generate_batch: slots are in use");
-    if (!m->fused) return fail(GTN_ERR_ARG, "model_generate_batch: needs Q8/Q4 weights of the TinyLlama, Zephyr or MiniCPM family");
+    if (!m->fused) return fail(GTN_ERR_ARG, "model_generate_batch: needs a model with 64-wide heads");
     for (long i = 0; i < (long)batch * n_prompt; ++i)
         if (prompts[i] < 0 || prompts[i] >= m->n_vocab) return fail(GTN_ERR_ARG, "model_generate_batch: token id %d", prompts[i]);
     const long ts = m->max_ctx + 1;
@@ -1080,7 +1085,7 @@ int gtn_model_generate_device(gtn_model* m, const int32_t* prompt, int n_prompt,
 
 int gtn_slot_start(gtn_model* m, const int32_t* prompt, int n_prompt, int* slot, int32_t* first_id) {
     if (!m || !m->loaded || !prompt || n_prompt <= 0 || !slot) return fail(GTN_ERR_ARG, "slot_start: arguments");
-    if (!m->fused) return fail(GTN_ERR_ARG, "slot_start: needs Q8/Q4 weights of the TinyLlama, Zephyr or MiniCPM family");
+    if (!m->fused) return fail(GTN_ERR_ARG, "slot_start: needs a model with 64-wide heads");
     if (n_prompt > m->max_ctx) return fail(GTN_ERR_ARG, "slot_start: %d prompt tokens exceed max_ctx %d", n_prompt, m->max_ctx);
     for (int i = 0; i < n_prompt; ++i)
         if (prompt[i] < 0 || prompt[i] >= m->n_vocab) return fail(GTN_ERR_ARG, "slot_start: token id %d", prompt[i]);
@@ -1112,7 +1117,7 @@ int gtn_slot_start(gtn_model* m, const int32_t* prompt, int n_prompt, int* slot,
 
 int gtn_slots_step(gtn_model* m, int32_t* ids) {
     if (!m || !m->loaded || !ids) return fail(GTN_ERR_ARG, "slots_step: arguments");
-    if (!m->fused) return fail(GTN_ERR_ARG, "slots_step: needs Q8/Q4 weights of the TinyLlama, Zephyr or MiniCPM family");
+    if (!m->fused) return fail(GTN_ERR_ARG, "slots_step: needs a model with 64-wide heads");
     int nact = 0;
     for (int b = 0; b < m->max_batch; ++b) {
         const int p = m->slot_pos[b];

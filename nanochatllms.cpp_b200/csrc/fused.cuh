@@ -376,27 +376,8 @@ __global__ void __launch_bounds__(NW * 32) k_fgemv(const FArgs a) {
     }
 }
 
-// Computes the activation rows of one GEMV once (residual update + norm, or the SwiGLU chain) and
-// writes them to `act` (row stride act_s bytes); grid (1, B), block 512, dynamic smem K floats
-// for RESNORM. It lets the following GEMV launch at once, so its weight prefetch overlaps this.
-template <int PRO>
-static __global__ void __launch_bounds__(512) k_prep(const FArgs a, uint8_t* act, long act_s) {
-    extern __shared__ float sval[];
-    if (PRO == PRO_RESNORM) {  // the norm weights do not depend on the previous kernel: warm L2 now
-        const int lines = (a.K * 2 + 127) / 128;
-        for (int i = threadIdx.x; i < lines; i += blockDim.x) {
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.nw) + 128L * i));
-            if (a.nb) asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.nb) + 128L * i));
-        }
-    }
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;");
-    const int m = blockIdx.y;
-    fgemv_prologue<PRO, 1>(a, act + (long)m * act_s, sval, m, 1);
-}
-
 // ---- residual update + norm on a cluster of PCL CTAs ------------------------------------------
-// The same computation as k_prep<PRO_RESNORM>, spread over a thread-block cluster so that the
+// The residual update and norm of fgemv_prologue<PRO_RESNORM>, spread over a thread-block cluster so that the
 // per-block requantizations (three per 32 elements) run on PCL SMs instead of one. CTA c updates
 // the 32-blocks [c*E, (c+1)*E) of the residual row (E = ceil(blocks / PCL)) and stores the new
 // values into the shared memory of every CTA of the cluster (distributed shared memory); after one
@@ -590,6 +571,7 @@ struct AArgs {
     const int* active;                       // [B] 0: idle slot (no cache write), or null
     const float* y; long ys;                 // stacked q|k|v fp32 rows
     const uint16_t *bq, *bk, *bv;            // Zephyr biases (or null)
+    const uint16_t *qnw, *knw;               // OpenELM QK-norm gains [d] (or null)
     const float2* cs; int half;              // RoPE table [pos][half] (cos, sin), half = rd/2
     uint8_t* kc; uint8_t* vc; long kvs;      // cache of this layer: row stride kvs bytes
     long khs;                                // bytes between kv heads
@@ -600,8 +582,8 @@ struct AArgs {
 
 // grid (q_heads, B); block ATT_THREADS. Decode attention of sequence b at position p = pos[b]
 // (keys 0..p), preceded by the q/k/v epilogue of the stacked projection, one Linear output head
-// each: requant (Linear) [-> + bias -> requant (bias_add_inplace)] [-> RoPE -> requant]. The
-// epilogue runs one warp per (tensor, 32-block). The q-head 0 of each kv group writes the new K/V
+// each: requant (Linear) [-> + bias -> requant (bias_add_inplace)] [-> QK RMSNorm -> requant]
+// [-> RoPE -> requant]. The epilogue runs one warp per (tensor, 32-block). The q-head 0 of each kv group writes the new K/V
 // cache rows; key p is taken from this CTA's own epilogue values. Then att_core / att_out.
 static __global__ void __launch_bounds__(ATT_THREADS) k_fattn(const AArgs a) {
     extern __shared__ __align__(16) uint8_t sm[];
@@ -645,6 +627,27 @@ static __global__ void __launch_bounds__(ATT_THREADS) k_fattn(const AArgs a) {
         tmp[t][i] = v;
     }
     __syncthreads();
+    if (a.qnw) {
+        // OpenELM QK-norm (openelm.cpp:44-50 -> rms_norm 3-D, ops.cpp:830-846 and :862-885): per
+        // head, the sequential fp32 sum of squares, sqrt of its mean, x / (rms + 1e-6) * w, requant
+        if (tid < 2) {
+            float ss = 0.0f;
+            for (int i = 0; i < d; ++i) {
+                const float x = tmp[tid][i];
+                const float x2 = x * x;
+                ss = ss + x2;
+            }
+            s_stat[tid] = sqrtf(ss / (float)d);
+        }
+        __syncthreads();
+        for (int w = warp; w < 2 * nbh; w += ATT_THREADS / 32) {
+            const int t = w / nbh, k = w - t * nbh, i = k * GTN_QBLK + lane;
+            const float x = tmp[t][i] / (s_stat[t] + 1e-6f);
+            const float y = x * h2f((t == 0 ? a.qnw : a.knw)[i]);
+            tmp[t][i] = requant(y, lane, GTN_QBLK, a.adt, nullptr, 0);
+        }
+        __syncthreads();
+    }
     // (2) RoPE (q, k) and the final requant into the head rows
     for (int w = warp; w < 3 * nbh; w += ATT_THREADS / 32) {
         const int t = w / nbh, k = w - t * nbh, i = k * GTN_QBLK + lane;

@@ -125,6 +125,11 @@ bool gemv_q_fits(int M, int wdt, int K);
 cudaError_t gemv_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
                    long ldy, cudaStream_t st, bool dry);
 
+// Exact fp16 x fp16 matmul (k_mm_f16, the reference's 8-lane order) for M activation rows; W 16-byte
+// aligned with the `padded` precondition of matmul_f32. `dry` only configures shared memory.
+cudaError_t gemm_f16(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y, long ldy,
+                     cudaStream_t st, bool dry);
+
 // Exact GEMM for M >= 2 activation rows of Q8 against Q8 or Q4 weights (16-byte aligned weight
 // rows, same `padded` precondition): the tensor-core kernel k_gemm_tc from TC_MIN_M rows on when
 // `tc` scratch is given, else k_gemm3 on the CUDA cores; `dry` only configures shared memory and
@@ -135,6 +140,21 @@ cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, 
                    long ldy, cudaStream_t st, bool dry, const TcScratch& tc = TcScratch());
 // Whether matmul_f32 / gemm_q take the tensor-core path for this shape given scratch `tc`.
 bool tc_fits(const uint8_t* W, long ws, int M, int wdt, int K, const TcScratch& tc);
+
+// Checked arguments of matmul_2d (ops.cpp:617-636) in byte terms: rows [start_pos, n_ctx) of x
+// (M rows from X, stride xs bytes), w [N, K] (stride ws), out (data, row stride os; 0 for a 1-D out).
+struct MatmulArgs {
+    bool quant, one_d;
+    int M, N, K, xdt, wdt, odt;
+    const uint8_t* X;
+    const uint8_t* W;
+    uint8_t* out;
+    long xs, ws, os;
+};
+// The argument checks of gtn_matmul_2d (shapes, dtypes, start_pos, quantized row overlap); returns
+// GTN_OK or GTN_ERR_ARG with the message prefixed by `who`.
+int matmul_args(const gtn_tensor* x, const gtn_tensor* w, const gtn_tensor* out, int start_pos, const char* who,
+                MatmulArgs* a);
 
 // Host table of (cos, sin) for positions [0, npos) and j < rd/2, as rotary_emb_impl computes them
 // (ops.cpp:791-812): theta = m * powf(10000, -((2j)/rd)), then cosf / sinf.

@@ -9,10 +9,15 @@
 #   -include cstring: minicpm/minicpm.cpp:24 uses std::memcpy without including <cstring>.
 # Nothing is copied out of the reference tree; outputs go to oracle/_ref/ only.
 set -euo pipefail
-REF="${1:-${GTEN_REFERENCE_DIR:-/root/reference}}"
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
+# The checkout: the first argument, else $GTEN_REFERENCE_DIR, else BASELINE.json's reference_path.
+REF="${1:-${GTEN_REFERENCE_DIR:-}}"
+if [ -z "$REF" ]; then
+    REF="$(python3 -c 'import json,sys; print(json.load(open(sys.argv[1])).get("reference_path") or "")' \
+           "$HERE/../BASELINE.json" 2>/dev/null || true)"
+fi
 OUT="$HERE/_ref"
-if [ ! -d "$REF/src/gten" ]; then
+if [ -z "$REF" ] || [ ! -d "$REF/src/gten" ]; then
     echo "reference checkout not found at $REF; keeping any prebuilt $OUT/libgtenref.so" >&2
     exit 0
 fi

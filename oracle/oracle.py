@@ -36,6 +36,21 @@ def row_bytes(dt: int, n: int) -> int:
     return 4 * n
 
 
+def reference_dir() -> str | None:
+    """The reference checkout to build or read from: $GTEN_REFERENCE_DIR, else the
+    ``reference_path`` that BASELINE.json (repository root) records; None when neither names an
+    existing checkout (e.g. on a GPU box, which only uses the prebuilt oracle/_ref library)."""
+    d = os.environ.get("GTEN_REFERENCE_DIR")
+    if not d:
+        try:
+            import json
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                d = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            d = None
+    return d if d and os.path.isdir(os.path.join(d, "src", "gten")) else None
+
+
 def _p(a):
     return None if a is None else a.ctypes.data_as(C.c_void_p)
 

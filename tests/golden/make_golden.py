@@ -17,9 +17,23 @@ where the reference checkout exists; the GPU box only reads the outputs).
   libstdc++ calls) from one std::mt19937(seed) in place of std::random_device; with each step's gap
   between the k-th and (k+1)-th largest logit (a tie there would make the pick library-specific).
 
-Usage: python tests/golden/make_golden.py [reference_dir]
+* model_tokens.json: the other BASELINE architectures at full size, each with seeded N(0, 0.02)
+  weights packed by the oracle's packer and a seeded uniform-random prompt: the compiled reference's
+  first 64 greedy ids (same harness as greedy_tokens.json) with each step's top-2 margin.
+  StableLM-2-Zephyr-1.6B Q4 (512-token prompt), MiniCPM-2B Q8 and Q4 (128-token prompt) and
+  OpenELM-1.1B (openelm_lg_cfg) fp16 (1024-token prompt; the reference runs OpenELM in fp16 only).
+  n_ctx = 2 x (prompt + 64) keeps the reference's attention-probability rows apart
+  (ops.cpp:1033-1034 offsets them by element counts used as byte counts).
+
+The reference checkout is named by the first non-option argument, GTEN_REFERENCE_DIR or
+BASELINE.json's reference_path (the packer goldens need it; the model goldens only need oracle/_ref/libgtenref.so, which
+oracle/build_ref.sh builds from the same checkout).
+
+Usage: python tests/golden/make_golden.py <reference_dir>
        python tests/golden/make_golden.py --sampled     (sampled_tokens.json only)
+       python tests/golden/make_golden.py --models [name ...]   (model_tokens.json; default all)
 """
+import hashlib
 import io
 import json
 import os
@@ -59,8 +73,18 @@ def pack_cases():
     return w
 
 
+def reference_dir():
+    from oracle.oracle import reference_dir as configured
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    d = args[0] if args else configured()
+    if not d or not os.path.isdir(os.path.join(d, "src")):
+        sys.exit("make_golden.py: name the reference checkout (argument, GTEN_REFERENCE_DIR or BASELINE.json "
+                 "reference_path)")
+    return d
+
+
 def main():
-    ref_dir = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_dir = reference_dir()
     import torch
 
     ns = reference_packer(ref_dir)
@@ -178,8 +202,66 @@ def sampled():
         json.dump(gold, f)
 
 
+# name -> (gtenfile kind, weight dtype, prompt tokens); BASELINE configs[2], [3], [4]
+MODEL_CASES = {
+    "zephyr_w4": (1, Q4, 512),
+    "minicpm_w3": (2, Q8, 128),
+    "minicpm_w4": (2, Q4, 128),
+    "openelm_lg_w1": (5, F16, 1024),
+}
+MODEL_VOCAB = {0: 32003, 1: 100352, 2: 122753, 5: 32000}
+
+
+def models(names):
+    """model_tokens.json: the compiled reference's first 64 greedy ids on full-size models."""
+    import time
+
+    from gten_b200 import gtenfile
+    orc, ref = Oracle(), Reference()
+
+    def pack(wt, dt):
+        return orc.pack_q8(wt.numpy()) if dt == Q8 else orc.pack_q4(wt.numpy())
+
+    path_json = os.path.join(HERE, "model_tokens.json")
+    gold = json.load(open(path_json)) if os.path.exists(path_json) else {}
+    for name in names:
+        kind, wdt, n_prompt = MODEL_CASES[name]
+        seed, n_gen = 1234, 64
+        n_ctx = 2 * (n_prompt + n_gen)
+        t0 = time.time()
+        img = gtenfile.synthetic_image(kind, wdt, seed, pack)
+        path = f"/tmp/golden_{name}.gten"
+        img.tofile(path)
+        del img
+        prompt = np.random.default_rng(42).integers(0, 32000, n_prompt).astype(np.int32)
+        rm = ReferenceModel(ref, kind, wdt, n_ctx, path, MODEL_VOCAB[kind])
+        # the greedy loop of ref_model_greedy (sampler.cpp:11-53), step by step so that the logits
+        # of the prefill and of two decode steps are recorded as SHA-256 digests of their fp32 bytes
+        toks, ids, margins, digests = [int(t) for t in prompt], [], [], {}
+        for i in range(n_gen):
+            lg = rm.logits(np.array(toks, np.int32), 0 if i == 0 else len(toks) - 1)
+            t = int(np.argmax(lg))  # the first maximum, as the reference's strict '>' scan
+            top = np.sort(lg)[::-1]
+            margins.append(float(top[0] - top[1]))
+            if i in (0, 1, n_gen - 1):
+                digests[str(i)] = hashlib.sha256(lg.astype(np.float32).tobytes()).hexdigest()
+            ids.append(t)
+            toks.append(t)
+        del rm
+        os.remove(path)
+        gold[name] = {"kind": kind, "wdtype": wdt, "seed": seed, "n_ctx": n_ctx, "prompt": prompt.tolist(),
+                      "tokens": ids, "margins": margins, "logits_sha256": digests}
+        print(name, ids[:16], "distinct", len(set(ids)), "min margin", min(margins), f"{time.time() - t0:.0f} s",
+              flush=True)
+        with open(path_json, "w") as f:
+            json.dump(gold, f)
+
+
 if __name__ == "__main__":
-    if "--sampled" in sys.argv:
+    if "--models" in sys.argv:
+        names = [a for a in sys.argv[sys.argv.index("--models") + 1:] if not a.startswith("--")]
+        models(names or list(MODEL_CASES))
+    elif "--sampled" in sys.argv:
         sampled()
     else:
         main()

@@ -27,6 +27,7 @@ CUSTOM = {
     "llama": [1000, 256, 2, 4, 2, 512, 0],
     "zephyr": [777, 192, 2, 3, 3, 320, 1],
     "minicpm": [900, 128, 3, 2, 2, 288, 2],
+    "openelm": [1100, 192, 2, 6, 2, 352, 3],
 }
 
 
@@ -70,12 +71,13 @@ def test_long_prefill_in_passes_matches_oracle(orc, gpu):
 
 
 @pytest.mark.parametrize("name", list(CUSTOM))
-@pytest.mark.parametrize("wdt", [Q8, Q4])
+@pytest.mark.parametrize("wdt", [Q8, Q4, F16])
 @pytest.mark.parametrize("batch", [3, 11, 20, 40])
 def test_batched_generation_matches_single_sequences(orc, gpu, name, wdt, batch):
     """The reference has no batching: each sequence of a batch must produce exactly the ids the
     oracle gives for it alone (batch 11 exercises a second 8-row tile of the fused GEMVs; 20 and
-    40 run the decode steps' projections on the tensor-core GEMM, 40 with a partial second row tile)."""
+    40 run the decode steps' Q8/Q4 projections on the tensor-core GEMM, 40 with a partial second
+    row tile; fp16 weights run the 8-lane CUDA-core kernel in tiles of 8 rows)."""
     from oracle.oracle import OracleModel
     dims = CUSTOM[name]
     img = gtenfile.synthetic_image(6, wdt, 77, cpu_pack(orc), dims=dims, std=0.05, gain_std=0.1)
@@ -133,7 +135,7 @@ def test_load_file_matches_load(orc, gpu, name, tmp_path):
 
 
 @pytest.mark.parametrize("name", list(CUSTOM))
-@pytest.mark.parametrize("wdt", [Q8, Q4])
+@pytest.mark.parametrize("wdt", [Q8, Q4, F16])
 def test_continuous_batching_matches_single_sequences(orc, gpu, name, wdt):
     """Eleven requests of mixed prompt lengths and lengths of generation through 4 slots: requests
     join the running batch as slots free up; each must get exactly the oracle's single-sequence
@@ -188,7 +190,7 @@ GOLDEN = os.path.join(HERE, "golden", "greedy_tokens.json")
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("wdt", [Q8, Q4])
+@pytest.mark.parametrize("wdt", [Q8, Q4, F16])
 def test_tinyllama_greedy_matches_reference(orc, gpu, wdt):
     """Full-size TinyLlama, seeded N(0, 0.02) weights, 64-token prompt, 64 greedy tokens: the ids
     must equal the reference CPU build's (tests/golden/greedy_tokens.json, made by
@@ -202,6 +204,57 @@ def test_tinyllama_greedy_matches_reference(orc, gpu, wdt):
     m.load(img)
     got = m.generate(prompt, len(case["tokens"]))
     assert got.tolist() == case["tokens"]
+    m.close()
+
+
+MODELS = os.path.join(HERE, "golden", "model_tokens.json")
+with open(MODELS) as _f:
+    MODEL_CASES = sorted(json.load(_f))
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name", MODEL_CASES)
+def test_full_size_model_matches_reference(orc, gpu, name):
+    """The other BASELINE architectures at full size (StableLM-2-Zephyr-1.6B Q4 with a 512-token
+    prompt, MiniCPM-2B Q8 / Q4 with 128 tokens, OpenELM-1.1B fp16 with 1024 tokens), seeded
+    N(0, 0.02) weights: the prefill logits must be the compiled reference's bit for bit (SHA-256 of
+    the fp32 vector) and the 64 greedy ids of the fused decode path its ids
+    (tests/golden/model_tokens.json, made by tests/golden/make_golden.py --models)."""
+    import hashlib
+    with open(MODELS) as f:
+        case = json.load(f)[name]
+    img = gtenfile.synthetic_image(case["kind"], case["wdtype"], case["seed"], gtenfile.cuda_packer())
+    prompt = np.array(case["prompt"], np.int32)
+    m = G.Model(case["kind"], case["wdtype"], case["n_ctx"])
+    m.load(img)
+    del img
+    lg = m.logits(prompt, 0)
+    assert hashlib.sha256(lg.tobytes()).hexdigest() == case["logits_sha256"]["0"]
+    got = m.generate(prompt, len(case["tokens"]))
+    assert got.tolist() == case["tokens"]
+    m.close()
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("wdt", [Q8, Q4, F16])
+def test_openelm_sm_matches_oracle(orc, gpu, wdt):
+    """OpenELM-270M (openelm_sm_cfg: per-layer query / KV heads and FFN widths, QK-norm) at full
+    size against the oracle's OpenELM wiring: prefill logits bit for bit, then greedy ids through
+    the fused decode step. The reference runs OpenELM in fp16 only (its RoPE buffer is fp16,
+    modules.cpp:247-249), so Q8 / Q4 follow the generic quantized-model semantics of the other
+    families (Q8 activations everywhere), as the oracle restates them."""
+    from oracle.oracle import OracleModel
+
+    def pack(w, dt):
+        return orc.pack_q8(w.numpy()) if dt == Q8 else orc.pack_q4(w.numpy())
+
+    img = gtenfile.synthetic_image(G.OPENELM_SM, wdt, 4321, pack, std=0.05, gain_std=0.1)
+    prompt = np.random.default_rng(3).integers(0, 32000, 12).astype(np.int32)
+    n_gen, max_ctx = 6, 64
+    m = G.Model(G.OPENELM_SM, wdt, max_ctx)
+    m.load(img)
+    assert np.array_equal(m.logits(prompt, 0), OracleModel(orc, G.OPENELM_SM, wdt, max_ctx, img).logits(prompt, 0))
+    assert np.array_equal(m.generate(prompt, n_gen), OracleModel(orc, G.OPENELM_SM, wdt, max_ctx, img).greedy(prompt, n_gen))
     m.close()
 
 

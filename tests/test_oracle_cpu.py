@@ -66,9 +66,10 @@ def test_fp16_conversions_exhaustive(orc, ref):
 
 def test_reference_python_packer_live(orc):
     """The reference converter's own q8_quantize / q4_quantize on fresh seeded tensors."""
-    ref_dir = "/root/reference"
-    if not os.path.isdir(os.path.join(ref_dir, "src")):
-        pytest.skip("reference checkout not present")
+    from oracle.oracle import reference_dir
+    ref_dir = reference_dir()
+    if ref_dir is None:
+        pytest.skip("no reference checkout (GTEN_REFERENCE_DIR or BASELINE.json reference_path)")
     import io
 
     import torch
