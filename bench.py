@@ -124,31 +124,55 @@ def barrier(world):
         dist.barrier()
 
 
-def cpu_reference_sample(image, wdt: int, prompt, n_decode: int = 16):
-    """Times the compiled reference on the host: prefill of the prompt, then n_decode greedy
-    steps; returns (extrapolated tok/s for the 256-token request, details)."""
-    import numpy as np
-    from oracle.oracle import Reference, ReferenceModel
-    path = f"/tmp/gten_bench_{os.getpid()}.gten"
-    image.tofile(path)
-    try:
-        ref = Reference()
-        rm = ReferenceModel(ref, 0, wdt, N_PROMPT + N_GEN, path, 32003)
-        toks = list(prompt)
+class RefRequestTimer:
+    """Times the compiled reference on the host for one batch-1 request (64-token prompt, 256 greedy
+    tokens) on the given .gten image. The prompt's prefill is timed as is; the decode steps are
+    timed at contexts spread over the request, because the reference's per-token cost grows with the
+    context (it re-reads and transposes the whole V prefix every call, ops.cpp:1091-1132). The cache
+    is filled once with a prefill of all 319 positions; a decode step at context n is then
+    Model::logits(tokens[:n], n - 1), which recomputes only row n - 1 over the cached rows below it
+    (the work of that step of the request; rows below n - 1 are not touched). A least-squares line
+    t(n) = a + b*n through the samples, summed over n = 65..319, gives the request's decode time."""
+
+    CTX = (65, 128, 192, 256, 319)
+
+    def __init__(self, image, wdt: int, prompt):
+        import numpy as np
+        from oracle.oracle import Reference, ReferenceModel
+        self.path = f"/tmp/gten_bench_{os.getpid()}.gten"
+        image.tofile(self.path)
+        # max_ctx 2 x 320 keeps the reference's probability rows apart (ops.cpp:1033-1034)
+        self.rm = ReferenceModel(Reference(), 0, wdt, 2 * (N_PROMPT + N_GEN), self.path, 32003)
+        self.toks = np.concatenate([prompt, np.random.default_rng(5).integers(0, 32000, N_GEN - 1)]).astype(np.int32)
+        self.rm.logits(self.toks, 0)  # fills the cache rows 0..318 (untimed)
+
+    def sample(self, reps: int = 2):
+        """Returns (tok/s of one request, details)."""
+        import numpy as np
         t0 = time.perf_counter()
-        lg = rm.logits(np.array(toks, np.int32), 0)
+        self.rm.logits(self.toks[:N_PROMPT], 0)
         t_prefill = time.perf_counter() - t0
-        toks.append(int(np.argmax(lg)))
-        t0 = time.perf_counter()
-        for _ in range(n_decode):
-            lg = rm.logits(np.array(toks, np.int32), len(toks) - 1)
-            toks.append(int(np.argmax(lg)))
-        t_dec = (time.perf_counter() - t0) / n_decode
-        del rm
-    finally:
-        os.remove(path)
-    tps = N_GEN / (t_prefill + (N_GEN - 1) * t_dec)
-    return tps, {"prefill_s": t_prefill, "decode_ms_per_token": t_dec * 1e3}
+        xs, ys = [], []
+        for _ in range(reps):
+            for n in self.CTX:
+                t0 = time.perf_counter()
+                self.rm.logits(self.toks[:n], n - 1)
+                ys.append(time.perf_counter() - t0)
+                xs.append(n)
+        b, a = np.polyfit(np.array(xs, float), np.array(ys, float), 1)
+        t_dec = float(sum(a + b * n for n in range(N_PROMPT + 1, N_PROMPT + N_GEN)))
+        return N_GEN / (t_prefill + t_dec), {"prefill_s": t_prefill, "decode_ms_at_65": (a + b * 65) * 1e3,
+                                              "decode_ms_at_319": (a + b * 319) * 1e3, "decode_s": t_dec}
+
+    def close(self):
+        del self.rm
+        os.remove(self.path)
+
+
+def ref_sample_text(det) -> str:
+    return (f"compiled reference on the same .gten bytes: the 64-token prefill ({det['prefill_s']:.2f} s) and decode "
+            f"steps timed at contexts 65-319 ({det['decode_ms_at_65']:.1f} -> {det['decode_ms_at_319']:.1f} ms/token, "
+            f"a linear fit summed over the 255 steps)")
 
 
 def gemv_roofline(G, torch, wdt: int, device, hbm_peak: float, only: str | None = None):
@@ -261,45 +285,85 @@ def gemm_sweep(G, torch, wdt: int, device, M: int, only: str | None = None):
     return out
 
 
-def run_ours(args, rank, world, local):
-    import numpy as np
-    import torch
+def weight_bytes(kind: int, wdt: int) -> int:
+    """Algorithmic weight bytes one decode token streams: every projection matrix and the lm_head
+    (the embedding contributes one row), in the reference's block format."""
+    from gten_b200 import gtenfile, row_bytes
+    a = gtenfile.arch(kind)
+    tot = 0
+    for qh, kv, ff in a.layers:
+        qd, kvd = qh * 64, kv * 64
+        tot += (qd + 2 * kvd) * row_bytes(wdt, a.d) + a.d * row_bytes(wdt, qd)
+        tot += 2 * ff * row_bytes(wdt, a.d) + a.d * row_bytes(wdt, ff)
+    return tot + a.n_vocab * row_bytes(wdt, a.d)
 
-    import gten_b200 as G
+
+def kv_bytes_per_ctx(kind: int, wdt: int) -> int:
+    """K and V bytes one decode step reads per token of context (all layers, activation dtype)."""
+    from gten_b200 import gtenfile, row_bytes
+    adt = 1 if wdt == 1 else 3
+    return sum(2 * kv * row_bytes(adt, 64) for _, kv, _ in gtenfile.arch(kind).layers)
+
+
+def time_request(G, torch, wdt, prompt, device, steps, warmup, hbm, image=None, clocks_index=None):
+    """One batch-1 TinyLlama request (64-token prompt, 256 greedy tokens) on the device: CUDA events
+    on the model's stream over `steps` requests with the prompt and ids in HBM; also the prompt's
+    prefill + first id alone, so that the decode steps' time per token is the difference / 255.
+    Returns (model, image, dict)."""
     from gten_b200 import gtenfile
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    hbm, peak_kind = peaks()
-    wdt = args.wdtype
-    image = gtenfile.synthetic_image_device(G.TINYLLAMA, wdt, SEED)
-    prompt = np.random.default_rng(42).integers(0, 32000, N_PROMPT).astype(np.int32)
+    if image is None:  # the bytes the reference arm loads: CPU-seeded values, packed bit-exactly on the GPU
+        image = gtenfile.synthetic_image(G.TINYLLAMA, wdt, SEED, gtenfile.cuda_packer(str(device)))
     m = G.Model(G.TINYLLAMA, wdt, N_PROMPT + N_GEN)
     m.load(image)
     st = torch.cuda.ExternalStream(m.stream_ptr, device=device)
     p_dev = torch.from_numpy(prompt).to(device)
     o_dev = torch.empty(N_GEN, dtype=torch.int32, device=device)
-    torch.cuda.synchronize()
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         m.generate_device(p_dev, N_GEN, o_dev)
+        m.generate_device(p_dev, 1, o_dev)
     m.check()
     torch.cuda.synchronize()
+    res = {}
+    clocks = Clocks(clocks_index) if clocks_index is not None else None
+    for key, n in (("request", N_GEN), ("prefill", 1)):
+        launches0 = G.kernel_launches()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            m.generate_device(p_dev, n, o_dev)
+        e1.record(st)
+        torch.cuda.synchronize()
+        res[key] = e0.elapsed_time(e1) * 1e-3 / steps
+        if key == "request":
+            res["launches"] = G.kernel_launches() - launches0
+    res["clocks"] = clocks.stop() if clocks else None
+    m.check()
+    dec = (res["request"] - res["prefill"]) / (N_GEN - 1)
+    # bytes per decode token: the weights plus the K/V rows of the mean context of the decode steps
+    mean_ctx = N_PROMPT + N_GEN / 2
+    byt = weight_bytes(G.TINYLLAMA, wdt) + kv_bytes_per_ctx(G.TINYLLAMA, wdt) * mean_ctx
+    res["decode_s_per_token"] = dec
+    res["step_roofline"] = {"bound": "hbm", "bytes_per_token": int(byt), "achieved": round(byt / dec / 1e9, 1),
+                            "peak": hbm, "unit": "GB/s", "frac": round(byt / dec / 1e9 / hbm, 4)}
+    return m, image, res
 
-    # device-timed region
+
+def run_ours(args, rank, world, local):
+    import numpy as np
+    import torch
+
+    import gten_b200 as G
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    hbm, peak_kind = peaks()
+    wdt = args.wdtype
+    prompt = np.random.default_rng(42).integers(0, 32000, N_PROMPT).astype(np.int32)
     barrier(world)
     torch.cuda.synchronize()
-    clocks = Clocks(local)
-    launches0 = G.kernel_launches()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(args.steps):
-        m.generate_device(p_dev, N_GEN, o_dev)
-    e1.record(st)
-    torch.cuda.synchronize()
-    launches = G.kernel_launches() - launches0
-    clk = clocks.stop()
+    m, image, req = time_request(G, torch, wdt, prompt, device, args.steps, args.warmup, hbm, clocks_index=local)
+    launches, clk = req["launches"], req["clocks"]
     barrier(world)
-    m.check()
-    t = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+    t = max_over_ranks(req["request"] * args.steps, world)
     value = world * args.steps * N_GEN / t
 
     # end to end through the public API with host buffers (pinned prompt, ids read back)
@@ -313,6 +377,18 @@ def run_ours(args, rank, world, local):
         pin_o.numpy()[:] = out
     t_e2e = max_over_ranks(time.perf_counter() - t0, world)
     e2e = world * args.steps * N_GEN / t_e2e
+    m.close()
+
+    # the north-star configuration: the same request with Q4 weights (BASELINE target: >= 0.70 of
+    # the HBM roofline per decode token)
+    q4 = None
+    if wdt != 4:
+        mq, _, rq = time_request(G, torch, 4, prompt, device, args.steps, args.warmup, hbm)
+        mq.close()
+        q4 = {"value": round(N_GEN / rq["request"], 2), "unit": "tok/s",
+              "ms_per_step": round(rq["request"] * 1e3, 3),
+              "decode_ms_per_token": round(rq["decode_s_per_token"] * 1e3, 4),
+              "step_roofline": rq["step_roofline"], "target_frac": 0.70}
 
     dom, sweep = gemv_roofline(G, torch, wdt, device, hbm)
     result = None
@@ -320,11 +396,11 @@ def run_ours(args, rank, world, local):
         cpu = None
         if world == 1:
             try:
-                tps, det = cpu_reference_sample(image, wdt, prompt)
+                rt = RefRequestTimer(image, wdt, prompt)
+                tps, det = rt.sample()
+                rt.close()
                 cpu = {"value": round(tps, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "reference",
-                       "sample": f"compiled reference, 64-token prefill + 16 greedy steps timed, extrapolated to "
-                                 f"the 256-token request ({det['prefill_s']:.2f} s prefill, "
-                                 f"{det['decode_ms_per_token']:.1f} ms/token)"}
+                       "sample": ref_sample_text(det)}
             except Exception as ex:  # reference library missing on this machine
                 cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "reference",
                        "sample": f"unavailable: {ex}"}
@@ -337,11 +413,13 @@ def run_ours(args, rank, world, local):
             "warmup": args.warmup,
             "ms_per_step": round(t / args.steps * 1e3, 3),
             "ms_per_token": round(t / args.steps / N_GEN * 1e3, 4),
+            "decode_ms_per_token": round(req["decode_s_per_token"] * 1e3, 4),
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": "int8-blocks/fp32-accum (Q8 weights, Q8 activations)" if wdt == 3 else WDT_NAMES[wdt],
-            "data": "synthetic: seeded N(0,0.02) weights (CUDA generator), uniform-random prompt ids",
+            "data": "synthetic: seeded N(0,0.02) weights (CPU generator, the reference arm's bytes), uniform-random "
+                    "prompt ids",
             "config": {"workload": f"TinyLlama-1.1B {WDT_NAMES[wdt].upper()} batch-1, 64-token prompt + 256 greedy "
                                    f"decode tokens per request (BASELINE configs[0])",
                        "model": "tinyllama-1.1b", "global_batch": world, "seq_len": N_PROMPT + N_GEN,
@@ -349,6 +427,8 @@ def run_ours(args, rank, world, local):
                        "l2": f"weights {WEIGHT_GB[wdt]} GB > 126 MB L2; no flush needed"},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": N_PROMPT * 4,
                     "d2h_bytes_per_step": N_GEN * 4},
+            "step_roofline": req["step_roofline"],
+            "q4_bs1": q4,
             "roofline": {"bound": "hbm", "kernel": f"k_gemv3 (exact {WDT_NAMES[wdt].upper()} GEMV, gate_up 11264x2048)",
                          "achieved": dom["GB_s"], "peak": hbm, "unit": "GB/s",
                          "frac": round(dom["GB_s"] / hbm, 3), "peak_kind": peak_kind,
@@ -359,13 +439,14 @@ def run_ours(args, rank, world, local):
         }
         if clk:
             result["clocks"] = clk
-    m.close()
     return result
 
 
 BATCH_MODELS = {"tinyllama": ("TinyLlama-1.1B", 0), "zephyr": ("StableLM-2-Zephyr-1.6B", 1),
-                "minicpm": ("MiniCPM-2B", 2)}
-BATCH_PROMPT = {"tinyllama": N_PROMPT, "zephyr": 512, "minicpm": 128}  # BASELINE configs[0], [2], [3]
+                "minicpm": ("MiniCPM-2B", 2), "openelm": ("OpenELM-1.1B", 5)}
+# BASELINE configs[0], [2], [3], [4]: prompt tokens and greedy tokens per sequence
+BATCH_PROMPT = {"tinyllama": N_PROMPT, "zephyr": 512, "minicpm": 128, "openelm": 1024}
+BATCH_GEN = {"tinyllama": N_GEN, "zephyr": N_GEN, "minicpm": N_GEN, "openelm": 512}
 
 
 def run_batch(args, rank, world, local):
@@ -382,16 +463,16 @@ def run_batch(args, rank, world, local):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     name, kind = BATCH_MODELS[args.model]
-    n_prompt = BATCH_PROMPT[args.model]
+    n_prompt, n_gen = BATCH_PROMPT[args.model], BATCH_GEN[args.model]
     start, count = shard_range(args.batch, world, rank)
-    m = G.Model(kind, args.wdtype, n_prompt + N_GEN, max(1, count))
+    m = G.Model(kind, args.wdtype, n_prompt + n_gen, max(1, count))
     m.load(gtenfile.synthetic_image_device(kind, args.wdtype, SEED))
     prompts = np.random.default_rng(42).integers(0, 32000, (args.batch, n_prompt)).astype(np.int32)
     mine = prompts[start:start + count]
     st = torch.cuda.ExternalStream(m.stream_ptr, device=device)
     for _ in range(args.warmup):
         if count:
-            m.generate_batch(mine, N_GEN)
+            m.generate_batch(mine, n_gen)
     torch.cuda.synchronize()
     barrier(world)
     clocks = Clocks(local)
@@ -400,7 +481,7 @@ def run_batch(args, rank, world, local):
     e0.record(st)
     for _ in range(args.steps):
         if count:
-            m.generate_batch(mine, N_GEN)
+            m.generate_batch(mine, n_gen)
     e1.record(st)
     torch.cuda.synchronize()
     launches = G.kernel_launches() - launches0
@@ -409,12 +490,12 @@ def run_batch(args, rank, world, local):
     barrier(world)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        out = generate_sharded(m, prompts, N_GEN) if world > 1 else m.generate_batch(prompts, N_GEN)
+        out = generate_sharded(m, prompts, n_gen) if world > 1 else m.generate_batch(prompts, n_gen)
     t_e2e = max_over_ranks(time.perf_counter() - t0, world)
     m.close()
     if rank != 0:
         return None
-    tot = args.batch * N_GEN * args.steps
+    tot = args.batch * n_gen * args.steps
     res = {
         "metric": "decode tok/s", "value": round(tot / t, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 3),
@@ -422,11 +503,11 @@ def run_batch(args, rank, world, local):
         "dtype": "int8-blocks/fp32-accum (Q8 weights, Q8 activations)" if args.wdtype == 3 else WDT_NAMES[args.wdtype],
         "data": "synthetic: seeded N(0,0.02) weights (CUDA generator), uniform-random prompt ids",
         "config": {"workload": f"{name} {WDT_NAMES[args.wdtype].upper()} batch {args.batch} sharded by sequence over "
-                               f"{world} GPU(s), {n_prompt}-token prompts + {N_GEN} greedy tokens",
-                   "model": args.model, "global_batch": args.batch, "seq_len": n_prompt + N_GEN,
+                               f"{world} GPU(s), {n_prompt}-token prompts + {n_gen} greedy tokens",
+                   "model": args.model, "global_batch": args.batch, "seq_len": n_prompt + n_gen,
                    "parallelism": f"sequence shards x{world} (no collective on the data path)"},
         "e2e": {"value": round(tot / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": args.batch * n_prompt * 4,
-                "d2h_bytes_per_step": args.batch * N_GEN * 4},
+                "d2h_bytes_per_step": args.batch * n_gen * 4},
         "gpu_launches": int(launches),
         "first_ids": [int(x) for x in out[0, :4]],
     }
@@ -539,11 +620,13 @@ def run_reference(args, rank, world):
     # CPU-seeded weights packed by the oracle packer (bit-exact with the reference converter)
     image = gtenfile.synthetic_image(0, args.wdtype, SEED, pack)
     prompt = np.random.default_rng(42).integers(0, 32000, N_PROMPT).astype(np.int32)
+    rt = RefRequestTimer(image, args.wdtype, prompt)
     vals = []
     for i in range(args.warmup + args.steps):
-        tps, det = cpu_reference_sample(image, args.wdtype, prompt, n_decode=8)
+        tps, det = rt.sample(reps=1)
         if i >= args.warmup:
             vals.append(tps)
+    rt.close()
     v = statistics.mean(vals)
     wdt = args.wdtype
     return {
@@ -554,7 +637,7 @@ def run_reference(args, rank, world):
                                f"decode tokens per request (BASELINE configs[0])", "model": "tinyllama-1.1b",
                    "global_batch": 1, "seq_len": N_PROMPT + N_GEN, "parallelism": "cpu (OpenMP, all cores)"},
         "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "reference",
-                         "sample": "per step: 64-token prefill + 8 greedy steps timed, extrapolated to 256 tokens"},
+                         "sample": "per step: " + ref_sample_text(det)},
         "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 

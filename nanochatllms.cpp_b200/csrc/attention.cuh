@@ -318,7 +318,7 @@ __device__ __forceinline__ void att_softmax(float* p, int n, int last, float mx,
 #pragma unroll
     for (int w = 0; w < ATT_THREADS / 32; ++w) mk = max(mk, redk[w]);
     const float m = __uint_as_float((mk & 0x80000000u) ? (mk ^ 0x80000000u) : ~mk);
-    for (int j = tid; j < n; j += ATT_THREADS) p[j] = j <= last ? exp_cr(p[j] - m) : 0.0f;
+    for (int j = tid; j < n; j += ATT_THREADS) p[j] = j <= last ? expf_ref(p[j] - m) : 0.0f;
     __syncthreads();
     if (tid == 0) {
         float sum = 0.0f;

@@ -33,10 +33,50 @@ __device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__flo
 
 __device__ __forceinline__ uint16_t ld_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
-// exp rounded correctly to float: computed in double precision by CUDA's exp() and rounded once.
-// glibc's expf (what the reference calls) agrees with the correctly rounded value on all but
-// about 7.6e-5 of float inputs, where it is one ulp away.
-__device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
+// expf as the reference's math library evaluates it. The reference calls glibc's expf (silu,
+// ops.cpp:733-772; softmax, ops.cpp:1064-1070), whose method is Szabolcs Nagy's table-driven
+// exponential from Arm's optimized-routines (2017): with N = 32,
+//   z = x * N / ln 2 (double),  k = round(z) (by adding 1.5 * 2^52),  r = z - k,
+//   exp(x) = 2^(k/N) * (1 + c2 r + c1 r^2 + c0 r^3),  2^(k/N) = 2^floor(k/N) * tab[k mod N],
+// evaluated in double and rounded once to float. tab[i] is the double nearest 2^(i/32), stored
+// minus (i << 47) so that adding k << 47 to its bits also applies 2^floor(k/N); c0..c2 are the
+// method's published minimax coefficients scaled by N^-3, N^-2, N^-1. glibc's x86-64 build for CPUs
+// with FMA (the variant its loader selects on them) forms r = x * (N / ln 2) - k with one fused
+// multiply-add, so r does so here. Against the host's expf this is bit-identical on all 2^32 float
+// inputs (checked exhaustively); a correctly rounded exp differs from glibc's on 170,648 of them.
+__constant__ static unsigned long long k_expf_tab[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull,
+};
+__device__ __forceinline__ float expf_ref(float x) {
+    const unsigned int ax = __float_as_uint(x) & 0x7fffffffu;
+    if (ax >= 0x42b00000u) {                         // |x| >= 88, inf or nan
+        if (__float_as_uint(x) == 0xff800000u) return 0.0f;  // exp(-inf)
+        if (ax >= 0x7f800000u) return x + x;         // +inf, nan
+        if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);  // overflow
+        if (x < -0x1.9fe368p6f) return 0.0f;         // underflow below 2^-150
+    }
+    const double inv_ln2n = 0x1.71547652b82fep+5, shift = 0x1.8p+52;
+    const double xd = (double)x;
+    const double z = __dmul_rn(inv_ln2n, xd);
+    double kd = __dadd_rn(z, shift);
+    const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
+    kd = __dsub_rn(kd, shift);
+    const double r = __fma_rn(inv_ln2n, xd, -kd);
+    const double s = __longlong_as_double((long long)(k_expf_tab[ki & 31u] + (ki << 47)));
+    const double c0 = 0x1.c6af84b912394p-20, c1 = 0x1.ebfce50fac4f3p-13, c2 = 0x1.62e42ff0c52d6p-6;
+    const double p = __dadd_rn(__dmul_rn(c0, r), c1);
+    const double r2 = __dmul_rn(r, r);
+    double y = __dadd_rn(__dmul_rn(c2, r), 1.0);
+    y = __dadd_rn(__dmul_rn(p, r2), y);
+    return __double2float_rn(__dmul_rn(y, s));
+}
 
 // Quantize one 32-element block held one element per lane (quants.cpp:16-30): absmax over the
 // valid lanes, delta = absmax/127 (fp32, stored as fp16), scale = 1/delta of the UNROUNDED delta,

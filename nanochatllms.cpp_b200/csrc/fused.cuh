@@ -113,7 +113,7 @@ __device__ __forceinline__ void fgemv_prologue(const FArgs& a, uint8_t* xq, floa
             for (int blk = warp; blk < nbk; blk += nwarps) {
                 const int i = blk * GTN_QBLK + lane, nv = min(GTN_QBLK, K - blk * GTN_QBLK);
                 const float gv = requant(i < K ? g[i] : 0.0f, lane, nv, a.adt, nullptr, blk);
-                const float den = 1.0f + exp_cr(-gv);
+                const float den = 1.0f + expf_ref(-gv);
                 const float sv = requant(gv / den, lane, nv, a.adt, nullptr, blk);
                 const float uv = requant(i < K ? u[i] : 0.0f, lane, nv, a.adt, nullptr, blk);
                 requant(sv * uv, lane, nv, a.adt, xq + (long)m * xrb, blk);
@@ -558,7 +558,7 @@ static __global__ void __launch_bounds__(1024) k_prep_swiglu(const FArgs a, uint
     const float* u = g + K;
     const int i = blk * GTN_QBLK + lane, nv = min(GTN_QBLK, K - blk * GTN_QBLK);
     const float gv = requant(i < K ? g[i] : 0.0f, lane, nv, a.adt, nullptr, blk);
-    const float den = 1.0f + exp_cr(-gv);
+    const float den = 1.0f + expf_ref(-gv);
     const float sv = requant(gv / den, lane, nv, a.adt, nullptr, blk);
     const float uv = requant(i < K ? u[i] : 0.0f, lane, nv, a.adt, nullptr, blk);
     requant(sv * uv, lane, nv, a.adt, act + (long)m * act_s, blk);

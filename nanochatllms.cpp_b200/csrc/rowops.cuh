@@ -44,7 +44,7 @@ static __global__ void k_rowop(const uint8_t* a, long as, const uint8_t* b, long
     const float x = valid ? load_elem(a + (long)row * as, dt, i) : 0.0f;
     float y;
     if (OP == ROP_SILU) {
-        const float den = 1.0f + exp_cr(-x);
+        const float den = 1.0f + expf_ref(-x);
         y = x / den;
     } else if (OP == ROP_MUL) {
         y = x * (valid ? load_elem(b + (long)row * bs, dt, i) : 0.0f);

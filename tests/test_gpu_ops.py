@@ -195,6 +195,25 @@ def test_elementwise(orc, gpu, dt, D):
     assert np.array_equal(from_dev(buf), orc.bias_add_inplace(x, dt, M, D, bias))
 
 
+def test_silu_uses_the_reference_expf(orc, gpu):
+    """silu on fp32 rows at inputs where the reference's expf (glibc's, ops.cpp:733-772) and a
+    correctly rounded exp differ and the difference reaches silu's result
+    (tests/golden/expf_cases.npy, made by make_expf_cases.py from the host's libm): the device must
+    give the host library's bits. The oracle calls the host's expf."""
+    import os
+    x = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "expf_cases.npy"))
+    D = 128
+    M = (x.size + D - 1) // D
+    xs = np.zeros(M * D, np.float32)
+    xs[: x.size] = x
+    out = dev_out(xs.nbytes, gpu)
+    G.silu(G.GT(to_dev(xs, gpu), F32, (M, D)), G.GT(out, F32, (M, D)))
+    want = orc.silu(xs.view(np.uint8), F32, M, D, 0)
+    got = from_dev(out)
+    bad = np.flatnonzero(got.view(np.uint32) != want.view(np.uint32))
+    assert bad.size == 0, f"{bad.size} of {xs.size} differ, e.g. x = {xs[bad[:4]]}"
+
+
 @pytest.mark.parametrize("wdt", [Q8, Q4, F16])
 def test_token_embed(orc, gpu, wdt):
     rng = np.random.default_rng(21 + wdt)
