@@ -735,10 +735,32 @@ static cudaError_t fg_mt(const FArgs& a, cudaStream_t st, bool dry) {
     return big ? fg_launch<WDT, 4, 8, PRO>(a, st, dry) : fg_launch<WDT, 1, 8, PRO>(a, st, dry);
 }
 
-// A GEMV whose activation needs a prologue runs it once into m->act (residual + norm: k_prep_cl,
-// one cluster per sequence; SwiGLU: k_prep_swiglu); the GEMV then reads that row.
+// k_fgemv3: one sequence's GEMV with its prologue in every CTA (Q8 / Q4 weights).
+template <int WDT, int PRO>
+static cudaError_t fg3_launch(const gtn_model* m, const FArgs& a, int R, int RP, bool dry) {
+    const size_t smem = gv3_smem<WDT>(R, a.K) + fg3_extra_smem(PRO, a.K);
+    const cudaError_t e = ensure_smem(k_fgemv3<WDT, PRO>, smem);
+    if (e != cudaSuccess || dry) return e;
+    ++g_step_kernels;
+    const int ngroups = (a.N + R - 1) / R;
+    const int occ = (int)((227 * 1024) / (smem + 8 * 1024)) >= 2 ? 2 : 1;  // + static shared memory
+    const int gx = std::min(ngroups, device_sm_count() * occ);
+    return launch_pdl(k_fgemv3<WDT, PRO>, dim3(gx), dim3(GV3_THREADS), smem, m->st, a, R, RP);
+}
+
+// A GEMV whose activation needs a prologue: for one sequence (Q8 / Q4 weights) k_fgemv3 computes it
+// in every CTA; otherwise it runs once into m->act (residual + norm: k_prep_cl, one cluster per
+// sequence; SwiGLU: k_prep_swiglu) and the GEMV reads that row.
 static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) {
     FArgs g = a;
+    int R = 0, RP = 0;
+    // (the SwiGLU prologue stays a kernel of its own: every GEMV CTA would redo the whole row's
+    // exp and three requantizations per element on 8 warps, longer than one wide pass)
+    if (pro == PRO_RESNORM && a.B == 1 && !a.active && (m->wdt == GTN_Q8 || m->wdt == GTN_Q4) &&
+        a.K <= FG3_PER * GV3_THREADS && gemv1_plan(m->wdt, a.W, a.ws, a.N, a.K, fg3_extra_smem(pro, a.K), &R, &RP)) {
+        if (m->wdt == GTN_Q8) return fg3_launch<GTN_Q8, PRO_RESNORM>(m, a, R, RP, dry);
+        return fg3_launch<GTN_Q4, PRO_RESNORM>(m, a, R, RP, dry);
+    }
     if (pro != PRO_COPY) {
         cudaError_t e;
         if (pro == PRO_RESNORM) {

@@ -86,7 +86,7 @@ __host__ __device__ inline size_t fgemv_smem(int nw, int mt, int K, int adt, int
 }
 
 // Builds the MT activation rows of this launch in shared memory (xq), per the prologue kind.
-template <int PRO, int MT>
+template <int PRO, int MT, int PER = SEQSUM_PER_MAX>
 __device__ __forceinline__ void fgemv_prologue(const FArgs& a, uint8_t* xq, float* sval, int m0, int mt) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
     const int K = a.K, nbk = (K + GTN_QBLK - 1) / GTN_QBLK;
@@ -199,11 +199,29 @@ __device__ __forceinline__ void fgemv_prologue(const FArgs& a, uint8_t* xq, floa
         __shared__ SeqSumSmem ss;
         unsigned int mb = lane < nwarps ? wmax[lane] : 0u;
         mb = __reduce_max_sync(0xffffffffu, mb);
-        const float sq = seq_sum_squares(sval, K, ss, reinterpret_cast<int*>(sval + (size_t)mt * K), mb);
+        const float sq = seq_sum_squares<PER>(sval, K, ss, nullptr, mb);
         if (tid == 0) {
             stat[0][0] = 0.0f;
             stat[0][1] = sqrtf(sq / (float)K);
         }
+    } else if (mt == 1) {
+        // LayerNorm of one row (ops.cpp:669-698): the reference's serial mean, then the exact
+        // parallel form of the sequential sum of squared deviations
+        __shared__ SeqSumSmem ss;
+        if (tid == 0) {
+            float s0 = 0.0f;
+            for (int i = 0; i < K; ++i) s0 = s0 + sval[i];
+            stat[0][0] = s0 / (float)K;
+        }
+        __syncthreads();
+        const float mean = stat[0][0];
+        const float dev = seq_sum_exact<PER>(
+            [sval, mean](int i) {
+                const float d = sval[i] - mean;
+                return d * d;
+            },
+            K, ss, nullptr);
+        if (tid == 0) stat[0][1] = sqrtf(dev / (float)K);
     } else if (tid < mt) {
         const float* v = sval + (long)tid * K;
         if (a.layer) {
@@ -374,6 +392,33 @@ __global__ void __launch_bounds__(NW * 32) k_fgemv(const FArgs a) {
         const float t = t01 + __shfl_xor_sync(0xffffffffu, t01, 2);
         if (l == 0 && r_local < nrows && m < mt) a.Y[(long)(m0 + m) * a.ldy + row0 + r_local] = t;
     }
+}
+
+// ---- batch-1 decode GEMV with its activation prologue ------------------------------------------
+// The exact single-row GEMV of k_gemv3 (gv3_prefetch / gv3_main) preceded by the activation
+// prologue, computed by every CTA into its own shared memory: PRO_RESNORM (residual update, block 0
+// writes the new residual row; then RMSNorm / LayerNorm with the exact sums, requantized) or
+// PRO_SWIGLU (per 32-block). The weight copies of the CTA's first two groups are issued before the
+// kernel waits for its predecessor. grid: persistent over groups of R rows; block GV3_THREADS;
+// dynamic shared memory gv3_smem<WDT>(R, K) + fg3_extra_smem(PRO, K) (the row's values for the
+// norm). PER: terms per thread of the exact sums (K <= PER * GV3_THREADS).
+constexpr int FG3_PER = 10;
+__host__ __device__ inline size_t fg3_extra_smem(int pro, int K) {
+    return pro == PRO_RESNORM ? (size_t)K * sizeof(float) : 0;
+}
+
+template <int WDT, int PRO>
+__global__ void __launch_bounds__(GV3_THREADS, 2) k_fgemv3(const FArgs a, int R, int RP) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int abort_flag;
+    int nissued[2];
+    gv3_prefetch<WDT>(smem, a.W, a.ws, a.N, a.K, R, &abort_flag, nissued);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    uint8_t* xs = gv3_xs<WDT>(smem, R, a.K);
+    float* sval = reinterpret_cast<float*>(smem + gv3_smem<WDT>(R, a.K));
+    fgemv_prologue<PRO, 1, FG3_PER>(a, xs, sval, 0, 1);
+    __syncthreads();
+    gv3_main<WDT>(smem, a.W, a.ws, a.N, a.K, a.Y, R, RP, a.err, &abort_flag, nissued);
 }
 
 // ---- residual update + norm on a cluster of PCL CTAs ------------------------------------------

@@ -492,62 +492,75 @@ __device__ __forceinline__ int gv3_pair(const uint32_t* w, int o1, int o2) {
     return (int)__byte_perm(w[o1 >> 2], w[o2 >> 2], sel);
 }
 
+// Shared memory of k_gemv3: [mbarriers 128][2 stages of R weight rows][products R*4 rows of pstr
+// floats][the activation row]. gv3_bars / gv3_stage / gv3_prod / gv3_xs give the pieces.
 template <int WDT>
-__global__ void __launch_bounds__(GV3_THREADS, 2) k_gemv3(const uint8_t* __restrict__ W, long w_stride, int N, int K,
-                                                         const uint8_t* __restrict__ X, float* __restrict__ Y, int R,
-                                                         int RP, unsigned int* err) {
+__device__ __forceinline__ uint8_t* gv3_stage(uint8_t* smem) { return smem + 128; }
+template <int WDT>
+__device__ __forceinline__ float* gv3_prod(uint8_t* smem, int R, int K) {
+    return reinterpret_cast<float*>(smem + 128 + (size_t)2 * R * gv3_rstride<WDT>(K));
+}
+template <int WDT>
+__device__ __forceinline__ uint8_t* gv3_xs(uint8_t* smem, int R, int K) {
+    return reinterpret_cast<uint8_t*>(gv3_prod<WDT>(smem, R, K) + (size_t)R * 4 * gv3_pstr(K / GTN_QBLK));
+}
+
+// Issues the TMA copies of group g (R rows, W and w_stride 16-byte aligned) into stage s; warp 0.
+template <int WDT>
+__device__ __forceinline__ void gv3_issue(uint8_t* smem, const uint8_t* W, long w_stride, int N, int K, int R, int g,
+                                          int s) {
+    const int lane = threadIdx.x & 31, rstride = gv3_rstride<WDT>(K);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+    uint8_t* stage = gv3_stage<WDT>(smem);
+    const int r0 = g * R, nr = min(R, N - r0);
+    if (lane == 0) mbar_arrive_expect_tx(&bars[s], (uint32_t)rstride * (uint32_t)nr);
+    __syncwarp();
+    for (int r = lane; r < nr; r += 32)
+        bulk_g2s(stage + ((size_t)s * R + r) * rstride, W + (size_t)(r0 + r) * w_stride, (uint32_t)rstride, &bars[s]);
+}
+
+// Before the kernel waits for its predecessor: barrier init and the copies of this CTA's first two
+// groups. nissued[s]: copies issued into stage s (meaningful in warp 0).
+template <int WDT>
+__device__ __forceinline__ void gv3_prefetch(uint8_t* smem, const uint8_t* W, long w_stride, int N, int K, int R,
+                                             int* abort_flag, int nissued[2]) {
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+        *abort_flag = 0;
+    }
+    __syncthreads();
+    const int ngroups = (N + R - 1) / R, g0 = blockIdx.x;
+    nissued[0] = nissued[1] = 0;
+    if ((threadIdx.x >> 5) == 0) {
+        if (g0 < ngroups) gv3_issue<WDT>(smem, W, w_stride, N, K, R, g0, 0), ++nissued[0];
+        if (g0 + (int)gridDim.x < ngroups) gv3_issue<WDT>(smem, W, w_stride, N, K, R, g0 + gridDim.x, 1), ++nissued[1];
+    }
+}
+
+// The GEMV over this CTA's groups once the Q8 activation row is in shared memory (gv3_xs): phase 1
+// products, phase 2 lane chains, Y[r] = (L0+L1)+(L2+L3). Ends with griddepcontrol.launch_dependents.
+template <int WDT>
+__device__ __forceinline__ void gv3_main(uint8_t* smem, const uint8_t* __restrict__ W, long w_stride, int N, int K,
+                                         float* __restrict__ Y, int R, int RP, unsigned int* err, int* abort_flag,
+                                         int nissued[2]) {
     using C = MMCfg<WDT>;
     constexpr int GB = 4 * C::BLK_BYTES, GW = GB / 4;  // bytes / words of 4 weight blocks
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ int abort_flag;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
     const int nb = K / GTN_QBLK, nbg = nb / 4;
     const int rstride = gv3_rstride<WDT>(K);
     const int pstr = gv3_pstr(nb);
-    uint8_t* stage = smem + 128;
-    float* prod = reinterpret_cast<float*>(stage + (size_t)2 * R * rstride);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint8_t* stage = gv3_stage<WDT>(smem);
+    float* prod = gv3_prod<WDT>(smem, R, K);
+    const uint8_t* xs = gv3_xs<WDT>(smem, R, K);
+    const int tid = threadIdx.x, warp = tid >> 5;
     const int j = tid % nbg, rs = tid / nbg;
     const bool p1 = rs < RP;
-    const int ngroups = (N + R - 1) / R;
-
-    auto issue = [&](int g, int s) {  // warp 0; W and w_stride are 16-byte aligned
-        const int r0 = g * R, nr = min(R, N - r0);
-        if (lane == 0) mbar_arrive_expect_tx(&bars[s], (uint32_t)rstride * (uint32_t)nr);
-        __syncwarp();
-        for (int r = lane; r < nr; r += 32)
-            bulk_g2s(stage + ((size_t)s * R + r) * rstride, W + (size_t)(r0 + r) * w_stride, (uint32_t)rstride,
-                     &bars[s]);
-    };
-
-    if (tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
-        fence_mbar_init();
-        abort_flag = 0;
-    }
-    __syncthreads();
-    const int g0 = blockIdx.x;
-    int nissued0 = 0, nissued1 = 0;  // meaningful in warp 0, which issues every copy
-    if (warp == 0) {
-        if (g0 < ngroups) issue(g0, 0), ++nissued0;
-        if (g0 + (int)gridDim.x < ngroups) issue(g0 + gridDim.x, 1), ++nissued1;
-    }
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    // the activation row into shared memory (coalesced), then this thread's lane words of blocks
-    // 4j..4j+3 (same packing as build_prep_q8) from four 34-byte blocks read as 8-byte words
-    uint8_t* xs = reinterpret_cast<uint8_t*>(prod + (size_t)R * 4 * pstr);
-    {
-        const int xbytes = nb * GTN_Q8_BYTES;
-        if ((reinterpret_cast<uintptr_t>(X) & 3) == 0) {
-            for (int i = tid; i < xbytes / 4; i += GV3_THREADS)
-                reinterpret_cast<uint32_t*>(xs)[i] = reinterpret_cast<const uint32_t*>(X)[i];
-            if (tid < (xbytes & 3)) xs[(xbytes & ~3) + tid] = X[(xbytes & ~3) + tid];
-        } else {
-            for (int i = tid; i < xbytes; i += GV3_THREADS) xs[i] = X[i];
-        }
-    }
-    __syncthreads();
+    const int ngroups = (N + R - 1) / R, g0 = blockIdx.x;
+    // this thread's lane words of activation blocks 4j..4j+3 (same packing as build_prep_q8) from
+    // four 34-byte blocks read as 8-byte words
     int a0[16], a1[16], asum[16];
     float da[4];
     {
@@ -577,9 +590,9 @@ __global__ void __launch_bounds__(GV3_THREADS, 2) k_gemv3(const uint8_t* __restr
     for (int g = g0; g < ngroups; g += gridDim.x, ++it) {
         const int s = it & 1;
         const int r0 = g * R, nr = min(R, N - r0);
-        if (!abort_flag && !mbar_wait_bounded(&bars[s], (it >> 1) & 1, err)) abort_flag = 1;
+        if (!*abort_flag && !mbar_wait_bounded(&bars[s], (it >> 1) & 1, err)) *abort_flag = 1;
         __syncthreads();
-        if (abort_flag) break;
+        if (*abort_flag) break;
         if (p1) {
             for (int r = rs; r < nr; r += RP) {
                 const uint2* src = reinterpret_cast<const uint2*>(stage + ((size_t)s * R + r) * rstride + (size_t)j * GB);
@@ -618,9 +631,8 @@ __global__ void __launch_bounds__(GV3_THREADS, 2) k_gemv3(const uint8_t* __restr
         }
         __syncthreads();
         if (warp == 0 && g + 2 * (int)gridDim.x < ngroups) {
-            issue(g + 2 * gridDim.x, s);
-            if (s == 0) ++nissued0;
-            else ++nissued1;
+            gv3_issue<WDT>(smem, W, w_stride, N, K, R, g + 2 * gridDim.x, s);
+            ++nissued[s];
         }
         if (tid < ((R * 4 + 31) & ~31)) {  // whole warps: the combine shuffles need every lane
             const int r = tid >> 2, l = tid & 3;
@@ -642,15 +654,37 @@ __global__ void __launch_bounds__(GV3_THREADS, 2) k_gemv3(const uint8_t* __restr
         __syncthreads();  // the products are rewritten by the next group
     }
     asm volatile("griddepcontrol.launch_dependents;");
-    if (abort_flag && tid == 0) {
+    if (*abort_flag && tid == 0) {
         // bounded wait for the last copy issued into each stage (phase nissued-1)
-        const int ni[2] = {nissued0, nissued1};
         for (int s = 0; s < 2; ++s) {
-            if (ni[s] == 0) continue;
+            if (nissued[s] == 0) continue;
             for (uint32_t i = 0; i < GTN_WAIT_LIMIT; ++i)
-                if (mbar_try_wait(&bars[s], (uint32_t)(ni[s] - 1) & 1)) break;
+                if (mbar_try_wait(&bars[s], (uint32_t)(nissued[s] - 1) & 1)) break;
         }
     }
+}
+
+template <int WDT>
+__global__ void __launch_bounds__(GV3_THREADS, 2) k_gemv3(const uint8_t* __restrict__ W, long w_stride, int N, int K,
+                                                         const uint8_t* __restrict__ X, float* __restrict__ Y, int R,
+                                                         int RP, unsigned int* err) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int abort_flag;
+    int nissued[2];
+    gv3_prefetch<WDT>(smem, W, w_stride, N, K, R, &abort_flag, nissued);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // the activation row into shared memory (coalesced)
+    uint8_t* xs = gv3_xs<WDT>(smem, R, K);
+    const int xbytes = (K / GTN_QBLK) * GTN_Q8_BYTES, tid = threadIdx.x;
+    if ((reinterpret_cast<uintptr_t>(X) & 3) == 0) {
+        for (int i = tid; i < xbytes / 4; i += GV3_THREADS)
+            reinterpret_cast<uint32_t*>(xs)[i] = reinterpret_cast<const uint32_t*>(X)[i];
+        if (tid < (xbytes & 3)) xs[(xbytes & ~3) + tid] = X[(xbytes & ~3) + tid];
+    } else {
+        for (int i = tid; i < xbytes; i += GV3_THREADS) xs[i] = X[i];
+    }
+    __syncthreads();
+    gv3_main<WDT>(smem, W, w_stride, N, K, Y, R, RP, err, &abort_flag, nissued);
 }
 
 // ---- exact GEMM for M >= 2 activation rows (prefill, batched decode) ----------------------------

@@ -40,7 +40,7 @@ constexpr int SEQSUM_THREADS_MAX = 1024;
 constexpr int SEQSUM_SLOTS = 64;      // binade slot = floor(log2(Q)), Q = the fixed-point sum
 constexpr int SEQSUM_TIES_MAX = 128;
 constexpr int SEQSUM_FRAC_BITS = 25;  // the largest term becomes < 2^(24 + 25)
-constexpr int SEQSUM_PER_MAX = 8;     // terms per thread kept in registers
+constexpr int SEQSUM_PER_MAX = 8;     // default terms per thread kept in registers
 
 struct SeqSumSmem {
     long long wsum[2][SEQSUM_THREADS_MAX / 32];  // per-warp partials of the two scans
