@@ -217,13 +217,13 @@ bool gemv_q_fits(int M, int wdt, int K) {
 // k_gemv3 plan for one activation row: rows per stage R = RP * passes (RP = rows covered by one
 // pass of 256 threads), as many passes (up to 16 rows) as keep two CTAs per SM.
 template <int WDT>
-static bool gv3_plan(const uint8_t* W, long ws, int N, int K, int* R, int* RP, size_t extra = 0) {
+static bool gv3_plan(const uint8_t* W, long ws, int N, int K, int* R, int* RP) {
     const int nb = K / GTN_QBLK;
     if (K % GTN_QBLK || nb % 4 || nb / 4 > GV3_THREADS || nb == 0) return false;
     if ((reinterpret_cast<uintptr_t>(W) & 15) || (ws & 15)) return false;
     const int rp = std::min(GV3_THREADS / (nb / 4), GV3_THREADS / 4);  // phase 2: 4 threads per row
     for (int passes = std::max(1, 16 / rp); passes >= 1; --passes)
-        if (gv3_smem<WDT>(rp * passes, K) + extra <= 110 * 1024) {
+        if (gv3_smem<WDT>(rp * passes, K) <= 110 * 1024) {
             *R = rp * passes;
             *RP = rp;
             // few rows (e.g. 2048-2560): halve the group so that every SM gets two groups
@@ -232,14 +232,6 @@ static bool gv3_plan(const uint8_t* W, long ws, int N, int K, int* R, int* RP, s
         }
     return false;
 }
-
-bool gemv1_plan(int wdt, const uint8_t* W, long ws, int N, int K, size_t extra, int* R, int* RP) {
-    if (wdt == GTN_Q8) return gv3_plan<GTN_Q8>(W, ws, N, K, R, RP, extra);
-    if (wdt == GTN_Q4) return gv3_plan<GTN_Q4>(W, ws, N, K, R, RP, extra);
-    return false;
-}
-
-int device_sm_count() { return sm_count(); }
 
 template <int WDT>
 static cudaError_t launch_gv3(const uint8_t* X, const uint8_t* W, long ws, int N, int K, float* Y, int R, int RP,

@@ -345,14 +345,23 @@ __device__ __forceinline__ void att_softmax(float* p, int n, int last, float mx,
     __syncthreads();
 }
 
+// Rows of the V tile starting at key t0: T keys, or up to the key n8 the lane chains stop at; the
+// tile that holds key n8 - 1 (tile 0 when n8 = 0) also takes the tail keys n8..n-1 when they fit,
+// so that att_out reads them from shared memory.
+__device__ __forceinline__ int att_vtile_rows(int t0, int n, int n8, int T) {
+    return (n8 - t0 <= T && n - t0 <= T) ? n - t0 : min(T, n8 - t0);
+}
+
 // Scores (keys [0, last] of the cache, -inf above), softmax, and the P.V lane chains, leaving the 8
 // lane partial sums in sm.part[l * d + c] (keys < n8). Key `jp` is read from kspecial / vspecial
 // (shared memory) instead of the cache. The first V tile is copied while the scores are computed.
-// Returns after a CTA barrier with no copy in flight.
+// Returns after a CTA barrier with no copy in flight; the last V tile stays in sm.vt (its first key
+// in *vt0, its rows in *vnt) for att_out.
 __device__ __forceinline__ void att_core(const uint8_t* k, long ks, const uint8_t* v, long vs, int hb, int n, int last,
                                          int jp, const uint8_t* kspecial, const uint8_t* vspecial,
                                          const uint8_t* qraw, const AttSmem& sm, int dt, int d, float* red,
-                                         float* stat, unsigned int* err, bool prefetched = false) {
+                                         float* stat, unsigned int* err, int* vt0, int* vnt,
+                                         bool prefetched = false) {
     const int tid = threadIdx.x;
     const int T = att_tile(hb);
     const bool kb = att_bulk(k, ks, hb), vb = att_bulk(v, vs, hb);
@@ -364,7 +373,7 @@ __device__ __forceinline__ void att_core(const uint8_t* k, long ks, const uint8_
     float mx = -INFINITY;
     if (!prefetched) {  // else the caller issued exactly these two fetches (att_prefetch)
         att_fetch(sm.kt, krs, k, ks, 0, max(0, min(min(T, n), last + 1)), hb, kb, &sm.bars[0]);
-        att_fetch(sm.vt, vrs, v, vs, 0, min(T, n8), hb, vb, &sm.bars[1]);
+        att_fetch(sm.vt, vrs, v, vs, 0, att_vtile_rows(0, n, n8, T), hb, vb, &sm.bars[1]);
     }
     for (int t0 = 0; t0 < n; t0 += T) {
         const int nt = min(T, n - t0);
@@ -392,11 +401,15 @@ __device__ __forceinline__ void att_core(const uint8_t* k, long ks, const uint8_
     att_softmax(sm.p, n, last, mx, dt, red, stat);
     const int units = d * 4;  // (channel, lane pair)
     float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};  // d <= 128: at most 2 units per thread
-    for (int t0 = 0; t0 < n8; t0 += T) {
-        const int nt = min(T, n8 - t0);
+    *vt0 = 0;
+    *vnt = 0;
+    for (int t0 = 0; t0 == 0 || t0 < n8; t0 += T) {
+        const int nt = att_vtile_rows(t0, n, n8, T);
         if (t0 > 0) att_fetch(sm.vt, vrs, v, vs, t0, nt, hb, vb, &sm.bars[1]);
         att_land(sm.vt, vrs, t0, nt, hb, jp, vspecial, vb, false, &sm.bars[1], vpar, sm.abort, err);
-        vpar ^= 1u;
+        if (nt > 0) vpar ^= 1u;
+        *vt0 = t0;
+        *vnt = nt;
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             const int un = tid + u * ATT_THREADS;
@@ -404,7 +417,7 @@ __device__ __forceinline__ void att_core(const uint8_t* k, long ks, const uint8_
         }
         __syncthreads();
     }
-    att_wait_group<0>();  // n8 == 0: the V group that was never landed
+    att_wait_group<0>();
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
         const int un = tid + u * ATT_THREADS;
@@ -431,13 +444,15 @@ __device__ __forceinline__ void att_prefetch(const uint8_t* k, long ks, const ui
     const int T = att_tile(hb), n8 = (n / 8) * 8;
     const bool kb = att_bulk(k, ks, hb), vb = att_bulk(v, vs, hb);
     att_fetch(sm.kt, kb ? (int)ks : att_rs(hb), k, ks, 0, max(0, min(min(T, n), last + 1)), hb, kb, &sm.bars[0]);
-    att_fetch(sm.vt, vb ? (int)vs : att_rs(hb), v, vs, 0, min(T, n8), hb, vb, &sm.bars[1]);
+    att_fetch(sm.vt, vb ? (int)vs : att_rs(hb), v, vs, 0, att_vtile_rows(0, n, n8, T), hb, vb, &sm.bars[1]);
 }
 
 // Output row of one head: the lane partials summed left to right, then the tail keys n8..n-1
-// (vec_f32x8_sum + the scalar loop of vec_dot_product_f32), written in dtype dt.
+// (vec_f32x8_sum + the scalar loop of vec_dot_product_f32), written in dtype dt. Tail keys held by
+// the last V tile (keys vt0 .. vt0 + vnt - 1 at vt, rows of vrs bytes) are read from it.
 __device__ __forceinline__ void att_out(const float* part, const float* p, const uint8_t* v, long vs, int n, int jp,
-                                        const uint8_t* vspecial, int dt, int d, uint8_t* dst) {
+                                        const uint8_t* vspecial, int dt, int d, uint8_t* dst, const uint8_t* vt,
+                                        int vrs, int vt0, int vnt) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int n8 = (n / 8) * 8;
     for (int blk = warp; blk * GTN_QBLK < d; blk += ATT_THREADS / 32) {
@@ -447,7 +462,7 @@ __device__ __forceinline__ void att_out(const float* part, const float* p, const
             y = part[c] + part[d + c];
             for (int l = 2; l < 8; ++l) y = y + part[l * d + c];
             for (int j = n8; j < n; ++j) {
-                const uint8_t* vr = j == jp ? vspecial : v + (long)j * vs;
+                const uint8_t* vr = j - vt0 < vnt ? vt + (long)(j - vt0) * vrs : (j == jp ? vspecial : v + (long)j * vs);
                 const float pr = p[j] * load_elem(vr, dt, c);
                 y = y + pr;
             }
@@ -479,9 +494,12 @@ static __global__ void __launch_bounds__(ATT_THREADS) k_attn(const uint8_t* q, l
     att_init_bars(bars, &abort_flag);
     if (dt == GTN_Q8) build_prep_q8(qh, 0, 0, 1, d / GTN_QBLK, L.qp);
     __syncthreads();
+    int vt0, vnt;
     att_core(k + (long)g * khs, ks, v + (long)g * vhs, vs, (int)hb, n, r, -1, nullptr, nullptr, qh, L, dt, d, red,
-             s_stat, err);
-    att_out(L.part, L.p, v + (long)g * vhs, vs, n, -1, nullptr, dt, d, out + (long)r * os + (long)h * hb);
+             s_stat, err, &vt0, &vnt);
+    const int vrs = att_bulk(v + (long)g * vhs, vs, (int)hb) ? (int)vs : att_rs(hb);
+    att_out(L.part, L.p, v + (long)g * vhs, vs, n, -1, nullptr, dt, d, out + (long)r * os + (long)h * hb, L.vt, vrs,
+            vt0, vnt);
 }
 
 }  // namespace gtn

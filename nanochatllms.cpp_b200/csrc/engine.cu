@@ -735,44 +735,27 @@ static cudaError_t fg_mt(const FArgs& a, cudaStream_t st, bool dry) {
     return big ? fg_launch<WDT, 4, 8, PRO>(a, st, dry) : fg_launch<WDT, 1, 8, PRO>(a, st, dry);
 }
 
-// k_fgemv3: one sequence's GEMV with its prologue in every CTA (Q8 / Q4 weights).
-template <int WDT, int PRO>
-static cudaError_t fg3_launch(const gtn_model* m, const FArgs& a, int R, int RP, bool dry) {
-    const size_t smem = gv3_smem<WDT>(R, a.K) + fg3_extra_smem(PRO, a.K);
-    const cudaError_t e = ensure_smem(k_fgemv3<WDT, PRO>, smem);
-    if (e != cudaSuccess || dry) return e;
+// Residual update + norm of every sequence into m->act: one cluster of PCL CTAs per sequence (the
+// row and the sum's scratch: 2K floats of shared memory).
+static cudaError_t prep_resnorm(const gtn_model* m, const FArgs& a, bool dry) {
+    const size_t csmem = 2 * sizeof(float) * (size_t)a.K;
+    if (dry) return ensure_smem(k_prep_cl, csmem);
     ++g_step_kernels;
-    const int ngroups = (a.N + R - 1) / R;
-    const int occ = (int)((227 * 1024) / (smem + 8 * 1024)) >= 2 ? 2 : 1;  // + static shared memory
-    const int gx = std::min(ngroups, device_sm_count() * occ);
-    return launch_pdl(k_fgemv3<WDT, PRO>, dim3(gx), dim3(GV3_THREADS), smem, m->st, a, R, RP);
+    return launch_pdl_cluster(k_prep_cl, dim3(PCL, a.B), dim3(PCL_THREADS), csmem, m->st, PCL, a, m->act, m->act_s);
 }
 
-// A GEMV whose activation needs a prologue: for one sequence (Q8 / Q4 weights) k_fgemv3 computes it
-// in every CTA; otherwise it runs once into m->act (residual + norm: k_prep_cl, one cluster per
-// sequence; SwiGLU: k_prep_swiglu) and the GEMV reads that row.
+// A GEMV whose activation needs a prologue runs it once into m->act (residual + norm: k_prep_cl;
+// SwiGLU: k_prep_swiglu); the GEMV then reads that row. (Computing the prologue inside every GEMV
+// CTA instead was measured slower: each of ~300 CTAs then redoes every block's requantizations and
+// the norm on 8 warps, 20-28 us per GEMV against 8 us for the cluster. Doing the SwiGLU in the
+// gate/up GEMV's epilogue, per 32-block by the CTA that completes it, was measured no faster than
+// the separate kernel.)
 static cudaError_t fgemv(const gtn_model* m, const FArgs& a, int pro, bool dry) {
     FArgs g = a;
-    int R = 0, RP = 0;
-    // (the SwiGLU prologue stays a kernel of its own: every GEMV CTA would redo the whole row's
-    // exp and three requantizations per element on 8 warps, longer than one wide pass)
-    if (pro == PRO_RESNORM && a.B == 1 && !a.active && (m->wdt == GTN_Q8 || m->wdt == GTN_Q4) &&
-        a.K <= FG3_PER * GV3_THREADS && gemv1_plan(m->wdt, a.W, a.ws, a.N, a.K, fg3_extra_smem(pro, a.K), &R, &RP)) {
-        if (m->wdt == GTN_Q8) return fg3_launch<GTN_Q8, PRO_RESNORM>(m, a, R, RP, dry);
-        return fg3_launch<GTN_Q4, PRO_RESNORM>(m, a, R, RP, dry);
-    }
     if (pro != PRO_COPY) {
         cudaError_t e;
         if (pro == PRO_RESNORM) {
-            // one cluster of PCL CTAs per sequence (the row and the sum's scratch: 2K floats)
-            const size_t csmem = 2 * sizeof(float) * (size_t)a.K;
-            if (dry) {
-                e = ensure_smem(k_prep_cl, csmem);
-            } else {
-                ++g_step_kernels;
-                e = launch_pdl_cluster(k_prep_cl, dim3(PCL, a.B), dim3(PCL_THREADS), csmem, m->st, PCL, a, m->act,
-                                       m->act_s);
-            }
+            e = prep_resnorm(m, a, dry);
         } else if (!dry) {
             ++g_step_kernels;
             const int nbk = (a.K + GTN_QBLK - 1) / GTN_QBLK;

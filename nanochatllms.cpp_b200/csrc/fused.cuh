@@ -194,9 +194,9 @@ __device__ __forceinline__ void fgemv_prologue(const FArgs& a, uint8_t* xq, floa
     if (lane == 0) wmax[warp] = mxb;
     __syncthreads();
     __shared__ float stat[MT][2];
+    __shared__ SeqSumSmem ss;
     if (mt == 1 && !a.layer) {
         // one row: the exact parallel form of the sequential sum of squares (seqsum.cuh)
-        __shared__ SeqSumSmem ss;
         unsigned int mb = lane < nwarps ? wmax[lane] : 0u;
         mb = __reduce_max_sync(0xffffffffu, mb);
         const float sq = seq_sum_squares<PER>(sval, K, ss, nullptr, mb);
@@ -207,7 +207,6 @@ __device__ __forceinline__ void fgemv_prologue(const FArgs& a, uint8_t* xq, floa
     } else if (mt == 1) {
         // LayerNorm of one row (ops.cpp:669-698): the reference's serial mean, then the exact
         // parallel form of the sequential sum of squared deviations
-        __shared__ SeqSumSmem ss;
         if (tid == 0) {
             float s0 = 0.0f;
             for (int i = 0; i < K; ++i) s0 = s0 + sval[i];
@@ -392,33 +391,6 @@ __global__ void __launch_bounds__(NW * 32) k_fgemv(const FArgs a) {
         const float t = t01 + __shfl_xor_sync(0xffffffffu, t01, 2);
         if (l == 0 && r_local < nrows && m < mt) a.Y[(long)(m0 + m) * a.ldy + row0 + r_local] = t;
     }
-}
-
-// ---- batch-1 decode GEMV with its activation prologue ------------------------------------------
-// The exact single-row GEMV of k_gemv3 (gv3_prefetch / gv3_main) preceded by the activation
-// prologue, computed by every CTA into its own shared memory: PRO_RESNORM (residual update, block 0
-// writes the new residual row; then RMSNorm / LayerNorm with the exact sums, requantized) or
-// PRO_SWIGLU (per 32-block). The weight copies of the CTA's first two groups are issued before the
-// kernel waits for its predecessor. grid: persistent over groups of R rows; block GV3_THREADS;
-// dynamic shared memory gv3_smem<WDT>(R, K) + fg3_extra_smem(PRO, K) (the row's values for the
-// norm). PER: terms per thread of the exact sums (K <= PER * GV3_THREADS).
-constexpr int FG3_PER = 10;
-__host__ __device__ inline size_t fg3_extra_smem(int pro, int K) {
-    return pro == PRO_RESNORM ? (size_t)K * sizeof(float) : 0;
-}
-
-template <int WDT, int PRO>
-__global__ void __launch_bounds__(GV3_THREADS, 2) k_fgemv3(const FArgs a, int R, int RP) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ int abort_flag;
-    int nissued[2];
-    gv3_prefetch<WDT>(smem, a.W, a.ws, a.N, a.K, R, &abort_flag, nissued);
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    uint8_t* xs = gv3_xs<WDT>(smem, R, a.K);
-    float* sval = reinterpret_cast<float*>(smem + gv3_smem<WDT>(R, a.K));
-    fgemv_prologue<PRO, 1, FG3_PER>(a, xs, sval, 0, 1);
-    __syncthreads();
-    gv3_main<WDT>(smem, a.W, a.ws, a.N, a.K, a.Y, R, RP, a.err, &abort_flag, nissued);
 }
 
 // ---- residual update + norm on a cluster of PCL CTAs ------------------------------------------
@@ -720,10 +692,13 @@ static __global__ void __launch_bounds__(ATT_THREADS) k_fattn(const AArgs a) {
     }
     if (a.adt == GTN_Q8) build_prep_q8(hrow[0], 0, 0, 1, nbh, L.qp);
     __syncthreads();
+    int vt0, vnt;
     att_core(kc, a.kvs, vc, a.kvs, (int)hb, n, p, p, hrow[1], hrow[2], hrow[0], L, a.adt, d, red, s_stat, a.err,
-             true);
+             &vt0, &vnt, true);
     asm volatile("griddepcontrol.launch_dependents;");
-    att_out(L.part, L.p, vc, a.kvs, n, p, hrow[2], a.adt, d, a.out + (long)b * a.os + (long)h * hb);
+    const int vrs = att_bulk(vc, a.kvs, (int)hb) ? (int)a.kvs : att_rs(hb);
+    att_out(L.part, L.p, vc, a.kvs, n, p, hrow[2], a.adt, d, a.out + (long)b * a.os + (long)h * hb, L.vt, vrs, vt0,
+            vnt);
 }
 
 inline size_t fattn_smem(int n, int adt, int d) { return attn_smem(n, adt, d); }

@@ -125,13 +125,6 @@ bool gemv_q_fits(int M, int wdt, int K);
 cudaError_t gemv_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
                    long ldy, cudaStream_t st, bool dry);
 
-// Plan of the single-row exact GEMV (k_gemv3 and the decode step's k_fgemv3) for Q8 / Q4 weights:
-// R rows per group, RP rows per pass, with `extra` more bytes of dynamic shared memory per CTA;
-// false when the shape or the weight alignment does not fit it.
-bool gemv1_plan(int wdt, const uint8_t* W, long ws, int N, int K, size_t extra, int* R, int* RP);
-// Number of SMs of the current device (cached per host thread).
-int device_sm_count();
-
 // Exact fp16 x fp16 matmul (k_mm_f16, the reference's 8-lane order) for M activation rows; W 16-byte
 // aligned with the `padded` precondition of matmul_f32. `dry` only configures shared memory.
 cudaError_t gemm_f16(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y, long ldy,
