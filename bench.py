@@ -668,6 +668,8 @@ def main():
                          "from a file in the page cache)")
     ap.add_argument("--decode-only", type=int, default=0, metavar="T",
                     help="only load the model and run one request of T generated tokens (for a launch list)")
+    ap.add_argument("--topk", type=int, default=0, metavar="K",
+                    help="with --decode-only: draw with top-k sampling (temperature 0.9, seed 7) instead of greedy")
     args = ap.parse_args()
     if args.decode_only:
         import numpy as np
@@ -678,7 +680,12 @@ def main():
         m = G.Model(G.TINYLLAMA, args.wdtype, N_PROMPT + N_GEN)
         m.load(gtenfile.synthetic_image_device(G.TINYLLAMA, args.wdtype, SEED))
         prompt = np.random.default_rng(42).integers(0, 32000, N_PROMPT).astype(np.int32)
-        out = m.generate(prompt, args.decode_only)
+        if args.topk:
+            rng = G.Rng(7)
+            out = m.generate_topk(prompt, args.decode_only, 0.9, args.topk, rng)
+            rng.close()
+        else:
+            out = m.generate(prompt, args.decode_only)
         m.check()
         m.close()
         print(json.dumps({"decode_only": args.decode_only, "first_ids": [int(x) for x in out[:8]]}), flush=True)
