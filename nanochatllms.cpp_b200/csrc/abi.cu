@@ -409,12 +409,17 @@ cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, 
 
 cudaError_t gemm_f16(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y, long ldy,
                      cudaStream_t st, bool dry) {
-    if (M >= 2) {  // k_gemm_f16: 32 weight rows x 16 activation rows per CTA
-        const size_t smem = mf_smem();
-        const cudaError_t e = ensure_smem(k_gemm_f16, smem);
+    if (M >= 2) {  // k_gemm_f16: 128 (or 32, for grids under two waves) weight rows x 16 rows per CTA
+        const int mtiles = (M + MF_MT - 1) / MF_MT;
+        const bool wide = (long)((N + mf_rows(4) - 1) / mf_rows(4)) * mtiles >= 2L * sm_count();
+        const size_t smem = mf_smem(wide ? 4 : 1);
+        const cudaError_t e = wide ? ensure_smem(k_gemm_f16<4>, smem) : ensure_smem(k_gemm_f16<1>, smem);
         if (e != cudaSuccess || dry) return e;
-        return launch_pdl(k_gemm_f16, dim3((N + MF_ROWS - 1) / MF_ROWS, (M + MF_MT - 1) / MF_MT), dim3(MF_THREADS),
-                          smem, st, W, ws, N, K, X, xs, M, Y, ldy, device_error_word());
+        if (wide)
+            return launch_pdl(k_gemm_f16<4>, dim3((N + mf_rows(4) - 1) / mf_rows(4), mtiles), dim3(MF_THREADS), smem,
+                              st, W, ws, N, K, X, xs, M, Y, ldy, device_error_word());
+        return launch_pdl(k_gemm_f16<1>, dim3((N + mf_rows(1) - 1) / mf_rows(1), mtiles), dim3(MF_THREADS), smem, st,
+                          W, ws, N, K, X, xs, M, Y, ldy, device_error_word());
     }
     const int mt = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
     int nw = 4;

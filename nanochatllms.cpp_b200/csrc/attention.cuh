@@ -345,11 +345,17 @@ __device__ __forceinline__ void att_softmax(float* p, int n, int last, float mx,
     __syncthreads();
 }
 
-// Rows of the V tile starting at key t0: T keys, or up to the key n8 the lane chains stop at; the
-// tile that holds key n8 - 1 (tile 0 when n8 = 0) also takes the tail keys n8..n-1 when they fit,
-// so that att_out reads them from shared memory.
-__device__ __forceinline__ int att_vtile_rows(int t0, int n, int n8, int T) {
-    return (n8 - t0 <= T && n - t0 <= T) ? n - t0 : min(T, n8 - t0);
+// Keys whose probability can be non-zero: 0..last (keys above are masked, p = 0). The reference's
+// P.V runs its 8 lane chains over keys < n8 = 8 * floor(n / 8) and a scalar tail over n8..n-1 of
+// every key, masked ones included; a masked key adds 0 * v = +-0 to a chain or to the tail, which
+// leaves an accumulator that started at +0 unchanged (round to nearest never makes it -0), so the
+// chains stop at key min(n8, last + 1) and the tail at key last (identical unless V holds inf or
+// NaN above the causal limit, where the reference's 0 * inf gives NaN).
+// Rows of the V tile starting at key t0: T keys, or up to key e8 = min(n8, last + 1) where the
+// chains stop; the tile that holds key e8 - 1 (tile 0 when e8 = 0) also takes the tail keys
+// n8..last when they fit, so that att_out reads them from shared memory.
+__device__ __forceinline__ int att_vtile_rows(int t0, int nk, int e8, int T) {
+    return (e8 - t0 <= T && nk - t0 <= T) ? nk - t0 : min(T, e8 - t0);
 }
 
 // Scores (keys [0, last] of the cache, -inf above), softmax, and the P.V lane chains, leaving the 8
@@ -368,12 +374,12 @@ __device__ __forceinline__ void att_core(const uint8_t* k, long ks, const uint8_
     const int krs = kb ? (int)ks : att_rs(hb), vrs = vb ? (int)vs : att_rs(hb);
     const bool kreg = d == 2 * GTN_QBLK && (krs & 15) == 0;  // 16-byte row loads (Q8 or fp16)
     const float scale = 1.0f / sqrtf((float)d);
-    const int n8 = (n / 8) * 8;
+    const int n8 = (n / 8) * 8, nk = min(n, last + 1), e8 = min(n8, nk);
     uint32_t kpar = 0, vpar = 0;
     float mx = -INFINITY;
     if (!prefetched) {  // else the caller issued exactly these two fetches (att_prefetch)
         att_fetch(sm.kt, krs, k, ks, 0, max(0, min(min(T, n), last + 1)), hb, kb, &sm.bars[0]);
-        att_fetch(sm.vt, vrs, v, vs, 0, att_vtile_rows(0, n, n8, T), hb, vb, &sm.bars[1]);
+        att_fetch(sm.vt, vrs, v, vs, 0, att_vtile_rows(0, nk, e8, T), hb, vb, &sm.bars[1]);
     }
     for (int t0 = 0; t0 < n; t0 += T) {
         const int nt = min(T, n - t0);
@@ -403,8 +409,8 @@ __device__ __forceinline__ void att_core(const uint8_t* k, long ks, const uint8_
     float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};  // d <= 128: at most 2 units per thread
     *vt0 = 0;
     *vnt = 0;
-    for (int t0 = 0; t0 == 0 || t0 < n8; t0 += T) {
-        const int nt = att_vtile_rows(t0, n, n8, T);
+    for (int t0 = 0; t0 == 0 || t0 < e8; t0 += T) {
+        const int nt = att_vtile_rows(t0, nk, e8, T);
         if (t0 > 0) att_fetch(sm.vt, vrs, v, vs, t0, nt, hb, vb, &sm.bars[1]);
         att_land(sm.vt, vrs, t0, nt, hb, jp, vspecial, vb, false, &sm.bars[1], vpar, sm.abort, err);
         if (nt > 0) vpar ^= 1u;
@@ -413,7 +419,7 @@ __device__ __forceinline__ void att_core(const uint8_t* k, long ks, const uint8_
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             const int un = tid + u * ATT_THREADS;
-            if (un < units) att_pv_tile(sm.vt, vrs, t0, nt, n8, sm.p, dt, un >> 2, 2 * (un & 3), acc[u][0], acc[u][1]);
+            if (un < units) att_pv_tile(sm.vt, vrs, t0, nt, e8, sm.p, dt, un >> 2, 2 * (un & 3), acc[u][0], acc[u][1]);
         }
         __syncthreads();
     }
@@ -441,18 +447,18 @@ __device__ __forceinline__ void att_core(const uint8_t* k, long ks, const uint8_
 // previous one: the cache rows below the new key do not depend on it).
 __device__ __forceinline__ void att_prefetch(const uint8_t* k, long ks, const uint8_t* v, long vs, int hb, int n,
                                              int last, const AttSmem& sm) {
-    const int T = att_tile(hb), n8 = (n / 8) * 8;
+    const int T = att_tile(hb), n8 = (n / 8) * 8, nk = min(n, last + 1), e8 = min(n8, nk);
     const bool kb = att_bulk(k, ks, hb), vb = att_bulk(v, vs, hb);
     att_fetch(sm.kt, kb ? (int)ks : att_rs(hb), k, ks, 0, max(0, min(min(T, n), last + 1)), hb, kb, &sm.bars[0]);
-    att_fetch(sm.vt, vb ? (int)vs : att_rs(hb), v, vs, 0, att_vtile_rows(0, n, n8, T), hb, vb, &sm.bars[1]);
+    att_fetch(sm.vt, vb ? (int)vs : att_rs(hb), v, vs, 0, att_vtile_rows(0, nk, e8, T), hb, vb, &sm.bars[1]);
 }
 
 // Output row of one head: the lane partials summed left to right, then the tail keys n8..n-1
 // (vec_f32x8_sum + the scalar loop of vec_dot_product_f32), written in dtype dt. Tail keys held by
 // the last V tile (keys vt0 .. vt0 + vnt - 1 at vt, rows of vrs bytes) are read from it.
-__device__ __forceinline__ void att_out(const float* part, const float* p, const uint8_t* v, long vs, int n, int jp,
-                                        const uint8_t* vspecial, int dt, int d, uint8_t* dst, const uint8_t* vt,
-                                        int vrs, int vt0, int vnt) {
+__device__ __forceinline__ void att_out(const float* part, const float* p, const uint8_t* v, long vs, int n, int last,
+                                        int jp, const uint8_t* vspecial, int dt, int d, uint8_t* dst,
+                                        const uint8_t* vt, int vrs, int vt0, int vnt) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int n8 = (n / 8) * 8;
     for (int blk = warp; blk * GTN_QBLK < d; blk += ATT_THREADS / 32) {
@@ -461,7 +467,7 @@ __device__ __forceinline__ void att_out(const float* part, const float* p, const
         if (c < d) {
             y = part[c] + part[d + c];
             for (int l = 2; l < 8; ++l) y = y + part[l * d + c];
-            for (int j = n8; j < n; ++j) {
+            for (int j = n8; j < n && j <= last; ++j) {  // masked tail keys add +-0
                 const uint8_t* vr = j - vt0 < vnt ? vt + (long)(j - vt0) * vrs : (j == jp ? vspecial : v + (long)j * vs);
                 const float pr = p[j] * load_elem(vr, dt, c);
                 y = y + pr;
@@ -498,8 +504,8 @@ static __global__ void __launch_bounds__(ATT_THREADS) k_attn(const uint8_t* q, l
     att_core(k + (long)g * khs, ks, v + (long)g * vhs, vs, (int)hb, n, r, -1, nullptr, nullptr, qh, L, dt, d, red,
              s_stat, err, &vt0, &vnt);
     const int vrs = att_bulk(v + (long)g * vhs, vs, (int)hb) ? (int)vs : att_rs(hb);
-    att_out(L.part, L.p, v + (long)g * vhs, vs, n, -1, nullptr, dt, d, out + (long)r * os + (long)h * hb, L.vt, vrs,
-            vt0, vnt);
+    att_out(L.part, L.p, v + (long)g * vhs, vs, n, r, -1, nullptr, dt, d, out + (long)r * os + (long)h * hb, L.vt,
+            vrs, vt0, vnt);
 }
 
 }  // namespace gtn

@@ -697,8 +697,8 @@ static __global__ void __launch_bounds__(ATT_THREADS) k_fattn(const AArgs a) {
              &vt0, &vnt, true);
     asm volatile("griddepcontrol.launch_dependents;");
     const int vrs = att_bulk(vc, a.kvs, (int)hb) ? (int)a.kvs : att_rs(hb);
-    att_out(L.part, L.p, vc, a.kvs, n, p, hrow[2], a.adt, d, a.out + (long)b * a.os + (long)h * hb, L.vt, vrs, vt0,
-            vnt);
+    att_out(L.part, L.p, vc, a.kvs, n, p, p, hrow[2], a.adt, d, a.out + (long)b * a.os + (long)h * hb, L.vt, vrs,
+            vt0, vnt);
 }
 
 inline size_t fattn_smem(int n, int adt, int d) { return attn_smem(n, adt, d); }

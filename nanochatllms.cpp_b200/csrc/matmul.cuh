@@ -327,39 +327,46 @@ __global__ void __launch_bounds__(NW * 32) k_mm_f16(const uint8_t* __restrict__ 
 }
 
 // ---- exact fp16 GEMM for several activation rows (prefill, batched decode) ----------------------
-// The arithmetic of k_mm_f16 (8 fp32 lanes over elements 8i+l, separate multiply and add roundings,
-// lanes summed left to right, then the scalar tail) for a tile of MF_ROWS weight rows x MF_MT
-// activation rows per CTA of 256 threads: thread (weight row r, lane l) keeps MF_MT accumulators.
-// Per K tile of MF_KT elements the weight rows arrive by TMA bulk copies (an MF_STAGES-deep ring)
-// and the activation tile is converted once to fp32 in an [element][row] layout (row stride padded
-// to 68 floats, so that the 8 lanes of a weight row read 8 consecutive elements with conflict-free
-// 16-byte loads): every float4 load feeds 4 products. grid (ceil(N / MF_ROWS), ceil(M / MF_MT)).
-constexpr int MF_ROWS = 32, MF_MT = 16, MF_KT = 128, MF_STAGES = MM_STAGES, MF_THREADS = 256;
+// The arithmetic of k_mm_f16 (8 fp32 lanes over elements 8i+l, lanes summed left to right, then the
+// scalar tail) for a tile of 32 * RW weight rows x MF_MT activation rows per CTA of 256 threads:
+// thread (row slot r, lane l) owns weight rows r + 32 i (i < RW) and keeps RW x MF_MT accumulators.
+// The reference multiplies and adds with separate roundings (no FMA in its build); a product of
+// two fp16 values is exact in fp32 (at most 22 significant bits, exponents within range), so
+// fma(x, w, acc) rounds exactly once, like fl(fl(x * w) + acc): one instruction per product here.
+// Per K tile (MF_KT(RW) elements) the weight rows arrive by TMA bulk copies (an MM_STAGES-deep
+// ring) and the activation tile is converted once to fp32 in an [element][row] layout (row stride
+// padded to 68 floats: the 8 lanes of a slot read 8 consecutive elements with conflict-free 16-byte
+// loads), so every float4 load feeds 4 * RW products. grid (ceil(N / (32 RW)), ceil(M / MF_MT)).
+constexpr int MF_MT = 16, MF_STAGES = MM_STAGES, MF_THREADS = 256;
 constexpr int MF_XSTR = 68;  // floats per element of the fp32 activation tile (16 rows + padding)
-__host__ __device__ inline int mf_wstride() { return MF_KT * 2 + 16; }
-__host__ __device__ inline size_t mf_smem() {
-    return 128 + (size_t)MF_STAGES * MF_ROWS * mf_wstride() + (size_t)MF_KT * MF_XSTR * sizeof(float);
+__host__ __device__ constexpr int mf_rows(int rw) { return 32 * rw; }
+__host__ __device__ constexpr int mf_kt(int rw) { return rw == 1 ? 128 : 64; }
+__host__ __device__ constexpr int mf_wstride(int rw) { return mf_kt(rw) * 2 + 16; }
+__host__ __device__ inline size_t mf_smem(int rw) {
+    return 128 + (size_t)MF_STAGES * mf_rows(rw) * mf_wstride(rw) + (size_t)mf_kt(rw) * MF_XSTR * sizeof(float);
 }
 
+template <int RW>
 static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t* __restrict__ W, long w_stride,
                                                                    int N, int K, const uint8_t* __restrict__ X,
                                                                    long x_stride, int M, float* __restrict__ Y,
                                                                    long y_stride, unsigned int* err) {
+    constexpr int ROWS = mf_rows(RW), KT = mf_kt(RW);
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int abort_flag;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-    const int wst = mf_wstride();
+    constexpr int WST = mf_wstride(RW);
     uint8_t* stages = smem + 128;
-    float* xt = reinterpret_cast<float*>(stages + (size_t)MF_STAGES * MF_ROWS * wst);
+    float* xt = reinterpret_cast<float*>(stages + (size_t)MF_STAGES * ROWS * WST);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int r = tid >> 3, l = tid & 7;
-    const int row0 = blockIdx.x * MF_ROWS, nrows = min(MF_ROWS, N - row0);
+    const int row0 = blockIdx.x * ROWS, nrows = min(ROWS, N - row0);
     const int m0 = blockIdx.y * MF_MT, mt = min(MF_MT, M - m0);
     const int K8 = (K / 8) * 8;
-    const int nkt = (K8 + MF_KT - 1) / MF_KT;
+    const int nkt = (K8 + KT - 1) / KT;
 
-    auto issue = [&](int kt) {  // warp 0: lane 0 arms the stage, lane i copies row i's tile
-        const int s = kt % MF_STAGES, e0 = kt * MF_KT, ne = min(MF_KT, K8 - e0);
+    auto issue = [&](int kt) {  // warp 0: lane 0 arms the stage, lane i copies rows i, i + 32, ...
+        const int s = kt % MF_STAGES, e0 = kt * KT, ne = min(KT, K8 - e0);
         uint32_t total = 0;
         for (int i = 0; i < nrows; ++i) {
             const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + i) * w_stride + (uintptr_t)e0 * 2;
@@ -370,7 +377,7 @@ static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t
         for (int i = lane; i < nrows; i += 32) {
             const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + i) * w_stride + (uintptr_t)e0 * 2;
             const uint32_t off = (uint32_t)(src & 15);
-            bulk_g2s(stages + ((size_t)s * MF_ROWS + i) * wst, reinterpret_cast<const void*>(src - off),
+            bulk_g2s(stages + ((size_t)s * ROWS + i) * WST, reinterpret_cast<const void*>(src - off),
                      (off + ne * 2 + 15) & ~15u, &bars[s]);
         }
     };
@@ -385,14 +392,16 @@ static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t
         for (int kt = 0; kt < min(MF_STAGES, nkt); ++kt) issue(kt);
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    float acc[MF_MT];
+    float acc[RW][MF_MT];
 #pragma unroll
-    for (int m = 0; m < MF_MT; ++m) acc[m] = 0.0f;
+    for (int i = 0; i < RW; ++i)
+#pragma unroll
+        for (int m = 0; m < MF_MT; ++m) acc[i][m] = 0.0f;
     for (int kt = 0; kt < nkt; ++kt) {
-        const int s = kt % MF_STAGES, e0 = kt * MF_KT, ne = min(MF_KT, K8 - e0);
+        const int s = kt % MF_STAGES, e0 = kt * KT, ne = min(KT, K8 - e0);
         // the activation tile as fp32, [element][row] (rows past M are 0); consecutive threads take
         // consecutive rows of one element pair (conflict-free stores)
-        for (int i = tid; i < MF_MT * (MF_KT / 2); i += MF_THREADS) {
+        for (int i = tid; i < MF_MT * (KT / 2); i += MF_THREADS) {
             const int m = i % MF_MT, e = 2 * (i / MF_MT);
             float2 v = make_float2(0.0f, 0.0f);
             if (m < mt && e < ne) {  // ne and e are even: both elements lie in the row
@@ -405,20 +414,31 @@ static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t
         }
         if (!abort_flag && !mbar_wait_bounded(&bars[s], (kt / MF_STAGES) & 1, err)) abort_flag = 1;
         __syncthreads();
-        if (!abort_flag && r < nrows) {
-            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + r) * w_stride + (uintptr_t)e0 * 2;
-            const uint16_t* wt = reinterpret_cast<const uint16_t*>(stages + ((size_t)s * MF_ROWS + r) * wst + (src & 15));
+        if (!abort_flag) {
+            const uint8_t* st = stages + (size_t)s * ROWS * WST;
+            const uint16_t* wt[RW];
+#pragma unroll
+            for (int i = 0; i < RW; ++i) {
+                const int rr = min(r + 32 * i, nrows - 1);  // rows past N: computed, never stored
+                const uintptr_t src =
+                    reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + rr) * w_stride + (uintptr_t)e0 * 2;
+                wt[i] = reinterpret_cast<const uint16_t*>(st + (size_t)(r + 32 * i) * WST + (src & 15));
+            }
             for (int e = l; e < ne; e += 8) {
-                const float w = h2f(wt[e]);
+                float w[RW];
+#pragma unroll
+                for (int i = 0; i < RW; ++i) w[i] = h2f(wt[i][e]);
                 const float4* xv = reinterpret_cast<const float4*>(xt + (size_t)e * MF_XSTR);
 #pragma unroll
                 for (int q = 0; q < MF_MT / 4; ++q) {
                     const float4 x4 = xv[q];
-                    const float p0 = x4.x * w, p1 = x4.y * w, p2 = x4.z * w, p3 = x4.w * w;
-                    acc[4 * q] = p0 + acc[4 * q];
-                    acc[4 * q + 1] = p1 + acc[4 * q + 1];
-                    acc[4 * q + 2] = p2 + acc[4 * q + 2];
-                    acc[4 * q + 3] = p3 + acc[4 * q + 3];
+#pragma unroll
+                    for (int i = 0; i < RW; ++i) {  // exact products: one rounding, as mul then add
+                        acc[i][4 * q] = __fmaf_rn(x4.x, w[i], acc[i][4 * q]);
+                        acc[i][4 * q + 1] = __fmaf_rn(x4.y, w[i], acc[i][4 * q + 1]);
+                        acc[i][4 * q + 2] = __fmaf_rn(x4.z, w[i], acc[i][4 * q + 2]);
+                        acc[i][4 * q + 3] = __fmaf_rn(x4.w, w[i], acc[i][4 * q + 3]);
+                    }
                 }
             }
         }
@@ -433,25 +453,29 @@ static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t
     // lanes summed left to right (simd_ops.h:75-78), then the scalar tail (ops.cpp:224-228)
     const int base = lane & ~7;
 #pragma unroll
-    for (int m = 0; m < MF_MT; ++m) {
-        float v[8];
+    for (int i = 0; i < RW; ++i) {
+        const int rr = r + 32 * i;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = __shfl_sync(0xffffffffu, acc[m], base + j);
-        if (l == 0 && r < nrows && m < mt) {
-            float d = v[0] + v[1];
-            d = d + v[2];
-            d = d + v[3];
-            d = d + v[4];
-            d = d + v[5];
-            d = d + v[6];
-            d = d + v[7];
-            const uint16_t* wr = reinterpret_cast<const uint16_t*>(W + (long)(row0 + r) * w_stride);
-            const uint16_t* xr = reinterpret_cast<const uint16_t*>(X + (long)(m0 + m) * x_stride);
-            for (int k = K8; k < K; ++k) {
-                const float pr = h2f(xr[k]) * h2f(wr[k]);
-                d = d + pr;
+        for (int m = 0; m < MF_MT; ++m) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __shfl_sync(0xffffffffu, acc[i][m], base + j);
+            if (l == 0 && rr < nrows && m < mt) {
+                float d = v[0] + v[1];
+                d = d + v[2];
+                d = d + v[3];
+                d = d + v[4];
+                d = d + v[5];
+                d = d + v[6];
+                d = d + v[7];
+                const uint16_t* wr = reinterpret_cast<const uint16_t*>(W + (long)(row0 + rr) * w_stride);
+                const uint16_t* xr = reinterpret_cast<const uint16_t*>(X + (long)(m0 + m) * x_stride);
+                for (int k = K8; k < K; ++k) {
+                    const float pr = h2f(xr[k]) * h2f(wr[k]);
+                    d = d + pr;
+                }
+                Y[(long)(m0 + m) * y_stride + row0 + rr] = d;
             }
-            Y[(long)(m0 + m) * y_stride + row0 + r] = d;
         }
     }
 }
