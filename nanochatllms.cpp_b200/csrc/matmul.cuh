@@ -333,17 +333,19 @@ __global__ void __launch_bounds__(NW * 32) k_mm_f16(const uint8_t* __restrict__ 
 // The reference multiplies and adds with separate roundings (no FMA in its build); a product of
 // two fp16 values is exact in fp32 (at most 22 significant bits, exponents within range), so
 // fma(x, w, acc) rounds exactly once, like fl(fl(x * w) + acc): one instruction per product here.
-// Per K tile (MF_KT(RW) elements) the weight rows arrive by TMA bulk copies (an MM_STAGES-deep
-// ring) and the activation tile is converted once to fp32 in an [element][row] layout (row stride
-// padded to 68 floats: the 8 lanes of a slot read 8 consecutive elements with conflict-free 16-byte
-// loads), so every float4 load feeds 4 * RW products. grid (ceil(N / (32 RW)), ceil(M / MF_MT)).
+// Per K tile (MF_KT(RW) elements) the weight rows and the activation rows arrive by TMA bulk copies
+// (an MM_STAGES-deep ring; activations 16-byte aligned, else loaded directly), and the activation
+// tile is converted once to fp32 in an [element][row] layout (row stride padded to 68 floats: the
+// 8 lanes of a slot read 8 consecutive elements with conflict-free 16-byte loads), so every float4
+// load feeds 4 * RW products. grid (ceil(N / (32 RW)), ceil(M / MF_MT)).
 constexpr int MF_MT = 16, MF_STAGES = MM_STAGES, MF_THREADS = 256;
 constexpr int MF_XSTR = 68;  // floats per element of the fp32 activation tile (16 rows + padding)
 __host__ __device__ constexpr int mf_rows(int rw) { return 32 * rw; }
 __host__ __device__ constexpr int mf_kt(int rw) { return rw == 1 ? 128 : 64; }
 __host__ __device__ constexpr int mf_wstride(int rw) { return mf_kt(rw) * 2 + 16; }
 __host__ __device__ inline size_t mf_smem(int rw) {
-    return 128 + (size_t)MF_STAGES * mf_rows(rw) * mf_wstride(rw) + (size_t)mf_kt(rw) * MF_XSTR * sizeof(float);
+    return 128 + (size_t)MF_STAGES * (mf_rows(rw) * mf_wstride(rw) + MF_MT * mf_kt(rw) * 2) +
+           (size_t)mf_kt(rw) * MF_XSTR * sizeof(float);
 }
 
 template <int RW>
@@ -357,17 +359,21 @@ static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
     constexpr int WST = mf_wstride(RW);
     uint8_t* stages = smem + 128;
-    float* xt = reinterpret_cast<float*>(stages + (size_t)MF_STAGES * ROWS * WST);
+    uint8_t* xst = stages + (size_t)MF_STAGES * ROWS * WST;  // [stage][MF_MT][KT] fp16 activation rows
+    float* xt = reinterpret_cast<float*>(xst + (size_t)MF_STAGES * MF_MT * KT * 2);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int r = tid >> 3, l = tid & 7;
     const int row0 = blockIdx.x * ROWS, nrows = min(ROWS, N - row0);
     const int m0 = blockIdx.y * MF_MT, mt = min(MF_MT, M - m0);
     const int K8 = (K / 8) * 8;
     const int nkt = (K8 + KT - 1) / KT;
+    // activation rows by bulk copy when every tile starts on a 16-byte boundary (tile sizes are
+    // multiples of 8 elements)
+    const bool xbulk = ((reinterpret_cast<uintptr_t>(X) | (uintptr_t)x_stride) & 15) == 0;
 
     auto issue = [&](int kt) {  // warp 0: lane 0 arms the stage, lane i copies rows i, i + 32, ...
         const int s = kt % MF_STAGES, e0 = kt * KT, ne = min(KT, K8 - e0);
-        uint32_t total = 0;
+        uint32_t total = xbulk ? (uint32_t)(mt * ne * 2) : 0u;
         for (int i = 0; i < nrows; ++i) {
             const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + i) * w_stride + (uintptr_t)e0 * 2;
             total += ((uint32_t)(src & 15) + ne * 2 + 15) & ~15u;
@@ -380,6 +386,9 @@ static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t
             bulk_g2s(stages + ((size_t)s * ROWS + i) * WST, reinterpret_cast<const void*>(src - off),
                      (off + ne * 2 + 15) & ~15u, &bars[s]);
         }
+        if (xbulk && lane < mt)
+            bulk_g2s(xst + ((size_t)s * MF_MT + lane) * KT * 2, X + (long)(m0 + lane) * x_stride + (long)e0 * 2,
+                     (uint32_t)(ne * 2), &bars[s]);
     };
 
     if (tid == 0) {
@@ -399,20 +408,21 @@ static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t
         for (int m = 0; m < MF_MT; ++m) acc[i][m] = 0.0f;
     for (int kt = 0; kt < nkt; ++kt) {
         const int s = kt % MF_STAGES, e0 = kt * KT, ne = min(KT, K8 - e0);
+        if (!abort_flag && !mbar_wait_bounded(&bars[s], (kt / MF_STAGES) & 1, err)) abort_flag = 1;
         // the activation tile as fp32, [element][row] (rows past M are 0); consecutive threads take
         // consecutive rows of one element pair (conflict-free stores)
         for (int i = tid; i < MF_MT * (KT / 2); i += MF_THREADS) {
             const int m = i % MF_MT, e = 2 * (i / MF_MT);
             float2 v = make_float2(0.0f, 0.0f);
             if (m < mt && e < ne) {  // ne and e are even: both elements lie in the row
-                const uint16_t* xr = reinterpret_cast<const uint16_t*>(X + (long)(m0 + m) * x_stride) + e0 + e;
+                const uint16_t* xr = xbulk ? reinterpret_cast<const uint16_t*>(xst + ((size_t)s * MF_MT + m) * KT * 2) + e
+                                           : reinterpret_cast<const uint16_t*>(X + (long)(m0 + m) * x_stride) + e0 + e;
                 v.x = h2f(xr[0]);
                 v.y = h2f(xr[1]);
             }
             xt[e * MF_XSTR + m] = v.x;
             xt[(e + 1) * MF_XSTR + m] = v.y;
         }
-        if (!abort_flag && !mbar_wait_bounded(&bars[s], (kt / MF_STAGES) & 1, err)) abort_flag = 1;
         __syncthreads();
         if (!abort_flag) {
             const uint8_t* st = stages + (size_t)s * ROWS * WST;
