@@ -231,7 +231,9 @@ def gemm_sweep(G, torch, wdt: int, device, M: int, only: str | None = None):
     gtn_matmul_2d (the tcgen05 kernel from 32 rows on) and, for comparison, gtn_matmul_2d_noalloc,
     which has no scratch for the activation image and so runs the CUDA-core GEMM. Rotating weight
     copies larger than L2. cells = M*N*K/8 lane sums; the CUDA-core bound of the exact epilogue is
-    SMs x 128 lanes x the SM clock / 3 ordered fp32 operations per lane sum."""
+    SMs x 128 lanes x the SM clock / 3 ordered fp32 operations per lane sum. With fp16 weights
+    (--wdtype 1) the exact fp16 GEMM (k_gemm_f16) is timed against SMs x 128 lanes x the clock
+    fused multiply-adds per second."""
     import ctypes as C
     from gten_b200 import row_bytes
     shapes = [(2560, 2048, "qkv"), (2048, 2048, "o"), (11264, 2048, "gate_up"), (2048, 5632, "down")]
@@ -241,19 +243,24 @@ def gemm_sweep(G, torch, wdt: int, device, M: int, only: str | None = None):
     bound = props.multi_processor_count * 128 * 1.965e9 / 3
     stream = torch.cuda.current_stream()
     out = {}
+    xdt = 1 if wdt == 1 else 3  # fp16 weights take fp16 activations, Q8 / Q4 weights Q8 ones
     for N, K, name in shapes:
         wb = N * row_bytes(wdt, K)
         ncopy = max(2, int(300e6 // wb) + 1)
-        ws = [torch.randint(0, 255, (wb,), dtype=torch.uint8, device=device) for _ in range(ncopy)]
-        bb = 34 if wdt == 3 else 18
-        for w in ws:  # valid fp16 deltas (1/1024) in every block
-            w.view(-1, bb)[:, 0] = 0x00
-            w.view(-1, bb)[:, 1] = 0x14
-        xq = torch.randint(0, 255, (M * row_bytes(3, K),), dtype=torch.uint8, device=device)
-        xq.view(-1, 34)[:, 0] = 0x00
-        xq.view(-1, 34)[:, 1] = 0x14
+        if wdt == 1:  # N(0, 0.02) fp16 weights, N(0, 1) fp16 activations
+            ws = [(torch.randn(N * K, device=device) * 0.02).half().view(torch.uint8) for _ in range(ncopy)]
+            xq = torch.randn(M * K, device=device).half().view(torch.uint8)
+        else:
+            ws = [torch.randint(0, 255, (wb,), dtype=torch.uint8, device=device) for _ in range(ncopy)]
+            bb = 34 if wdt == 3 else 18
+            for w in ws:  # valid fp16 deltas (1/1024) in every block
+                w.view(-1, bb)[:, 0] = 0x00
+                w.view(-1, bb)[:, 1] = 0x14
+            xq = torch.randint(0, 255, (M * row_bytes(3, K),), dtype=torch.uint8, device=device)
+            xq.view(-1, 34)[:, 0] = 0x00
+            xq.view(-1, 34)[:, 1] = 0x14
         y = torch.empty(M * N, dtype=torch.float32, device=device)
-        X, Y = G.GT(xq, 3, (M, K)), G.GT(y, 2, (M, N))
+        X, Y = G.GT(xq, xdt, (M, K)), G.GT(y, 2, (M, N))
 
         def tc(i):
             G.matmul_2d(X, G.GT(ws[i % ncopy], wdt, (N, K)), Y)
@@ -264,7 +271,7 @@ def gemm_sweep(G, torch, wdt: int, device, M: int, only: str | None = None):
             assert rc == 0, G.lib().gtn_last_error()
 
         res = {"N": N, "K": K, "M": M}
-        for key, fn in (("tc", tc), ("cuda_cores", cc)):
+        for key, fn in ((("k_gemm_f16", tc),) if wdt == 1 else (("tc", tc), ("cuda_cores", cc))):
             for i in range(3):
                 fn(i)
             reps = 2 * ncopy
@@ -276,9 +283,14 @@ def gemm_sweep(G, torch, wdt: int, device, M: int, only: str | None = None):
             ev1.record(stream)
             torch.cuda.synchronize()
             t = ev0.elapsed_time(ev1) / reps * 1e-3
-            cells = M * N * K / 8
-            res[key] = {"us": round(t * 1e6, 2), "T_cells_s": round(cells / t / 1e12, 3),
-                        "frac_of_epilogue_bound": round(cells / t / bound, 3)}
+            if wdt == 1:  # products: one fused multiply-add each on 128 lanes per SM
+                macs = M * N * K
+                res[key] = {"us": round(t * 1e6, 2), "T_mac_s": round(macs / t / 1e12, 3),
+                            "frac_of_fma_bound": round(macs / t / (bound * 3), 3)}
+            else:
+                cells = M * N * K / 8
+                res[key] = {"us": round(t * 1e6, 2), "T_cells_s": round(cells / t / 1e12, 3),
+                            "frac_of_epilogue_bound": round(cells / t / bound, 3)}
         out[name] = res
         del ws
     torch.cuda.empty_cache()

@@ -371,7 +371,16 @@ static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t
     // multiples of 8 elements)
     const bool xbulk = ((reinterpret_cast<uintptr_t>(X) | (uintptr_t)x_stride) & 15) == 0;
 
-    auto issue = [&](int kt) {  // warp 0: lane 0 arms the stage, lane i copies rows i, i + 32, ...
+    // warp 0: lane 0 arms the stage for the weight and activation bytes, lane i copies weight rows
+    // i, i + 32, ... and activation row i. The activation rows come from the previous kernel: the
+    // stages armed before griddepcontrol.wait get them from issue_x after it.
+    auto issue_x = [&](int kt) {
+        const int s = kt % MF_STAGES, e0 = kt * KT, ne = min(KT, K8 - e0);
+        if (xbulk && lane < mt)
+            bulk_g2s(xst + ((size_t)s * MF_MT + lane) * KT * 2, X + (long)(m0 + lane) * x_stride + (long)e0 * 2,
+                     (uint32_t)(ne * 2), &bars[s]);
+    };
+    auto issue = [&](int kt, bool with_x) {
         const int s = kt % MF_STAGES, e0 = kt * KT, ne = min(KT, K8 - e0);
         uint32_t total = xbulk ? (uint32_t)(mt * ne * 2) : 0u;
         for (int i = 0; i < nrows; ++i) {
@@ -386,9 +395,7 @@ static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t
             bulk_g2s(stages + ((size_t)s * ROWS + i) * WST, reinterpret_cast<const void*>(src - off),
                      (off + ne * 2 + 15) & ~15u, &bars[s]);
         }
-        if (xbulk && lane < mt)
-            bulk_g2s(xst + ((size_t)s * MF_MT + lane) * KT * 2, X + (long)(m0 + lane) * x_stride + (long)e0 * 2,
-                     (uint32_t)(ne * 2), &bars[s]);
+        if (with_x) issue_x(kt);
     };
 
     if (tid == 0) {
@@ -398,8 +405,10 @@ static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t
     }
     __syncthreads();
     if (warp == 0)
-        for (int kt = 0; kt < min(MF_STAGES, nkt); ++kt) issue(kt);
+        for (int kt = 0; kt < min(MF_STAGES, nkt); ++kt) issue(kt, false);  // weights: independent of it
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (warp == 0)
+        for (int kt = 0; kt < min(MF_STAGES, nkt); ++kt) issue_x(kt);
 
     float acc[RW][MF_MT];
 #pragma unroll
@@ -453,7 +462,7 @@ static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t
             }
         }
         __syncthreads();  // the stage and the activation tile are rewritten next
-        if (warp == 0 && !abort_flag && kt + MF_STAGES < nkt) issue(kt + MF_STAGES);
+        if (warp == 0 && !abort_flag && kt + MF_STAGES < nkt) issue(kt + MF_STAGES, true);
     }
     asm volatile("griddepcontrol.launch_dependents;");
     if (abort_flag) {
