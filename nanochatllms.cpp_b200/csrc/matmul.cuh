@@ -371,44 +371,56 @@ static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t
     // multiples of 8 elements)
     const bool xbulk = ((reinterpret_cast<uintptr_t>(X) | (uintptr_t)x_stride) & 15) == 0;
 
-    // warp 0: lane 0 arms the stage for the weight and activation bytes, lane i copies weight rows
-    // i, i + 32, ... and activation row i. The activation rows come from the previous kernel: the
-    // stages armed before griddepcontrol.wait get them from issue_x after it.
-    auto issue_x = [&](int kt) {
-        const int s = kt % MF_STAGES, e0 = kt * KT, ne = min(KT, K8 - e0);
-        if (xbulk && lane < mt)
-            bulk_g2s(xst + ((size_t)s * MF_MT + lane) * KT * 2, X + (long)(m0 + lane) * x_stride + (long)e0 * 2,
-                     (uint32_t)(ne * 2), &bars[s]);
+    // Copies of one K tile: every warp copies its own weight rows (slots 4w..4w+3: rows slot + 32 i;
+    // lanes 0..4 RW-1) and two activation rows (lanes 16, 17); thread 0 arms the stage's mbarrier
+    // with the tile's bytes before any of them is issued. The activation rows come from the
+    // previous kernel: for the stages armed before griddepcontrol.wait they are copied after it.
+    auto wrow_bytes = [&](int ne) {  // bytes of the tile's weight copies (16-byte rounded per row)
+        if (((reinterpret_cast<uintptr_t>(W) | (uintptr_t)w_stride) & 15) == 0) return (uint32_t)(nrows * ne * 2);
+        uint32_t t = 0;
+        for (int i = 0; i < nrows; ++i)
+            t += ((uint32_t)((reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + i) * w_stride) & 15) + ne * 2 + 15) &
+                 ~15u;
+        return t;
     };
-    auto issue = [&](int kt, bool with_x) {
+    const int ne_last = K8 - (nkt - 1) * KT;
+    const uint32_t wb_full = tid == 0 ? wrow_bytes(KT) : 0u, wb_last = tid == 0 ? wrow_bytes(ne_last) : 0u;
+    auto arm = [&](int kt) {  // thread 0
+        const int ne = min(KT, K8 - kt * KT);
+        mbar_arrive_expect_tx(&bars[kt % MF_STAGES],
+                              (ne == KT ? wb_full : wb_last) + (xbulk ? (uint32_t)(mt * ne * 2) : 0u));
+    };
+    auto copy_w = [&](int kt) {
         const int s = kt % MF_STAGES, e0 = kt * KT, ne = min(KT, K8 - e0);
-        uint32_t total = xbulk ? (uint32_t)(mt * ne * 2) : 0u;
-        for (int i = 0; i < nrows; ++i) {
-            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + i) * w_stride + (uintptr_t)e0 * 2;
-            total += ((uint32_t)(src & 15) + ne * 2 + 15) & ~15u;
+        if (lane < 4 * RW) {
+            const int i = 4 * warp + (lane & 3) + 32 * (lane >> 2);
+            if (i < nrows) {
+                const uintptr_t src =
+                    reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + i) * w_stride + (uintptr_t)e0 * 2;
+                const uint32_t off = (uint32_t)(src & 15);
+                bulk_g2s(stages + ((size_t)s * ROWS + i) * WST, reinterpret_cast<const void*>(src - off),
+                         (off + ne * 2 + 15) & ~15u, &bars[s]);
+            }
         }
-        if (lane == 0) mbar_arrive_expect_tx(&bars[s], total);
-        __syncwarp();
-        for (int i = lane; i < nrows; i += 32) {
-            const uintptr_t src = reinterpret_cast<uintptr_t>(W) + (uintptr_t)(row0 + i) * w_stride + (uintptr_t)e0 * 2;
-            const uint32_t off = (uint32_t)(src & 15);
-            bulk_g2s(stages + ((size_t)s * ROWS + i) * WST, reinterpret_cast<const void*>(src - off),
-                     (off + ne * 2 + 15) & ~15u, &bars[s]);
-        }
-        if (with_x) issue_x(kt);
+    };
+    auto copy_x = [&](int kt) {
+        const int s = kt % MF_STAGES, e0 = kt * KT, ne = min(KT, K8 - e0);
+        const int m = 2 * warp + (lane - 16);
+        if (xbulk && lane >= 16 && lane < 18 && m < mt)
+            bulk_g2s(xst + ((size_t)s * MF_MT + m) * KT * 2, X + (long)(m0 + m) * x_stride + (long)e0 * 2,
+                     (uint32_t)(ne * 2), &bars[s]);
     };
 
     if (tid == 0) {
         for (int s = 0; s < MF_STAGES; ++s) mbar_init(&bars[s], 1);
         fence_mbar_init();
         abort_flag = 0;
+        for (int kt = 0; kt < min(MF_STAGES, nkt); ++kt) arm(kt);
     }
     __syncthreads();
-    if (warp == 0)
-        for (int kt = 0; kt < min(MF_STAGES, nkt); ++kt) issue(kt, false);  // weights: independent of it
+    for (int kt = 0; kt < min(MF_STAGES, nkt); ++kt) copy_w(kt);  // weights: independent of it
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (warp == 0)
-        for (int kt = 0; kt < min(MF_STAGES, nkt); ++kt) issue_x(kt);
+    for (int kt = 0; kt < min(MF_STAGES, nkt); ++kt) copy_x(kt);
 
     float acc[RW][MF_MT];
 #pragma unroll
@@ -461,8 +473,12 @@ static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t
                 }
             }
         }
+        if (tid == 0 && !abort_flag && kt + MF_STAGES < nkt) arm(kt + MF_STAGES);  // every thread passed the wait
         __syncthreads();  // the stage and the activation tile are rewritten next
-        if (warp == 0 && !abort_flag && kt + MF_STAGES < nkt) issue(kt + MF_STAGES, true);
+        if (!abort_flag && kt + MF_STAGES < nkt) {
+            copy_w(kt + MF_STAGES);
+            copy_x(kt + MF_STAGES);
+        }
     }
     asm volatile("griddepcontrol.launch_dependents;");
     if (abort_flag) {
