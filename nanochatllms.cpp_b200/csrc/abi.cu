@@ -540,7 +540,9 @@ static int norm_common(const gtn_tensor* inp, const gtn_tensor* weight, const gt
         GTN_REQUIRE(bias->ndim == 1 && bias->dtype == GTN_F16 && bias->shape[0] == n, "layer_norm: bias");
     }
     const size_t smem = 2 * sizeof(float) * (size_t)n;  // values + the exact sum's scratch
-    const int nthreads = n > 1024 ? 512 : 256;  // the exact sum keeps <= 8 terms per thread up to n = 4096
+    // the exact parallel sum (n > 256) keeps <= 8 terms per thread up to n = 4096; shorter rows sum
+    // serially, with a block of at least one warp per 32-element block
+    const int nthreads = n > 1024 ? 512 : (n > 256 ? 256 : ((n + 31) / 32 * 32 < 64 ? 64 : (n + 31) / 32 * 32));
     cudaError_t e;
     if (layer) {
         e = ensure_smem(k_norm<true>, smem);

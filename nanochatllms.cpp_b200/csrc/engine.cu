@@ -654,9 +654,9 @@ static int forward(gtn_model* m, int seq, int n, int sp) {
         const long hb = row_bytes(adt, dh);
         if (m->family == 3) {
             // openelm.cpp:44-52: QK RMSNorm over heads, then RoPE into the cache / query buffer.
-            GK(launch_pdl(k_norm<false>, dim3(Ly.nh, M), dim3(256), 2 * sizeof(float) * dh, st, (const uint8_t*)m->q, rq,
+            GK(launch_pdl(k_norm<false>, dim3(Ly.nh, M), dim3(64), 2 * sizeof(float) * dh, st, (const uint8_t*)m->q, rq,
                           hb, m->qn, rq, hb, adt, dh, 0, Ly.qnw, (const uint16_t*)nullptr));
-            GK(launch_pdl(k_norm<false>, dim3(Ly.nkv, M), dim3(256), 2 * sizeof(float) * dh, st,
+            GK(launch_pdl(k_norm<false>, dim3(Ly.nkv, M), dim3(64), 2 * sizeof(float) * dh, st,
                           (const uint8_t*)kr, rkv, hb, m->kn, rkv, hb, adt, dh, 0, Ly.knw, (const uint16_t*)nullptr));
             // the rope kernels index rows by absolute position; local buffers get bases shifted by -sp rows
             GK(launch_pdl(k_rope, dim3(Ly.nh, M), dim3(32), 0, st, (const uint8_t*)(m->qn - (long)sp * rq), rq,

@@ -64,7 +64,8 @@ static __global__ void k_rowop(const uint8_t* a, long as, const uint8_t* b, long
 // order, as the reference computes them (one thread), the rest is element-parallel.
 //   rms_norm_vec_f32 ops.cpp:830-846: x / (sqrt(sum(x^2)/n) + 1e-6) * w
 //   vec_layer_norm_f32 ops.cpp:669-698: ((x - mean) / (sqrt(sum((x-mean)^2)/n) + 1e-5)) * w + b
-// grid: (heads, rows); block 256 (512 for n > 1024); dynamic smem 2n floats (values + the exact
+// grid: (heads, rows); block 64 for the head norms (n = 64), 256 (512 for n > 1024) otherwise, and
+// all threads reach the exact parallel sum (n > 256); dynamic smem 2n floats (values + the exact
 // sum's scratch).
 template <bool LAYER>
 static __global__ void k_norm(const uint8_t* x, long xs, long hs, uint8_t* out, long os, long ohs, int dt, int n,
@@ -76,8 +77,9 @@ static __global__ void k_norm(const uint8_t* x, long xs, long hs, uint8_t* out, 
     const uint8_t* src = x + (long)row * xs + (long)h * hs;
     for (int i = threadIdx.x; i < n; i += blockDim.x) v[i] = load_elem(src, dt, i);
     __syncthreads();
-    if (!LAYER) {
-        // the sequential sum of squares, computed exactly in parallel (seqsum.cuh)
+    if (!LAYER && n > 256) {
+        // the sequential sum of squares, computed exactly in parallel (seqsum.cuh); short rows
+        // (OpenELM's 64-wide head norms) take the serial loop below, which is faster there
         __shared__ SeqSumSmem ss;
         const float sq = seq_sum_squares(v, n, ss, reinterpret_cast<int*>(v + n));
         if (threadIdx.x == 0) {
