@@ -236,6 +236,41 @@ void* gtn_model_stream(gtn_model* m);
 /* Waits for the model's stream and returns GTN_ERR_DEVICE if a kernel flagged an error. */
 int gtn_model_check(gtn_model* m);
 
+/* ---- tokenizers (src/gten/abc.h:31-54 Tokenizer; src/gten/tokenizer.{h,cpp}) ---------------- */
+/* Host code only (no CUDA calls). Ids and decoded bytes equal the reference's for every input;
+ * a handle may be used from several threads at once (encode and decode do not modify it). */
+
+typedef struct gtn_tokenizer gtn_tokenizer;
+
+/* LLamaTokenizer(path, vocab_size, eos, prompt_prefix, prompt_suffix, tokens_prefix, tokens_suffix)
+ * (tokenizer.h:27-31, tokenizer.cpp:30-65): the SentencePiece-BPE vocabulary file (int32
+ * max_token_length, then vocab_size records of float32 score, int32 length, bytes). The prompt
+ * strings are NUL-terminated (NULL = ""). GTN_ERR_FORMAT when the file holds fewer than vocab_size
+ * records (the reference exits). */
+int gtn_tokenizer_create_llama(const char* path, int vocab_size, int eos, const char* prompt_prefix,
+                               const char* prompt_suffix, const int32_t* tokens_prefix, int n_prefix,
+                               const int32_t* tokens_suffix, int n_suffix, gtn_tokenizer** out);
+
+/* Gpt2Tokenizer(vocab_path, n_vocab, eos) (tokenizer.h:51, tokenizer.cpp:249-268): records of
+ * uint32 length, bytes. As in the reference, ids past the file's last record repeat that record. */
+int gtn_tokenizer_create_gpt2(const char* path, int n_vocab, int eos, gtn_tokenizer** out);
+
+void gtn_tokenizer_free(gtn_tokenizer* t);
+int gtn_tokenizer_vocab_size(const gtn_tokenizer* t);
+int gtn_tokenizer_eos(const gtn_tokenizer* t);
+
+/* Tokenizer::encode(prompt) (abc.h:53; tokenizer.cpp:103-241 and 278-331): len bytes of host text
+ * -> ids (host int32). *n_ids receives the number of ids; when it exceeds cap nothing is copied and
+ * GTN_ERR_ARG is returned (call again with a larger buffer). The caller's text is not modified (the
+ * reference's LLamaTokenizer::encode rewrites its argument to prefix + prompt + suffix). */
+int gtn_tokenizer_encode(const gtn_tokenizer* t, const char* text, size_t len, int32_t* ids, int cap, int* n_ids);
+
+/* Tokenizer::decode(prev_token, token) (abc.h:52; tokenizer.cpp:77-93 and 272-275): *piece points
+ * to *len bytes owned by the tokenizer (valid until gtn_tokenizer_free), the bytes of the C string
+ * the reference returns. Ids outside [0, vocab_size) decode to "" (the reference reads out of bounds
+ * for negative LLamaTokenizer ids). */
+int gtn_tokenizer_decode(const gtn_tokenizer* t, int prev_token, int token, const char** piece, size_t* len);
+
 #ifdef __cplusplus
 }
 #endif

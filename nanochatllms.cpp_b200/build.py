@@ -1,6 +1,7 @@
-"""Builds lib/libgten_b200.so (all CUDA sources, sm_100a) in-tree.
+"""Builds lib/libgten_b200.so (all CUDA sources, sm_100a, and the host-only C++ sources) in-tree.
 
-Each translation unit in csrc/ is compiled in parallel with
+Each translation unit in csrc/ (``*.cu``, and ``*.cpp`` host code through the same driver) is
+compiled in parallel with
 ``nvcc -gencode arch=compute_100a,code=sm_100a -O3 --fmad=false -lineinfo``; objects are reused
 while their sources and headers are unchanged. ``--fmad=false`` is part of the numerics
 contract: the reference CPU build rounds every multiply and add separately.
@@ -45,7 +46,7 @@ def _compile(src: str) -> str:
 def build(verbose: bool = False) -> str:
     os.makedirs(OUT_DIR, exist_ok=True)
     os.makedirs(OBJ_DIR, exist_ok=True)
-    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
     with ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
         objs = list(ex.map(_compile, srcs))
     if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):

@@ -34,7 +34,9 @@ SRCS=(
   "$REF/src/zephyr/zephyr.cpp"
   "$REF/src/minicpm/minicpm.cpp"
   "$REF/src/openelm/openelm.cpp"
+  "$REF/src/gten/tokenizer.cpp"
   "$HERE/ref_harness.cpp"
+  "$HERE/tok_harness.cpp"
 )
 OBJS=()
 pids=()
@@ -50,5 +52,10 @@ for p in "${pids[@]}"; do wait "$p"; done
 # Link the OpenMP runtime by path: this toolchain's driver does not find libgomp.spec.
 GOMP="$($CXX -print-file-name=libgomp.so.1)"
 [ -f "$GOMP" ] || GOMP=/usr/lib/x86_64-linux-gnu/libgomp.so.1
-$CXX -shared -o "$OUT/libgtenref.so" "${OBJS[@]}" "$GOMP" -lpthread
+# Link the shared libstdc++ by path too: where the driver only finds libstdc++.a, the library would
+# carry its own copy, whose locale facets (GNU-unique symbols) clash with the shared copy that
+# other modules of the same process load (std::regex in Gpt2Tokenizer then crashes).
+STDCXX="$($CXX -print-file-name=libstdc++.so.6)"
+[ -f "$STDCXX" ] || STDCXX=/usr/lib/x86_64-linux-gnu/libstdc++.so.6
+$CXX -shared -o "$OUT/libgtenref.so" "${OBJS[@]}" "$STDCXX" "$GOMP" -lpthread
 echo "built $OUT/libgtenref.so"
