@@ -499,6 +499,12 @@ def run_batch(args, rank, world, local):
     launches = G.kernel_launches() - launches0
     clk = clocks.stop()
     t = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+    if world > 1:
+        # the ids' gather is the process's first point-to-point exchange: set it up (NCCL creates
+        # its communicators lazily, which took ~1 s at 4 ranks) before the end-to-end clock starts
+        import torch.distributed as dist
+        parts = [None] * world if rank == 0 else None
+        dist.gather_object((0, np.zeros((0, n_gen), np.int32)), parts, dst=0)
     barrier(world)
     t0 = time.perf_counter()
     for _ in range(args.steps):
