@@ -210,8 +210,9 @@ static cudaError_t gemv2(const uint8_t* X, long xs, int M, const uint8_t* W, lon
 #undef GV
 }
 
+// k_gemv2 serves one activation row where k_gemv3 does not apply; two or more go to k_gemm4.
 bool gemv_q_fits(int M, int wdt, int K) {
-    return M >= 1 && M <= 4 && (wdt == GTN_Q8 || wdt == GTN_Q4) && gv2_smem<GTN_Q8>(8, 1, K) <= GV2_SMEM_LIMIT;
+    return M == 1 && (wdt == GTN_Q8 || wdt == GTN_Q4) && gv2_smem<GTN_Q8>(8, 1, K) <= GV2_SMEM_LIMIT;
 }
 
 // k_gemv3 plan for one activation row: rows per stage R = RP * passes (RP = rows covered by one
@@ -289,6 +290,63 @@ static cudaError_t launch_gm3(const uint8_t* X, long xs, int M, const uint8_t* W
     if (e != cudaSuccess || dry) return e;
     return launch_pdl(k_gemm3<WDT>, dim3((N + p.R - 1) / p.R, (M + p.MT - 1) / p.MT), dim3(GV3_THREADS), smem, st, W,
                       ws, N, K, X, xs, M, Y, ldy, p.R, p.MT, p.MC, device_error_word());
+}
+
+// k_gemm4 plan: R weight rows per group (one pass of 256 threads over the 4-block groups), the
+// activation tile MT (all M rows, else halves) and MC rows per product chunk, preferring two CTAs
+// per SM (within 110 KB of shared memory), then one (200 KB).
+template <int WDT>
+static bool gm4_plan(const uint8_t* W, long ws, int M, int K, GM4Plan* p) {
+    const int nb = K / GTN_QBLK;
+    if (M < 2 || K % GTN_QBLK || nb % 4 || nb == 0 || nb / 4 > GV3_THREADS) return false;
+    if ((reinterpret_cast<uintptr_t>(W) & 15) || (ws & 15)) return false;
+    const int R = std::min(GV3_THREADS / (nb / 4), 64);
+    for (int occ = 2; occ >= 1; --occ) {
+        const size_t lim = occ == 2 ? (size_t)110 * 1024 : (size_t)200 * 1024;
+        for (int tiles = 1;; tiles *= 2) {
+            const int mt = (M + tiles - 1) / tiles;
+            for (int mc = std::min(mt, std::max(1, GV3_THREADS / (R * 4))); mc >= 1; --mc)
+                if (gm4_smem<WDT>(R, mt, mc, K) <= lim) {
+                    *p = GM4Plan{R, mt, mc, occ};
+                    return true;
+                }
+            if (mt == 1) break;
+        }
+    }
+    return false;
+}
+
+template <int WDT>
+static cudaError_t launch_gm4(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y,
+                              long ldy, const GM4Plan& p, cudaStream_t st, bool dry = false) {
+    // the model shapes' 4-block groups per row (K = 2048, 2304, 5632, 5760) at compile time
+    const int nbg = K / (4 * GTN_QBLK);
+    auto kern = nbg == 16 ? k_gemm4<WDT, 16> : nbg == 18 ? k_gemm4<WDT, 18> : nbg == 44 ? k_gemm4<WDT, 44>
+              : nbg == 45 ? k_gemm4<WDT, 45> : k_gemm4<WDT, 0>;
+    const size_t smem = gm4_smem<WDT>(p.R, p.MT, p.MC, K);
+    const cudaError_t e = ensure_smem(kern, smem);
+    if (e != cudaSuccess || dry) return e;
+    const int ngroups = (N + p.R - 1) / p.R, mtiles = (M + p.MT - 1) / p.MT;
+    const int gx = std::max(1, std::min(ngroups, sm_count() * p.occ / mtiles));
+    return launch_pdl(kern, dim3(gx, mtiles), dim3(GV3_THREADS), smem, st, W, ws, N, K, X, xs, M, Y, ldy, p.R, p.MT,
+                      p.MC, device_error_word());
+}
+
+// The CUDA-core GEMM for M >= 2 rows: k_gemm4 where its plan fits, else k_gemm3.
+template <int WDT>
+static bool cc_gemm_fits(const uint8_t* W, long ws, int M, int K) {
+    GM4Plan p4{};
+    GM3Plan p3{};
+    return gm4_plan<WDT>(W, ws, M, K, &p4) || gm3_plan<WDT>(W, ws, M, K, &p3);
+}
+template <int WDT>
+static cudaError_t cc_gemm(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y,
+                           long ldy, cudaStream_t st, bool dry) {
+    GM4Plan p4{};
+    if (gm4_plan<WDT>(W, ws, M, K, &p4)) return launch_gm4<WDT>(X, xs, M, W, ws, N, K, Y, ldy, p4, st, dry);
+    GM3Plan p3{};
+    if (gm3_plan<WDT>(W, ws, M, K, &p3)) return launch_gm3<WDT>(X, xs, M, W, ws, N, K, Y, ldy, p3, st, dry);
+    return cudaErrorInvalidValue;
 }
 
 // ---- tensor-core GEMM (k_gemm_tc) -----------------------------------------------------------
@@ -388,9 +446,8 @@ static cudaError_t launch_tc(const uint8_t* X, long xs, int M, const uint8_t* W,
 
 bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K, const TcScratch& tc) {
     if (tc_fits(W, ws, M, wdt, K, tc)) return true;
-    GM3Plan gp{};
-    if (wdt == GTN_Q8) return gm3_plan<GTN_Q8>(W, ws, M, K, &gp);
-    if (wdt == GTN_Q4) return gm3_plan<GTN_Q4>(W, ws, M, K, &gp);
+    if (wdt == GTN_Q8) return cc_gemm_fits<GTN_Q8>(W, ws, M, K);
+    if (wdt == GTN_Q4) return cc_gemm_fits<GTN_Q4>(W, ws, M, K);
     return false;
 }
 
@@ -399,11 +456,8 @@ cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, 
     if (tc_fits(W, ws, M, wdt, K, tc))
         return wdt == GTN_Q8 ? launch_tc<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, tc, st, dry)
                              : launch_tc<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, tc, st, dry);
-    GM3Plan gp{};
-    if (wdt == GTN_Q8 && gm3_plan<GTN_Q8>(W, ws, M, K, &gp))
-        return launch_gm3<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, gp, st, dry);
-    if (wdt == GTN_Q4 && gm3_plan<GTN_Q4>(W, ws, M, K, &gp))
-        return launch_gm3<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, gp, st, dry);
+    if (wdt == GTN_Q8) return cc_gemm<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, st, dry);
+    if (wdt == GTN_Q4) return cc_gemm<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, st, dry);
     return cudaErrorInvalidValue;
 }
 
@@ -435,9 +489,8 @@ static cudaError_t matmul_tma(const uint8_t* X, long xs, int M, const uint8_t* W
                               float* Y, long ldy, cudaStream_t st, const TcScratch& tc) {
     if (gemv_q_fits(M, wdt, K)) return gemv_q(X, xs, M, W, ws, wdt, N, K, Y, ldy, st, false);
     if (tc_fits(W, ws, M, wdt, K, tc)) return gemm_q(X, xs, M, W, ws, wdt, N, K, Y, ldy, st, false, tc);
-    GM3Plan gp{};
-    if (wdt == GTN_Q8 && gm3_plan<GTN_Q8>(W, ws, M, K, &gp)) return launch_gm3<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, gp, st);
-    if (wdt == GTN_Q4 && gm3_plan<GTN_Q4>(W, ws, M, K, &gp)) return launch_gm3<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, gp, st);
+    if (wdt == GTN_Q8 && cc_gemm_fits<GTN_Q8>(W, ws, M, K)) return cc_gemm<GTN_Q8>(X, xs, M, W, ws, N, K, Y, ldy, st, false);
+    if (wdt == GTN_Q4 && cc_gemm_fits<GTN_Q4>(W, ws, M, K)) return cc_gemm<GTN_Q4>(X, xs, M, W, ws, N, K, Y, ldy, st, false);
     const int mt = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
     if (wdt == GTN_F16) return gemm_f16(X, xs, M, W, ws, N, K, Y, ldy, st, false);
     int nw = 4;

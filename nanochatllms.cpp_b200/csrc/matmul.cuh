@@ -1044,6 +1044,213 @@ __global__ void __launch_bounds__(GV3_THREADS, 2) k_gemm3(const uint8_t* __restr
     asm volatile("griddepcontrol.launch_dependents;");
 }
 
+// ---- persistent exact GEMM for a few activation rows (batched decode steps) -----------------------
+// The arithmetic and order of k_gemm3 (and k_gemv3) for M >= 2 rows, arranged so that the weight
+// stream overlaps the arithmetic: a CTA prepares the lane words of its MT-row activation tile once
+// (k_gemm3's conflict-free layout) and then walks groups of R weight rows (one thread per (row,
+// 4-block group)) persistently. Per group it waits for the group's TMA bulk copies, moves its
+// weight lane words into registers, releases the single stage and at once issues the copies of
+// its next group, which land while this group computes: per chunk of MC activation rows, phase 1
+// writes the 16 products of each (activation row, thread) as four float4 and phase 2 runs the
+// MC * R * 4 lane chains in block order and the (L0 + L1) + (L2 + L3) combine.
+// Per product: two dp4a accumulating onto the bias 0x4B400000 (so the int32 lane sum L arrives as
+// the fp32 bit pattern of 1.5 * 2^23 + L, exact for |L| < 2^22), one subtraction of 1.5 * 2^23 (the
+// exact fp32 value of L) and the multiply by fp32(da) * fp32(dw); the activation lane words of
+// two lanes come in one 16-byte shared load ([row][block k][lane pair][group j] layout, threads of
+// consecutive groups read consecutive 16 bytes). NBG > 0 fixes K / 128 (the 4-block groups per
+// row) at compile time, so that every shared-memory offset is an immediate; NBG = 0 reads it from K.
+// grid (persistent over the groups, ceil(M / MT)); block 256; two CTAs per SM when shared memory
+// allows. W rows 16-byte aligned (rstride-byte copies).
+struct GM4Plan {
+    int R, MT, MC, occ;
+};
+template <int WDT>
+__host__ __device__ inline size_t gm4_prep_bytes(int MT, int nb) {
+    return ((size_t)MT * nb * (4 * 8 + 4 + (WDT == GTN_Q4 ? 16 : 0)) + 15) & ~(size_t)15;
+}
+template <int WDT>
+__host__ __device__ inline size_t gm4_smem(int R, int MT, int MC, int K) {
+    const int nb = K / GTN_QBLK;
+    return 128 + (size_t)R * gv3_rstride<WDT>(K) + gm4_prep_bytes<WDT>(MT, nb) +
+           (size_t)MC * R * 4 * gv3_pstr(nb) * sizeof(float);
+}
+
+template <int WDT, int NBG>
+__global__ void __launch_bounds__(GV3_THREADS, 2) k_gemm4(const uint8_t* __restrict__ W, long w_stride, int N, int K,
+                                                         const uint8_t* __restrict__ X, long x_stride, int M,
+                                                         float* __restrict__ Y, long y_stride, int R, int MT, int MC,
+                                                         unsigned int* err) {
+    using C = MMCfg<WDT>;
+    constexpr int GB = 4 * C::BLK_BYTES, GW = GB / 4;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int abort_flag;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+    const int nbg = NBG > 0 ? NBG : K / (4 * GTN_QBLK), nb = 4 * nbg;
+    const int rstride = gv3_rstride<WDT>(K), pstr = gv3_pstr(nb);
+    uint8_t* stage = smem + 128;
+    int4* pa = reinterpret_cast<int4*>(stage + (size_t)R * rstride);  // [MT][4 k][2 lane pairs][nbg]
+    float* pda = reinterpret_cast<float*>(pa + (size_t)MT * nb * 2);  // [MT][4 k][nbg]
+    int* ps = reinterpret_cast<int*>(pda + (size_t)MT * nb);          // Q4: lane sums [MT][4 k][4 l][nbg]
+    float* prod = reinterpret_cast<float*>(stage + (size_t)R * rstride + gm4_prep_bytes<WDT>(MT, nb));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int j = tid % nbg, rs = tid / nbg;
+    const int m0 = blockIdx.y * MT, mt = min(MT, M - m0);
+    const int ngroups = (N + R - 1) / R;
+    int nissued = 0;  // copies issued into the stage (warp 0)
+    auto issue = [&](int g) {  // warp 0: the rows of group g into the stage
+        const int r0 = g * R, nr = min(R, N - r0);
+        if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)rstride * (uint32_t)nr);
+        __syncwarp();
+        for (int r = lane; r < nr; r += 32)
+            bulk_g2s(stage + (size_t)r * rstride, W + (size_t)(r0 + r) * w_stride, (uint32_t)rstride, bar);
+    };
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+    if (warp == 0 && (int)blockIdx.x < ngroups) {  // weights do not depend on the previous kernel
+        issue(blockIdx.x);
+        ++nissued;
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // the tile's activation lane words; the raw rows are first copied with coalesced 4-byte loads
+    // into the (not yet used) product buffer when they fit there and are word aligned
+    const int xrow = nb * GTN_Q8_BYTES;
+    const bool stage_x = (size_t)mt * xrow <= (size_t)MC * R * 4 * pstr * sizeof(float) &&
+                         ((reinterpret_cast<uintptr_t>(X) | (uintptr_t)x_stride | (uintptr_t)xrow) & 3) == 0;
+    const uint8_t* xsrc = X + (long)m0 * x_stride;
+    long xss = x_stride;
+    if (stage_x) {
+        const int wpr = xrow / 4;
+        uint32_t* xd = reinterpret_cast<uint32_t*>(prod);
+        for (int i = tid; i < mt * wpr; i += GV3_THREADS) {
+            const int m = i / wpr, w = i - m * wpr;
+            xd[i] = reinterpret_cast<const uint32_t*>(xsrc + (long)m * x_stride)[w];
+        }
+        __syncthreads();
+        xsrc = reinterpret_cast<const uint8_t*>(prod);
+        xss = xrow;
+    }
+    for (int i = tid; i < mt * nb * 4; i += GV3_THREADS) {
+        const int l = i & 3, b = (i >> 2) % nb, m = (i >> 2) / nb;
+        const uint8_t* blk = xsrc + (long)m * xss + (long)b * GTN_Q8_BYTES;
+        const uint8_t* q = blk + 2;
+        const int w0 = (int)ld_u16(q + 2 * l) | ((int)ld_u16(q + 8 + 2 * l) << 16);
+        const int w1 = (int)ld_u16(q + 16 + 2 * l) | ((int)ld_u16(q + 24 + 2 * l) << 16);
+        const int jj = b >> 2, k = b & 3;
+        int* pw = reinterpret_cast<int*>(pa + ((size_t)(m * 4 + k) * 2 + (l >> 1)) * nbg + jj) + 2 * (l & 1);
+        pw[0] = w0;
+        pw[1] = w1;
+        if (WDT == GTN_Q4) ps[((size_t)(m * 4 + k) * 4 + l) * nbg + jj] = dp4a(w0, 0x01010101, dp4a(w1, 0x01010101, 0));
+        if (l == 0) pda[(size_t)(m * 4 + k) * nbg + jj] = h2f(ld_u16(blk));
+    }
+    __syncthreads();  // prepared lane words in place; the staged rows in the product buffer are done
+    const int nch = R * 4;  // chains per activation row
+    int it = 0;
+    for (int g = blockIdx.x; g < ngroups; g += gridDim.x, ++it) {
+        const int r0 = g * R, nr = min(R, N - r0);
+        const bool p1 = rs < nr;  // rs < R for every thread below R * nbg
+        if (!abort_flag && !mbar_wait_bounded(bar, (uint32_t)it & 1u, err)) abort_flag = 1;
+        __syncthreads();
+        if (abort_flag) break;
+        float dw[4];
+        int wl0[16], wl1[16];  // weight lane words per (block, lane)
+        {
+            uint32_t w[GW];
+            if (p1) {
+                const uint2* src = reinterpret_cast<const uint2*>(stage + (size_t)rs * rstride + (size_t)j * GB);
+#pragma unroll
+                for (int q = 0; q < GW / 2; ++q) {
+                    const uint2 t = src[q];
+                    w[2 * q] = t.x;
+                    w[2 * q + 1] = t.y;
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int ob = k * C::BLK_BYTES;
+                dw[k] = p1 ? h2f((uint16_t)gv3_u16(w, ob)) : 0.0f;
+#pragma unroll
+                for (int l = 0; l < 4; ++l) {
+                    if (WDT == GTN_Q8) {
+                        wl0[k * 4 + l] = p1 ? gv3_pair(w, ob + 2 + 2 * l, ob + 10 + 2 * l) : 0;
+                        wl1[k * 4 + l] = p1 ? gv3_pair(w, ob + 18 + 2 * l, ob + 26 + 2 * l) : 0;
+                    } else {
+                        const int wb = p1 ? gv3_pair(w, ob + 2 + 2 * l, ob + 10 + 2 * l) : 0;
+                        wl0[k * 4 + l] = (wb >> 4) & 0x0f0f0f0f;
+                        wl1[k * 4 + l] = wb & 0x0f0f0f0f;
+                    }
+                }
+            }
+        }
+        __syncthreads();  // the stage is free: the next group's copies land while this one computes
+        if (warp == 0 && g + (int)gridDim.x < ngroups) {
+            issue(g + gridDim.x);
+            ++nissued;
+        }
+        for (int c0 = 0; c0 < mt; c0 += MC) {
+            const int mc = min(MC, mt - c0);
+            if (p1) {
+                for (int mm = 0; mm < mc; ++mm) {
+                    const int m = c0 + mm;
+                    const int4* pam = pa + (size_t)m * 8 * nbg + j;
+                    const float* pdm = pda + (size_t)m * 4 * nbg + j;
+                    float o[4][4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float sc = pdm[k * nbg] * dw[k];
+#pragma unroll
+                        for (int lp = 0; lp < 2; ++lp) {
+                            const int4 av = pam[(k * 2 + lp) * nbg];  // lanes 2 lp and 2 lp + 1
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const int l = 2 * lp + h;
+                                int Lb = dp4a(wl0[k * 4 + l], h ? av.z : av.x,
+                                              dp4a(wl1[k * 4 + l], h ? av.w : av.y, 0x4B400000));
+                                if (WDT == GTN_Q4) Lb -= 7 * ps[((size_t)(m * 4 + k) * 4 + l) * nbg + j];
+                                o[l][k] = (__int_as_float(Lb) - 12582912.0f) * sc;
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int l = 0; l < 4; ++l)
+                        *reinterpret_cast<float4*>(prod + ((size_t)(mm * R + rs) * 4 + l) * pstr + 4 * j) =
+                            make_float4(o[l][0], o[l][1], o[l][2], o[l][3]);
+                }
+            }
+            __syncthreads();
+            for (int cb = 0; cb < mc * nch; cb += GV3_THREADS) {  // whole warps: the combine shuffles
+                const int c = cb + tid;
+                const int mm = c / nch, rl = c - mm * nch, r = rl >> 2;
+                const bool valid = c < mc * nch && r < nr;
+                float acc = 0.0f;
+                if (valid) {
+                    const float4* pp = reinterpret_cast<const float4*>(prod + (size_t)c * pstr);
+                    for (int b4 = 0; b4 < nbg; ++b4) {
+                        const float4 v = pp[b4];
+                        acc = acc + v.x;
+                        acc = acc + v.y;
+                        acc = acc + v.z;
+                        acc = acc + v.w;
+                    }
+                }
+                const float t01 = acc + __shfl_xor_sync(0xffffffffu, acc, 1);
+                const float t = t01 + __shfl_xor_sync(0xffffffffu, t01, 2);
+                if (valid && (c & 3) == 0) Y[(long)(m0 + c0 + mm) * y_stride + r0 + r] = t;
+            }
+            __syncthreads();  // the products are rewritten by the next chunk
+        }
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (abort_flag && tid == 0 && nissued > 0) {
+        // bounded wait for the last copy issued into the stage (phase nissued - 1)
+        for (uint32_t i = 0; i < GTN_WAIT_LIMIT; ++i)
+            if (mbar_try_wait(bar, (uint32_t)(nissued - 1) & 1u)) break;
+    }
+}
+
 // Plain-load variant for rows whose TMA tiles could reach outside the caller's weight buffer (an
 // unaligned base, or a last row that does not end on a 16-byte boundary). One warp per
 // (row, activation row): lanes 0..3 (Q8/Q4) or 0..7 (fp16) run the reference's lane chains with
