@@ -44,7 +44,9 @@ __device__ __forceinline__ uint16_t ld_u16(const uint8_t* p) { return *reinterpr
 // with FMA (the variant its loader selects on them) forms r = x * (N / ln 2) - k with one fused
 // multiply-add, so r does so here. Against the host's expf this is bit-identical on all 2^32 float
 // inputs (checked exhaustively); a correctly rounded exp differs from glibc's on 170,648 of them.
-__constant__ static unsigned long long k_expf_tab[32] = {
+// The table sits in global memory and is read through the read-only cache: the threads of a warp
+// index it with different k, which the constant cache would serve one address at a time.
+__device__ static const unsigned long long k_expf_tab[32] = {
     0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
     0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
     0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
@@ -69,7 +71,7 @@ __device__ __forceinline__ float expf_ref(float x) {
     const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
     kd = __dsub_rn(kd, shift);
     const double r = __fma_rn(inv_ln2n, xd, -kd);
-    const double s = __longlong_as_double((long long)(k_expf_tab[ki & 31u] + (ki << 47)));
+    const double s = __longlong_as_double((long long)(__ldg(&k_expf_tab[ki & 31u]) + (ki << 47)));
     const double c0 = 0x1.c6af84b912394p-20, c1 = 0x1.ebfce50fac4f3p-13, c2 = 0x1.62e42ff0c52d6p-6;
     const double p = __dadd_rn(__dmul_rn(c0, r), c1);
     const double r2 = __dmul_rn(r, r);

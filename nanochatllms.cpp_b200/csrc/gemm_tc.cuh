@@ -1,4 +1,4 @@
-// Exact Q8/Q4 GEMM on the 5th-generation tensor cores (tcgen05) for M >= 24 activation rows:
+// Exact Q8/Q4 GEMM on the 5th-generation tensor cores (tcgen05) for M >= 16 activation rows:
 // prefill and batched decode steps.
 //
 // Reference: ops.cpp:292-490 (vec_dot_product_q8, vec_dot_product_q8_q4) inside matmul_2d_impl

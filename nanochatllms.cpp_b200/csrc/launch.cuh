@@ -134,9 +134,11 @@ cudaError_t gemm_f16(const uint8_t* X, long xs, int M, const uint8_t* W, long ws
 // rows, same `padded` precondition): the tensor-core kernel k_gemm_tc from TC_MIN_M rows on when
 // `tc` scratch is given, else the persistent CUDA-core kernel k_gemm4 (k_gemm3 where its plan does
 // not fit); `dry` only configures shared memory and prepares the weight tensor map (so that a later
-// launch can be captured into a CUDA graph). Below 24 rows k_gemm4 is the faster of the two on the
-// model shapes (M = 16: 0.65-0.88x the tensor-core kernel's time), from 32 rows the tensor cores.
-constexpr int TC_MIN_M = 24;
+// launch can be captured into a CUDA graph). From 16 rows the tensor-core kernel: in isolation
+// k_gemm4 is faster on TinyLlama's shapes at 16 rows, but the graph-replayed decode steps of 16
+// sequences are faster on the tensor cores (MiniCPM-2B Q8 7.3 ms vs 8.5 ms, TinyLlama Q8 and
+// StableLM-2 Q4 by 1 % and 9 %).
+constexpr int TC_MIN_M = 16;
 bool gemm_q_fits(const uint8_t* W, long ws, int M, int wdt, int K, const TcScratch& tc = TcScratch());
 cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int wdt, int N, int K, float* Y,
                    long ldy, cudaStream_t st, bool dry, const TcScratch& tc = TcScratch());

@@ -23,7 +23,7 @@ def dev_out(nbytes, device, fill=None):
 @pytest.mark.parametrize("wdt", [Q8, Q4, F16])
 @pytest.mark.parametrize("M,K,N", [(1, 2048, 256), (1, 2048, 2048), (1, 5632, 2048), (3, 256, 96), (16, 2048, 64),
                                    (9, 5760, 64), (64, 2304, 96), (1, 2048, 32003), (1, 2048, 40),
-                                   # tensor-core GEMM (M >= 24; M = 16 runs k_gemm4): partial row / column tiles, one raw
+                                   # tensor-core GEMM (M >= 16): partial row / column tiles, one raw
                                    # chunk, ring wrap-around (K = 5632: 22 chunks); 32-row weight
                                    # tiles for small grids, 64-row tiles from one CTA per SM on
                                    # (9632 rows: 151 tiles, the last one half full)
