@@ -267,21 +267,38 @@ def gemm_sweep(G, torch, wdt: int, device, M: int, only: str | None = None):
 
         def cc(i):
             rc = G.lib().gtn_matmul_2d_noalloc(C.byref(X.desc()), C.byref(G.GT(ws[i % ncopy], wdt, (N, K)).desc()),
-                                               C.byref(Y.desc()), 0, C.c_void_p(stream.cuda_stream))
+                                               C.byref(Y.desc()), 0,
+                                               C.c_void_p(torch.cuda.current_stream().cuda_stream))
             assert rc == 0, G.lib().gtn_last_error()
 
-        res = {"N": N, "K": K, "M": M}
+        res = {"N": N, "K": K, "M": M, "timing": "graph"}
         for key, fn in ((("k_gemm_f16", tc),) if wdt == 1 else (("tc", tc), ("cuda_cores", cc))):
             for i in range(3):
                 fn(i)
             reps = 2 * ncopy
             torch.cuda.synchronize()
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            ev0.record(stream)
-            for i in range(reps):
-                fn(i)
-            ev1.record(stream)
-            torch.cuda.synchronize()
+            try:
+                # the calls replayed from one CUDA graph: device time only, no host work between launches
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for i in range(reps):
+                        fn(i)
+                graph.replay()
+                torch.cuda.synchronize()
+                ev0.record(stream)
+                graph.replay()
+                ev1.record(stream)
+                torch.cuda.synchronize()
+                del graph
+            except Exception:  # not capturable: back-to-back calls (host work can show in the time)
+                res["timing"] = "loop"
+                torch.cuda.synchronize()
+                ev0.record(stream)
+                for i in range(reps):
+                    fn(i)
+                ev1.record(stream)
+                torch.cuda.synchronize()
             t = ev0.elapsed_time(ev1) / reps * 1e-3
             if wdt == 1:  # products: one fused multiply-add each on 128 lanes per SM
                 macs = M * N * K

@@ -422,11 +422,8 @@ static cudaError_t launch_tc_nt(const uint8_t* X, long xs, int M, const uint8_t*
         const int mm = std::min(cap, M - r0), tiles = (mm + TC_MT - 1) / TC_MT;
         e = launch_pdl(k_tc_expand, dim3(nb, tiles), dim3(128), 0, st, X + (long)r0 * xs, xs, mm, K, tc.p);
         if (e != cudaSuccess) return e;
-        // persistent: at most one CTA per SM, each walking its share of the weight x row tiles
-        const long all_tiles = (long)((N + NT - 1) / NT) * tiles;
-        const int grid = (int)std::min<long>(all_tiles, sm_count());
-        e = launch_pdl(k_gemm_tc<WDT, NT>, dim3(grid), dim3(TcTile<NT>::THREADS), smem, st, map, N, K,
-                       (const uint8_t*)tc.p, mm, Y + (long)r0 * ldy, ldy, device_error_word());
+        e = launch_pdl(k_gemm_tc<WDT, NT>, dim3((N + NT - 1) / NT, tiles), dim3(TcTile<NT>::THREADS), smem, st, map,
+                       N, K, (const uint8_t*)tc.p, mm, Y + (long)r0 * ldy, ldy, device_error_word());
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

@@ -76,12 +76,13 @@ __host__ __device__ constexpr int tc_rstride() {  // raw chunk row: 8 blocks (27
     return TC_KB * (WDT == GTN_Q8 ? GTN_Q8_BYTES : GTN_Q4_BYTES);
 }
 template <int WDT, int NT>
-__host__ __device__ constexpr size_t tc_smem() {  // + the epilogue's combine buffer [4][TC_MT][TC_COMB_STRIDE]
+__host__ __device__ constexpr size_t tc_smem() {
     return 1024 + (size_t)TcTile<NT>::S * TC_G * (TC_AIMG + TcTile<NT>::BTILE) +
-           (size_t)TC_RS * NT * tc_rstride<WDT>() + (size_t)TcTile<NT>::S * TC_G * NT * sizeof(float) +
-           (size_t)4 * TC_MT * TC_COMB_STRIDE * sizeof(float) + 64;
+           (size_t)TC_RS * NT * tc_rstride<WDT>() + (size_t)TcTile<NT>::S * TC_G * NT * sizeof(float) + 64;
 }
 static_assert(tc_rstride<GTN_Q8>() % 16 == 0 && tc_rstride<GTN_Q4>() % 16 == 0, "TMA boxes are 16-byte rows");
+static_assert((size_t)4 * TC_MT * TC_COMB_STRIDE * sizeof(float) <= (size_t)2 * TC_G * TC_AIMG,
+              "the combine buffer reuses the activation tiles");
 static_assert(tc_smem<GTN_Q8, 32>() <= 227 * 1024 && tc_smem<GTN_Q8, 64>() <= 227 * 1024, "shared memory");
 static_assert(TC_KB % TC_G == 0, "groups never straddle raw chunks");
 
@@ -213,24 +214,18 @@ static __global__ void __launch_bounds__(128) k_tc_expand(const uint8_t* __restr
 // weights, bit-identical to the reference. `img`: k_tc_expand's image of X (M rows). `wmap`: the
 // weight matrix as a 2-D uint16 tensor (inner extent w_stride / 2, N rows, row stride w_stride),
 // box (tc_rstride / 2, NT); rows past N read as zeros. K / 32 a multiple of TC_G.
-// Persistent: grid min(tiles, SMs), one CTA per SM (it holds all of TMEM). CTA c takes tiles
-// c, c + gridDim.x, ... of the ceil(N / NT) x ceil(M / 32) tiles, row tile fastest (the row tiles
-// of one weight tile run at the same time and share it through L2). Block TcTile<NT>::THREADS,
-// dynamic shared memory tc_smem<WDT, NT>().
+// grid (ceil(N / NT), ceil(M / 32)), block TcTile<NT>::THREADS, dynamic shared memory tc_smem<WDT, NT>();
+// one CTA per SM (it holds all of TMEM).
 //
-// Roles, synchronised only by mbarriers (no block-wide barrier inside the main loop). Each role
-// counts the groups (the producer also the raw chunks) of all its tiles in one sequence, so ring
-// stages, TMEM slots and mbarrier phases run on across tiles:
-//   producer warp: weight chunks (raw_full / raw_empty ring) and the A' images of group G into
-//     slot s = G % T::S once the epilogue released the slot (tmem_empty of group G - T::S);
+// Roles, synchronised only by mbarriers (no block-wide barrier inside the main loop):
+//   producer warp: weight chunks (raw_full / raw_empty ring) and the A' images of group g into
+//     slot s = g % T::S once the epilogue released the slot (tmem_empty of group g - T::S);
 //   converter warps: wait for the slot and the raw chunk, write the weight tile and scales, arrive
 //     on b_full[s] (and on raw_empty once a chunk's last group is converted);
 //   MMA warp: waits for b_full[s] and a_full[s], issues the group's MMAs into TMEM slot s and
 //     commits them to mma_done[s];
 //   epilogue warps: wait mma_done[s], read the lane sums from TMEM, run the fp32 chains, release
-//     slot s (tmem_empty[s], 256 arrivals); after a tile's last group they meet (a named barrier of
-//     the epilogue warps only) to form (L0 + L1) + (L2 + L3) in their own combine buffer and store
-//     the tile, while the other roles already work on the next tile.
+//     slot s (tmem_empty[s], 256 arrivals).
 template <int WDT, int NT>
 __global__ void __launch_bounds__(TcTile<NT>::THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap wmap, int N, int K,
                                                            const uint8_t* __restrict__ img, int M,
@@ -252,16 +247,12 @@ __global__ void __launch_bounds__(TcTile<NT>::THREADS, 1) k_gemm_tc(const __grid
     uint8_t* btile = atile + T::S * TC_G * TC_AIMG;           // [T::S * TC_G][T::BTILE]
     uint8_t* raw = btile + T::S * TC_G * T::BTILE;            // [TC_RS][NT][RSTR]
     float* dw_s = reinterpret_cast<float*>(raw + (size_t)TC_RS * NT * RSTR);  // [T::S][TC_G][NT]
-    float* comb = dw_s + T::S * TC_G * NT;                    // [4][TC_MT][TC_COMB_STRIDE] (epilogue)
+    float* comb = reinterpret_cast<float*>(atile);  // [4][TC_MT][TC_COMB_STRIDE], after the last MMA
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int ntm = (M + TC_MT - 1) / TC_MT, ntiles = ((N + NT - 1) / NT) * ntm;
-    const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int n0 = blockIdx.x * NT, nr = min(NT, N - n0);
+    const int m0 = blockIdx.y * TC_MT, mr = min(TC_MT, M - m0);
     const int nb = K / GTN_QBLK, ngroups = nb / TC_G, nchunks = (nb + TC_KB - 1) / TC_KB;
-    const int total_groups = my_tiles * ngroups, total_chunks = my_tiles * nchunks;
-    // this CTA's tile i: first weight row, activation row tile
-    auto tile_n0 = [&](int i) { return (((int)blockIdx.x + i * (int)gridDim.x) / ntm) * NT; };
-    auto tile_mt = [&](int i) { return ((int)blockIdx.x + i * (int)gridDim.x) % ntm; };
     constexpr int CW0 = TC_EPI_WARPS;  // first converter warp
 
     if (warp == 0) {
@@ -289,41 +280,41 @@ __global__ void __launch_bounds__(TcTile<NT>::THREADS, 1) k_gemm_tc(const __grid
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    float acc[T::COLS];
+#pragma unroll
+    for (int j = 0; j < T::COLS; ++j) acc[j] = 0.0f;
     int g_issued = 0;                // MMA warp: groups whose MMAs were issued
     int a_issued = 0, w_issued = 0;  // producer: groups of A' images and weight chunks issued
 
     if (warp == T::PROD_WARP) {
         // ---- producer (one thread) ----
         if (lane == 0) {
-            for (int c = 0; c < min(TC_RS, total_chunks); ++c) {  // weights: independent of the previous kernel
+            for (int c = 0; c < min(TC_RS, nchunks); ++c) {  // weights: independent of the previous kernel
                 mbar_arrive_expect_tx(&raw_full[c], CHUNK_BYTES);
-                tma_load_2d(raw + (size_t)c * NT * RSTR, &wmap, (c % nchunks) * (RSTR / 2), tile_n0(c / nchunks),
-                            &raw_full[c]);
+                tma_load_2d(raw + (size_t)c * NT * RSTR, &wmap, c * (RSTR / 2), n0, &raw_full[c]);
             }
-            w_issued = min(TC_RS, total_chunks);
+            w_issued = min(TC_RS, nchunks);
             asm volatile("griddepcontrol.wait;" ::: "memory");  // the A' image comes from the pre-pass
+            const uint8_t* aimg = img + (size_t)blockIdx.y * nb * TC_AIMG;
             uint64_t t0 = globaltimer_ns();
-            while (a_issued < total_groups || w_issued < total_chunks) {
+            while (a_issued < ngroups || w_issued < nchunks) {
                 bool progressed = false;
-                if (a_issued < total_groups) {
-                    const int G = a_issued, s = G % T::S;
-                    if (G < T::S || mbar_test(&tmem_empty[s], (uint32_t)(G / T::S - 1) & 1u)) {
-                        const uint8_t* aimg =
-                            img + ((size_t)tile_mt(G / ngroups) * nb + (size_t)(G % ngroups) * TC_G) * TC_AIMG;
+                if (a_issued < ngroups) {
+                    const int g = a_issued, s = g % T::S;
+                    if (g < T::S || mbar_test(&tmem_empty[s], (uint32_t)(g / T::S - 1) & 1u)) {
                         mbar_arrive_expect_tx(&a_full[s], (uint32_t)(TC_G * TC_AIMG));
                         for (int blk = 0; blk < TC_G; ++blk)
-                            bulk_g2s(atile + (size_t)(s * TC_G + blk) * TC_AIMG, aimg + (size_t)blk * TC_AIMG,
-                                     (uint32_t)TC_AIMG, &a_full[s]);
+                            bulk_g2s(atile + (size_t)(s * TC_G + blk) * TC_AIMG,
+                                     aimg + (size_t)(g * TC_G + blk) * TC_AIMG, (uint32_t)TC_AIMG, &a_full[s]);
                         ++a_issued;
                         progressed = true;
                     }
                 }
-                if (w_issued < total_chunks) {
+                if (w_issued < nchunks) {
                     const int c = w_issued, st = c % TC_RS;
                     if (mbar_test(&raw_empty[st], (uint32_t)(c / TC_RS - 1) & 1u)) {
                         mbar_arrive_expect_tx(&raw_full[st], CHUNK_BYTES);
-                        tma_load_2d(raw + (size_t)st * NT * RSTR, &wmap, (c % nchunks) * (RSTR / 2),
-                                    tile_n0(c / nchunks), &raw_full[st]);
+                        tma_load_2d(raw + (size_t)st * NT * RSTR, &wmap, c * (RSTR / 2), n0, &raw_full[st]);
                         ++w_issued;
                         progressed = true;
                     }
@@ -346,11 +337,10 @@ __global__ void __launch_bounds__(TcTile<NT>::THREADS, 1) k_gemm_tc(const __grid
         // blocks) and written as the four 16-byte K-chunk rows of the fp16 tile ----
         const int ct = tid - 32 * CW0;
         const int blk = ct / NT, n = ct % NT;
-        for (int G = 0; G < total_groups; ++G) {
-            const int s = G % T::S, g = G % ngroups;
-            const int chunk = (G / ngroups) * nchunks + (g * TC_G) / TC_KB, stage = chunk % TC_RS;
+        for (int g = 0; g < ngroups; ++g) {
+            const int s = g % T::S, chunk = (g * TC_G) / TC_KB, stage = chunk % TC_RS;
             bool ok = *abort_flag == 0;
-            if (ok && G >= T::S) ok = tc_wait(&tmem_empty[s], (uint32_t)(G / T::S - 1) & 1u, err);
+            if (ok && g >= T::S) ok = tc_wait(&tmem_empty[s], (uint32_t)(g / T::S - 1) & 1u, err);
             if (ok) ok = tc_wait(&raw_full[stage], (uint32_t)(chunk / TC_RS) & 1u, err);
             if (ok) {
                 const int boff = ((g * TC_G + blk) % TC_KB) * BB;  // block offset in the raw row
@@ -399,9 +389,9 @@ __global__ void __launch_bounds__(TcTile<NT>::THREADS, 1) k_gemm_tc(const __grid
     } else if (warp == T::MMA_WARP) {
         // ---- MMA issue (one thread) ----
         if (lane == 0) {
-            for (int G = 0; G < total_groups; ++G) {
-                const int s = G % T::S;
-                const uint32_t ph = (uint32_t)(G / T::S) & 1u;
+            for (int g = 0; g < ngroups; ++g) {
+                const int s = g % T::S;
+                const uint32_t ph = (uint32_t)(g / T::S) & 1u;
                 if (*abort_flag != 0 || !tc_wait(&b_full[s], ph, err) || !tc_wait(&a_full[s], ph, err)) {
                     *abort_flag = 1;
                     break;
@@ -417,86 +407,72 @@ __global__ void __launch_bounds__(TcTile<NT>::THREADS, 1) k_gemm_tc(const __grid
                     tc_mma(d, tc_desc(a + 256, 128, 512), tc_desc(b + 256, 128, 512), T::IDESC, 1u);
                 }
                 tc_commit(&mma_done[s]);
-                g_issued = G + 1;
+                g_issued = g + 1;
             }
         }
         __syncwarp();
     } else {
         // ---- epilogue: thread (quarter q = reference lane l, column half, row m = lane) ----
         const int q = warp & 3, half = warp >> 2;
-        constexpr int CPB = T::COLS / 16, NCH = TC_G * CPB;
-        int G = 0;
-        for (int ti = 0; ti < my_tiles; ++ti) {
-            float acc[T::COLS];
-#pragma unroll
-            for (int j = 0; j < T::COLS; ++j) acc[j] = 0.0f;
-            for (int g = 0; g < ngroups; ++g, ++G) {
-                const int s = G % T::S;
-                if (*abort_flag != 0 || !tc_wait(&mma_done[s], (uint32_t)(G / T::S) & 1u, err)) {
-                    *abort_flag = 1;
-                    break;
-                }
-                tc_fence_after();
-                // 16-column chunks i = CPB * block + sub: the TMEM load of chunk i + 1 is in flight
-                // while chunk i is accumulated
-                const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s * TC_G * NT + half * T::COLS);
-                uint32_t va[16], vb[16];
-                tc_ld16(tq, va);
-                tc_wait_ld(va);
-#pragma unroll
-                for (int i = 0; i < NCH; ++i) {
-                    uint32_t(&cur)[16] = (i & 1) ? vb : va;
-                    uint32_t(&nxt)[16] = (i & 1) ? va : vb;
-                    if (i + 1 < NCH) tc_ld16(tq + (uint32_t)(((i + 1) / CPB) * NT + ((i + 1) % CPB) * 16), nxt);
-                    const int t = s * TC_G + i / CPB, sub = i % CPB;
-                    const float da = reinterpret_cast<const float*>(atile + (size_t)t * TC_AIMG + TC_ATILE)[lane];
-                    const float4* dw4 = reinterpret_cast<const float4*>(dw_s + t * NT + half * T::COLS + sub * 16);
-#pragma unroll
-                    for (int j4 = 0; j4 < 4; ++j4) {
-                        const float4 w = dw4[j4];
-                        const int j = sub * 16 + 4 * j4;
-                        const float s0 = da * w.x, s1 = da * w.y, s2 = da * w.z, s3 = da * w.w;
-                        const float p0 = __uint_as_float(cur[4 * j4]) * s0, p1 = __uint_as_float(cur[4 * j4 + 1]) * s1;
-                        const float p2 = __uint_as_float(cur[4 * j4 + 2]) * s2, p3 = __uint_as_float(cur[4 * j4 + 3]) * s3;
-                        acc[j] = acc[j] + p0;
-                        acc[j + 1] = acc[j + 1] + p1;
-                        acc[j + 2] = acc[j + 2] + p2;
-                        acc[j + 3] = acc[j + 3] + p3;
-                    }
-                    if (i + 1 < NCH) tc_wait_ld(nxt);
-                }
-                tc_fence_before();
-                mbar_arrive(&tmem_empty[s]);
+        for (int g = 0; g < ngroups; ++g) {
+            const int s = g % T::S;
+            if (*abort_flag != 0 || !tc_wait(&mma_done[s], (uint32_t)(g / T::S) & 1u, err)) {
+                *abort_flag = 1;
+                break;
             }
-            G = (ti + 1) * ngroups;  // an aborted tile leaves the count where the next tile starts
-            // (L0 + L1) + (L2 + L3): the four lane chains of each output meet in the combine buffer;
-            // every epilogue warp reaches both barriers of every tile, aborted or not
-            const bool ok = *abort_flag == 0;
-            if (ok) {
+            tc_fence_after();
+            // 16-column chunks i = CPB * block + sub: the TMEM load of chunk i + 1 is in flight while
+            // chunk i is accumulated
+            constexpr int CPB = T::COLS / 16, NCH = TC_G * CPB;
+            const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s * TC_G * NT + half * T::COLS);
+            uint32_t va[16], vb[16];
+            tc_ld16(tq, va);
+            tc_wait_ld(va);
 #pragma unroll
-                for (int j = 0; j < T::COLS; ++j)
-                    comb[(q * TC_MT + lane) * TC_COMB_STRIDE + half * T::COLS + j] = acc[j];
-            }
-            asm volatile("bar.sync 1, %0;" ::"r"(32 * TC_EPI_WARPS) : "memory");
-            if (ok) {
-                const int n0 = tile_n0(ti), m0 = tile_mt(ti) * TC_MT;
-                const int nr = min(NT, N - n0), mr = min(TC_MT, M - m0);
-                for (int i = tid; i < TC_MT * NT; i += 32 * TC_EPI_WARPS) {
-                    const int m = i / NT, n = i % NT;
-                    if (m < mr && n < nr) {
-                        const float c0 = comb[(0 * TC_MT + m) * TC_COMB_STRIDE + n];
-                        const float c1 = comb[(1 * TC_MT + m) * TC_COMB_STRIDE + n];
-                        const float c2 = comb[(2 * TC_MT + m) * TC_COMB_STRIDE + n];
-                        const float c3 = comb[(3 * TC_MT + m) * TC_COMB_STRIDE + n];
-                        Y[(long)(m0 + m) * y_stride + n0 + n] = (c0 + c1) + (c2 + c3);
-                    }
+            for (int i = 0; i < NCH; ++i) {
+                uint32_t(&cur)[16] = (i & 1) ? vb : va;
+                uint32_t(&nxt)[16] = (i & 1) ? va : vb;
+                if (i + 1 < NCH) tc_ld16(tq + (uint32_t)(((i + 1) / CPB) * NT + ((i + 1) % CPB) * 16), nxt);
+                const int t = s * TC_G + i / CPB, sub = i % CPB;
+                const float da = reinterpret_cast<const float*>(atile + (size_t)t * TC_AIMG + TC_ATILE)[lane];
+                const float4* dw4 = reinterpret_cast<const float4*>(dw_s + t * NT + half * T::COLS + sub * 16);
+#pragma unroll
+                for (int j4 = 0; j4 < 4; ++j4) {
+                    const float4 w = dw4[j4];
+                    const int j = sub * 16 + 4 * j4;
+                    const float s0 = da * w.x, s1 = da * w.y, s2 = da * w.z, s3 = da * w.w;
+                    const float p0 = __uint_as_float(cur[4 * j4]) * s0, p1 = __uint_as_float(cur[4 * j4 + 1]) * s1;
+                    const float p2 = __uint_as_float(cur[4 * j4 + 2]) * s2, p3 = __uint_as_float(cur[4 * j4 + 3]) * s3;
+                    acc[j] = acc[j] + p0;
+                    acc[j + 1] = acc[j + 1] + p1;
+                    acc[j + 2] = acc[j + 2] + p2;
+                    acc[j + 3] = acc[j + 3] + p3;
                 }
+                if (i + 1 < NCH) tc_wait_ld(nxt);
             }
-            asm volatile("bar.sync 1, %0;" ::"r"(32 * TC_EPI_WARPS) : "memory");  // the buffer is free again
+            tc_fence_before();
+            mbar_arrive(&tmem_empty[s]);
         }
     }
     __syncthreads();
-    if (*abort_flag != 0) {
+    const bool ok = *abort_flag == 0;
+    if (ok) {
+        // (L0 + L1) + (L2 + L3): the four lane chains of each output meet in shared memory
+        if (warp < TC_EPI_WARPS) {
+            const int q = warp & 3, half = warp >> 2;
+#pragma unroll
+            for (int j = 0; j < T::COLS; ++j) comb[(q * TC_MT + lane) * TC_COMB_STRIDE + half * T::COLS + j] = acc[j];
+        }
+        __syncthreads();
+        for (int i = tid; i < TC_MT * NT; i += T::THREADS) {
+            const int m = i / NT, n = i % NT;
+            if (m < mr && n < nr) {
+                const float c0 = comb[(0 * TC_MT + m) * TC_COMB_STRIDE + n], c1 = comb[(1 * TC_MT + m) * TC_COMB_STRIDE + n];
+                const float c2 = comb[(2 * TC_MT + m) * TC_COMB_STRIDE + n], c3 = comb[(3 * TC_MT + m) * TC_COMB_STRIDE + n];
+                Y[(long)(m0 + m) * y_stride + n0 + n] = (c0 + c1) + (c2 + c3);
+            }
+        }
+    } else {
         // an expired wait: let this CTA's MMAs and copies finish (bounded) before its TMEM and
         // shared memory are released; each slot / stage has at most one outstanding phase
         if (tid == 32 * T::MMA_WARP)
