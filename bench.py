@@ -702,10 +702,34 @@ def main():
                     help="only time the model upload (gtn_model_load from host memory, gtn_model_load_file "
                          "from a file in the page cache)")
     ap.add_argument("--decode-only", type=int, default=0, metavar="T",
-                    help="only load the model and run one request of T generated tokens (for a launch list)")
+                    help="only load the model and run one request of T generated tokens (for a launch list); "
+                         "with --batch B > 1: one warm generate_batch of B sequences of --model, then the measured "
+                         "one of T tokens inside the NVTX range 'gen' (ncu --nvtx --nvtx-include gen/)")
     ap.add_argument("--topk", type=int, default=0, metavar="K",
                     help="with --decode-only: draw with top-k sampling (temperature 0.9, seed 7) instead of greedy")
     args = ap.parse_args()
+    if args.decode_only and args.batch > 1:
+        import numpy as np
+        import torch
+
+        import gten_b200 as G
+        from gten_b200 import gtenfile
+        _, kind = BATCH_MODELS[args.model]
+        n_prompt = BATCH_PROMPT[args.model]
+        m = G.Model(kind, args.wdtype, n_prompt + BATCH_GEN[args.model], args.batch)
+        m.load(gtenfile.synthetic_image_device(kind, args.wdtype, SEED))
+        prompts = np.random.default_rng(42).integers(0, 32000, (args.batch, n_prompt)).astype(np.int32)
+        m.generate_batch(prompts, 2)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("gen")
+        out = m.generate_batch(prompts, args.decode_only)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        m.check()
+        m.close()
+        print(json.dumps({"decode_only": args.decode_only, "batch": args.batch, "model": args.model,
+                          "first_ids": [int(x) for x in out[0, :8]]}), flush=True)
+        return
     if args.decode_only:
         import numpy as np
         import torch

@@ -1115,38 +1115,46 @@ __global__ void __launch_bounds__(GV3_THREADS, 2) k_gemm4(const uint8_t* __restr
         ++nissued;
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // the tile's activation lane words; the raw rows are first copied with coalesced 4-byte loads
-    // into the (not yet used) product buffer when they fit there and are word aligned
+    // the tile's activation lane words. Word-aligned rows are first copied with coalesced 4-byte
+    // loads into the (not yet used) product buffer, as many rows per pass as fit there (long rows
+    // take several passes); converting straight from global memory with 2-byte loads is one chain
+    // of L2 round trips per thread
     const int xrow = nb * GTN_Q8_BYTES;
-    const bool stage_x = (size_t)mt * xrow <= (size_t)MC * R * 4 * pstr * sizeof(float) &&
-                         ((reinterpret_cast<uintptr_t>(X) | (uintptr_t)x_stride | (uintptr_t)xrow) & 3) == 0;
-    const uint8_t* xsrc = X + (long)m0 * x_stride;
-    long xss = x_stride;
-    if (stage_x) {
-        const int wpr = xrow / 4;
-        uint32_t* xd = reinterpret_cast<uint32_t*>(prod);
-        for (int i = tid; i < mt * wpr; i += GV3_THREADS) {
-            const int m = i / wpr, w = i - m * wpr;
-            xd[i] = reinterpret_cast<const uint32_t*>(xsrc + (long)m * x_stride)[w];
+    const size_t pbytes = (size_t)MC * R * 4 * pstr * sizeof(float);
+    const bool aligned = ((reinterpret_cast<uintptr_t>(X) | (uintptr_t)x_stride | (uintptr_t)xrow) & 3) == 0;
+    const int per_pass = aligned ? (int)min((size_t)mt, pbytes / (size_t)xrow) : 0;
+    const int step = per_pass > 0 ? per_pass : mt;
+    for (int p0 = 0; p0 < mt; p0 += step) {
+        const int pr = min(step, mt - p0);
+        const uint8_t* xsrc = X + (long)(m0 + p0) * x_stride;
+        long xss = x_stride;
+        if (per_pass > 0) {
+            const int wpr = xrow / 4;
+            uint32_t* xd = reinterpret_cast<uint32_t*>(prod);
+            for (int i = tid; i < pr * wpr; i += GV3_THREADS) {
+                const int m = i / wpr, w = i - m * wpr;
+                xd[i] = reinterpret_cast<const uint32_t*>(xsrc + (long)m * x_stride)[w];
+            }
+            __syncthreads();
+            xsrc = reinterpret_cast<const uint8_t*>(prod);
+            xss = xrow;
         }
-        __syncthreads();
-        xsrc = reinterpret_cast<const uint8_t*>(prod);
-        xss = xrow;
+        for (int i = tid; i < pr * nb * 4; i += GV3_THREADS) {
+            const int l = i & 3, b = (i >> 2) % nb, mp = (i >> 2) / nb, m = p0 + mp;
+            const uint8_t* blk = xsrc + (long)mp * xss + (long)b * GTN_Q8_BYTES;
+            const uint8_t* q = blk + 2;
+            const int w0 = (int)ld_u16(q + 2 * l) | ((int)ld_u16(q + 8 + 2 * l) << 16);
+            const int w1 = (int)ld_u16(q + 16 + 2 * l) | ((int)ld_u16(q + 24 + 2 * l) << 16);
+            const int jj = b >> 2, k = b & 3;
+            int* pw = reinterpret_cast<int*>(pa + ((size_t)(m * 4 + k) * 2 + (l >> 1)) * nbg + jj) + 2 * (l & 1);
+            pw[0] = w0;
+            pw[1] = w1;
+            if (WDT == GTN_Q4)
+                ps[((size_t)(m * 4 + k) * 4 + l) * nbg + jj] = dp4a(w0, 0x01010101, dp4a(w1, 0x01010101, 0));
+            if (l == 0) pda[(size_t)(m * 4 + k) * nbg + jj] = h2f(ld_u16(blk));
+        }
+        __syncthreads();  // this pass's lane words in place; the staged rows may be overwritten
     }
-    for (int i = tid; i < mt * nb * 4; i += GV3_THREADS) {
-        const int l = i & 3, b = (i >> 2) % nb, m = (i >> 2) / nb;
-        const uint8_t* blk = xsrc + (long)m * xss + (long)b * GTN_Q8_BYTES;
-        const uint8_t* q = blk + 2;
-        const int w0 = (int)ld_u16(q + 2 * l) | ((int)ld_u16(q + 8 + 2 * l) << 16);
-        const int w1 = (int)ld_u16(q + 16 + 2 * l) | ((int)ld_u16(q + 24 + 2 * l) << 16);
-        const int jj = b >> 2, k = b & 3;
-        int* pw = reinterpret_cast<int*>(pa + ((size_t)(m * 4 + k) * 2 + (l >> 1)) * nbg + jj) + 2 * (l & 1);
-        pw[0] = w0;
-        pw[1] = w1;
-        if (WDT == GTN_Q4) ps[((size_t)(m * 4 + k) * 4 + l) * nbg + jj] = dp4a(w0, 0x01010101, dp4a(w1, 0x01010101, 0));
-        if (l == 0) pda[(size_t)(m * 4 + k) * nbg + jj] = h2f(ld_u16(blk));
-    }
-    __syncthreads();  // prepared lane words in place; the staged rows in the product buffer are done
     const int nch = R * 4;  // chains per activation row
     int it = 0;
     for (int g = blockIdx.x; g < ngroups; g += gridDim.x, ++it) {
