@@ -294,14 +294,16 @@ static cudaError_t launch_gm3(const uint8_t* X, long xs, int M, const uint8_t* W
 
 // k_gemm4 plan: R weight rows per group (one pass of 256 threads over the 4-block groups), the
 // activation tile MT (all M rows, else halves) and MC rows per product chunk, preferring two CTAs
-// per SM (within 110 KB of shared memory), then one (200 KB).
+// per SM (within 110 KB of shared memory), then one (200 KB). Rows of 128 blocks or more (K >= 4096:
+// 5 weight rows per group) take one CTA per SM at once: its larger chunks give phase 2 more chains
+// at a time (MiniCPM-2B's batch-8 decode step 5.10 -> 4.72 ms).
 template <int WDT>
 static bool gm4_plan(const uint8_t* W, long ws, int M, int K, GM4Plan* p) {
     const int nb = K / GTN_QBLK;
     if (M < 2 || K % GTN_QBLK || nb % 4 || nb == 0 || nb / 4 > GV3_THREADS) return false;
     if ((reinterpret_cast<uintptr_t>(W) & 15) || (ws & 15)) return false;
     const int R = std::min(GV3_THREADS / (nb / 4), 64);
-    for (int occ = 2; occ >= 1; --occ) {
+    for (int occ = nb >= 128 ? 1 : 2; occ >= 1; --occ) {
         const size_t lim = occ == 2 ? (size_t)110 * 1024 : (size_t)200 * 1024;
         for (int tiles = 1;; tiles *= 2) {
             const int mt = (M + tiles - 1) / tiles;
