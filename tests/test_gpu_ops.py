@@ -46,6 +46,35 @@ def test_matmul_2d(orc, gpu, wdt, M, K, N, odt_kind):
         assert np.array_equal(got[sp * rb:], want[sp * rb:]), f"start_pos={sp}"
 
 
+@pytest.mark.parametrize("wdt", [Q8, Q4])
+@pytest.mark.parametrize("K", [2304, 5632, 5760])
+@pytest.mark.parametrize("M", [2, 5, 8, 12, 15])
+def test_small_batch_gemm(orc, gpu, wdt, K, M):
+    """The batched decode steps' GEMM for 2-15 rows (k_gemm4) on the models' row lengths: groups of
+    14 or 5 weight rows with a ragged last group (N = 97), two CTAs per SM for K = 2304 and one with
+    larger product chunks for the long rows, activation rows staged in one or several passes."""
+    import ctypes as C
+    rng = np.random.default_rng(M * 100 + K + wdt)
+    N = 97
+    x = act_rows(orc, rng, Q8, M, K)
+    w = weights(orc, rng, wdt, N, K)
+    want = orc.matmul_2d(x, Q8, M, K, w, wdt, N, F32, start_pos=0)
+    # weight rows padded to a multiple of 8 blocks (16-byte rows, as the model arena lays them out;
+    # K = 5760 is 180 blocks): the row stride of the descriptor says so
+    nb, bb = K // 32, 34 if wdt == Q8 else 18
+    nbp = (nb + 7) // 8 * 8
+    wp = np.zeros((N, nbp * bb), np.uint8)
+    wp[:, :nb * bb] = np.asarray(w, np.uint8).reshape(N, nb * bb)
+    wd = G.GT(to_dev(wp, gpu), wdt, (N, K)).desc()
+    wd.strides[0] = nbp * 32
+    xd = G.GT(to_dev(x, gpu), Q8, (M, K)).desc()
+    out = dev_out(4 * N * M, gpu)
+    od = G.GT(out, F32, (M, N)).desc()
+    rc = G.lib().gtn_matmul_2d(C.byref(xd), C.byref(wd), C.byref(od), 0, G._stream(None))
+    assert rc == 0, G.lib().gtn_last_error()
+    assert np.array_equal(from_dev(out), want)
+
+
 @pytest.mark.parametrize("wdt", [Q8, Q4, F16])
 def test_matmul_1d_logits(orc, gpu, wdt):
     """EmbeddingLinear's stride-0 fp32 output (modules.cpp:111-122): last row only."""
