@@ -65,10 +65,10 @@ def test_small_batch_gemm(orc, gpu, wdt, K, M):
     nbp = (nb + 7) // 8 * 8
     wp = np.zeros((N, nbp * bb), np.uint8)
     wp[:, :nb * bb] = np.asarray(w, np.uint8).reshape(N, nb * bb)
-    wd = G.GT(to_dev(wp, gpu), wdt, (N, K)).desc()
+    w_dev, x_dev, out = to_dev(wp, gpu), to_dev(x, gpu), dev_out(4 * N * M, gpu)  # alive through the call
+    wd = G.GT(w_dev, wdt, (N, K)).desc()
     wd.strides[0] = nbp * 32
-    xd = G.GT(to_dev(x, gpu), Q8, (M, K)).desc()
-    out = dev_out(4 * N * M, gpu)
+    xd = G.GT(x_dev, Q8, (M, K)).desc()
     od = G.GT(out, F32, (M, N)).desc()
     rc = G.lib().gtn_matmul_2d(C.byref(xd), C.byref(wd), C.byref(od), 0, G._stream(None))
     assert rc == 0, G.lib().gtn_last_error()
