@@ -465,17 +465,21 @@ cudaError_t gemm_q(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, 
 
 cudaError_t gemm_f16(const uint8_t* X, long xs, int M, const uint8_t* W, long ws, int N, int K, float* Y, long ldy,
                      cudaStream_t st, bool dry) {
-    if (M >= 2) {  // k_gemm_f16: 128 (or 32, for grids under two waves) weight rows x 16 rows per CTA
-        const int mtiles = (M + MF_MT - 1) / MF_MT;
-        const bool wide = (long)((N + mf_rows(4) - 1) / mf_rows(4)) * mtiles >= 2L * sm_count();
-        const size_t smem = mf_smem(wide ? 4 : 1);
-        const cudaError_t e = wide ? ensure_smem(k_gemm_f16<4>, smem) : ensure_smem(k_gemm_f16<1>, smem);
+    if (M >= 2) {
+        // k_gemm_f16: 128 (or 32, for grids under two waves) weight rows x 16 activation rows per
+        // CTA; 8 activation rows when the 32-row grid of 16-row tiles would still leave SMs with a
+        // single CTA (two fit), or when M <= 8
+        const long sms = sm_count();
+        const int mt16 = (M + 15) / 16;
+        const bool wide = (long)((N + mf_rows(4) - 1) / mf_rows(4)) * mt16 >= 2 * sms;
+        const bool narrow = !wide && (M <= 8 || (long)((N + mf_rows(1) - 1) / mf_rows(1)) * mt16 < 2 * sms);
+        const int mtile = narrow ? 8 : 16, rw = wide ? 4 : 1, mtiles = (M + mtile - 1) / mtile;
+        const size_t smem = mf_smem(rw, mtile);
+        auto kern = wide ? k_gemm_f16<4, 16> : (narrow ? k_gemm_f16<1, 8> : k_gemm_f16<1, 16>);
+        const cudaError_t e = ensure_smem(kern, smem);
         if (e != cudaSuccess || dry) return e;
-        if (wide)
-            return launch_pdl(k_gemm_f16<4>, dim3((N + mf_rows(4) - 1) / mf_rows(4), mtiles), dim3(MF_THREADS), smem,
-                              st, W, ws, N, K, X, xs, M, Y, ldy, device_error_word());
-        return launch_pdl(k_gemm_f16<1>, dim3((N + mf_rows(1) - 1) / mf_rows(1), mtiles), dim3(MF_THREADS), smem, st,
-                          W, ws, N, K, X, xs, M, Y, ldy, device_error_word());
+        return launch_pdl(kern, dim3((N + mf_rows(rw) - 1) / mf_rows(rw), mtiles), dim3(MF_THREADS), smem, st, W, ws,
+                          N, K, X, xs, M, Y, ldy, device_error_word());
     }
     const int mt = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
     int nw = 4;

@@ -338,22 +338,26 @@ __global__ void __launch_bounds__(NW * 32) k_mm_f16(const uint8_t* __restrict__ 
 // tile is converted once to fp32 in an [element][row] layout (row stride padded to 68 floats: the
 // 8 lanes of a slot read 8 consecutive elements with conflict-free 16-byte loads), so every float4
 // load feeds 4 * RW products. grid (ceil(N / (32 RW)), ceil(M / MF_MT)).
-constexpr int MF_MT = 16, MF_STAGES = MM_STAGES, MF_THREADS = 256;
-constexpr int MF_XSTR = 68;  // floats per element of the fp32 activation tile (16 rows + padding)
+// MF_MT activation rows per CTA: 16, or 8 when the 16-row grid would leave SMs with one CTA
+// (e.g. M = 32 against 2048 weight rows: 128 CTAs instead of 256) or M <= 8.
+constexpr int MF_STAGES = MM_STAGES, MF_THREADS = 256;
+// floats per element of the fp32 activation tile: the rows + 4 (bank spread of the 16-byte loads)
+__host__ __device__ constexpr int mf_xstr(int mt) { return mt == 16 ? 68 : 36; }
 __host__ __device__ constexpr int mf_rows(int rw) { return 32 * rw; }
 __host__ __device__ constexpr int mf_kt(int rw) { return rw == 1 ? 128 : 64; }
 __host__ __device__ constexpr int mf_wstride(int rw) { return mf_kt(rw) * 2 + 16; }
-__host__ __device__ inline size_t mf_smem(int rw) {
-    return 128 + (size_t)MF_STAGES * (mf_rows(rw) * mf_wstride(rw) + MF_MT * mf_kt(rw) * 2) +
-           (size_t)mf_kt(rw) * MF_XSTR * sizeof(float);
+__host__ __device__ inline size_t mf_smem(int rw, int mt = 16) {
+    return 128 + (size_t)MF_STAGES * (mf_rows(rw) * mf_wstride(rw) + mt * mf_kt(rw) * 2) +
+           (size_t)mf_kt(rw) * mf_xstr(mt) * sizeof(float);
 }
 
-template <int RW>
+template <int RW, int MF_MT>
 static __global__ void __launch_bounds__(MF_THREADS, 2) k_gemm_f16(const uint8_t* __restrict__ W, long w_stride,
                                                                    int N, int K, const uint8_t* __restrict__ X,
                                                                    long x_stride, int M, float* __restrict__ Y,
                                                                    long y_stride, unsigned int* err) {
-    constexpr int ROWS = mf_rows(RW), KT = mf_kt(RW);
+    constexpr int ROWS = mf_rows(RW), KT = mf_kt(RW), MF_XSTR = mf_xstr(MF_MT);
+    static_assert(MF_MT == 8 || MF_MT == 16, "8- or 16-row activation tiles");
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int abort_flag;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
