@@ -314,6 +314,38 @@ def gemm_sweep(G, torch, wdt: int, device, M: int, only: str | None = None):
     return out
 
 
+def run_tokenizers(assets: str) -> dict:
+    """Host tokenizers: encode() of one seeded ~16 KB text (words, digits, punctuation, whitespace
+    runs, multi-byte UTF-8) per model configuration; the reference's own tokenizer (compiled from
+    src/gten/tokenizer.cpp into oracle/_ref) is the baseline leg, and its ids must equal ours."""
+    import random
+
+    from gten_b200 import tokenizer as T
+    rng = random.Random(11)
+    alphabet = ([bytes([c]) for c in b"abcdefghijklmnopqrstuvwxyz ABCXYZ0123456789.,;:!?'-\n\t"] +
+                [w.encode() for w in ("the ", "and ", "é", "中文", "の", "🙂", "  ", "'s ", "'ll ")])
+    text = b"".join(rng.choice(alphabet) for _ in range(12000))[:16384]
+    ref_lib = os.path.join(ROOT, "oracle", "_ref", "libgtenref.so")
+    out = {"metric": "tokenizer encode ms", "text_bytes": len(text), "models": {}}
+    for name in ("tinyllama", "zephyr", "minicpm", "openelm"):
+        tok = T.for_model(name, assets)
+        t0 = time.perf_counter()
+        ids = tok.encode(text)
+        ours = time.perf_counter() - t0
+        rec = {"ours_ms": round(ours * 1e3, 3), "ids": len(ids)}
+        if os.path.exists(ref_lib):
+            from oracle.tokenizer_oracle import ReferenceTokenizer, for_model
+            ref = ReferenceTokenizer(ref_lib, for_model(name, assets))
+            t0 = time.perf_counter()
+            rids = ref.encode(text)
+            rec["reference_ms"] = round((time.perf_counter() - t0) * 1e3, 1)
+            rec["same_ids"] = rids == ids
+            ref.close()
+        tok.close()
+        out["models"][name] = rec
+    return out
+
+
 def weight_bytes(kind: int, wdt: int) -> int:
     """Algorithmic weight bytes one decode token streams: every projection matrix and the lm_head
     (the embedding contributes one row), in the reference's block format."""
@@ -705,9 +737,16 @@ def main():
                     help="only load the model and run one request of T generated tokens (for a launch list); "
                          "with --batch B > 1: one warm generate_batch of B sequences of --model, then the measured "
                          "one of T tokens inside the NVTX range 'gen' (ncu --nvtx --nvtx-include gen/)")
+    ap.add_argument("--tokenizers", default=None, metavar="DIR",
+                    help="only time encode() of a seeded 16 KB text with each model's tokenizer, from the "
+                         "vocabulary files in DIR (the reference's assets/tokenizers), against the reference's "
+                         "own tokenizer (oracle/_ref) where it was built")
     ap.add_argument("--topk", type=int, default=0, metavar="K",
                     help="with --decode-only: draw with top-k sampling (temperature 0.9, seed 7) instead of greedy")
     args = ap.parse_args()
+    if args.tokenizers:
+        print(json.dumps(run_tokenizers(args.tokenizers)), flush=True)
+        return
     if args.decode_only and args.batch > 1:
         import numpy as np
         import torch
