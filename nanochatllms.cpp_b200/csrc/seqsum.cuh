@@ -25,9 +25,14 @@
 //  (4) one int64 prefix scan of (increments + tie count * 2^48) gives every thread the increments
 //      and the ties before its chunk, so heads record their increment prefix and ties land in
 //      index order;
-//  (5) per binade (in parallel): the increments from its head to the next head, and the tie
-//      parities d_j; then one warp walks the binades in order: S = fl(S + p_head) (an exact IEEE
-//      add) must land in binade e, then S/u += increments + round-ups, which must stay below 2^24.
+//  (5) one warp: per binade the increments from its head to the next head and the tie parities
+//      d_j; then one thread walks the binades in order, reading them from shared memory:
+//      S = fl(S + p_head) (an exact IEEE add) must land in binade e, then S/u += increments +
+//      round-ups, which must stay below 2^24.
+// Each scan takes one CTA barrier, the tail one and the result one more: four barriers when the
+// caller supplies the largest term, six otherwise. (A walk that passed the binades between the lanes of a warp
+// by shuffles ran about 1,100-1,700 cycles per binade on sm_100a; the single-thread walk runs
+// about 80.)
 // Any failed check (a mispredicted crossing, a term below the fixed-point resolution, a subnormal
 // binade, a non-finite term, more ties than the list holds) makes the CTA fall back to the plain
 // sequential loop, so the result is always bit-identical to the serial sum.
@@ -43,27 +48,25 @@ constexpr int SEQSUM_FRAC_BITS = 25;  // the largest term becomes < 2^(24 + 25)
 constexpr int SEQSUM_PER_MAX = 8;     // default terms per thread kept in registers
 
 struct SeqSumSmem {
-    long long wsum[2][SEQSUM_THREADS_MAX / 32];  // per-warp partials of the two scans
+    long long wsum[2][SEQSUM_THREADS_MAX / 32];  // per-warp totals of the two scans
     long long hpre[SEQSUM_SLOTS];                // per binade: increments before its head
     int head[SEQSUM_SLOTS];
     float phead[SEQSUM_SLOTS];
     int d0[SEQSUM_SLOTS];  // parity of the first tie (or -1: no tie)
     int x[SEQSUM_SLOTS];   // sum of d_j xor d_(j-1) over the binade's ties
-    int sslot[SEQSUM_TIES_MAX], sd[SEQSUM_TIES_MAX];  // ties in index order: binade, parity d_j
-    // the walk's inputs, binades in order
-    float wph[SEQSUM_SLOTS];
-    int we[SEQSUM_SLOTS], wdd[SEQSUM_SLOTS];
-    long long wadd[SEQSUM_SLOTS];
-    int nbin;
+    int sslot[SEQSUM_TIES_MAX], sd[SEQSUM_TIES_MAX];  // ties in index order: binade, increment-prefix parity
+    int4 walk[SEQSUM_SLOTS];  // the binades in order: head term, exponent bits, tie mask, increments
     int bad;
     unsigned int maxbits;
     float result;
 };
 
-// Exclusive prefix of x over the CTA (thread order), in int64, with per-warp partials in `wsum`
-// (not read by a scan in flight); two CTA barriers.
+// Exclusive prefix of x over the CTA (thread order), in int64, with one CTA barrier: every warp
+// stores its total in `wsum`, then every warp sums the totals of the warps before its own (lane j
+// takes warp j's, a butterfly adds them up). `wsum` must not be written again before the next CTA
+// barrier.
 __device__ __forceinline__ long long seqsum_exscan64(long long x, long long* wsum) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     long long inc = x;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -72,17 +75,10 @@ __device__ __forceinline__ long long seqsum_exscan64(long long x, long long* wsu
     }
     if (lane == 31) wsum[warp] = inc;
     __syncthreads();
-    if (warp == 0) {
-        long long w = lane < nw ? wsum[lane] : 0;
+    long long pre = lane < warp ? wsum[lane] : 0;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const long long t = __shfl_up_sync(0xffffffffu, w, o);
-            if (lane >= o) w += t;
-        }
-        if (lane < nw) wsum[lane] = w;
-    }
-    __syncthreads();
-    return (warp > 0 ? wsum[warp - 1] : 0) + inc - x;
+    for (int o = 16; o > 0; o >>= 1) pre += __shfl_xor_sync(0xffffffffu, pre, o);
+    return pre + inc - x;
 }
 
 // p = M * 2^(E - 23) for a finite non-negative float (M < 2^24; subnormals E = -126).
@@ -120,9 +116,9 @@ __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, 
     }
     if (tid == 0) {
         s.bad = n > (1 << 14) || per > PER;  // n: keeps the fixed-point sum below 2^63
-        s.maxbits = maxbits;
+        s.maxbits = 0u;
     }
-    if (maxbits == 0u) {
+    if (maxbits == 0u) {  // uniform over the CTA
         __syncthreads();
         // (1) largest term (non-negative floats order like their bit patterns)
         unsigned int mb = 0u;
@@ -130,11 +126,12 @@ __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, 
         for (int k = 0; k < PER; ++k) mb = max(mb, __float_as_uint(pv[k]));  // pv >= +0
         mb = __reduce_max_sync(0xffffffffu, mb);
         if (lane == 0) atomicMax(&s.maxbits, mb);
+        __syncthreads();
+        maxbits = s.maxbits;
+        if (maxbits == 0u) return 0.0f;  // every term is +0: the sum is exactly 0
     }
-    __syncthreads();
-    maxbits = s.maxbits;
-    if (maxbits == 0u) return 0.0f;                   // every term is +0: the sum is exactly 0
-    if (maxbits >= 0x7f800000u) s.bad = 1;            // inf / nan / a negative term
+    // the shared state written above is next read after the first scan's barrier
+    bool bad = maxbits >= 0x7f800000u;  // inf / nan / a negative term
     const int emax = maxbits >= 0x800000u ? (int)(maxbits >> 23) - 127 : -126;
     // binade exponent of slot sl: Q = S * 2^eoff => e = sl - eoff
     const int eoff = 23 + SEQSUM_FRAC_BITS - emax;
@@ -154,7 +151,6 @@ __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, 
     // (3) per term: binade slot, head flag, increment, tie (independent once the slots are known)
     int slv[PER], inc[PER];
     bool hd[PER], tie[PER];
-    bool bad = false;
     {
         long long Q = Q0;
         int slp = Q0 > 0 ? 63 - __clzll(Q0) : -1;
@@ -190,101 +186,88 @@ __device__ __forceinline__ float seq_sum_exact(Term term, int n, SeqSumSmem& s, 
     }
     constexpr long long LOW48 = (1LL << 48) - 1;
     const long long P = seqsum_exscan64(itot + ((long long)ntl << 48), s.wsum[1]);
-    const long long total = s.wsum[1][nw - 1] & LOW48;  // inclusive over the last warp
-    const int ntie_all = (int)(s.wsum[1][nw - 1] >> 48);
     long long cur = P & LOW48;
     int trank = (int)(P >> 48);
-    long long tpre[PER];  // inclusive increment prefix at each term
+    // heads record their increment prefix; ties land in index order with the parity of the
+    // increment prefix up to and including their own floor
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
         cur += inc[k];
-        tpre[k] = cur;
         if (hd[k]) {
             s.head[slv[k]] = i0 + k;
             s.hpre[slv[k]] = cur;  // a head's own increment is 0
             s.phead[slv[k]] = pv[k];
         }
-    }
-    __syncthreads();
-    // (5a) ties in index order: binade and the parity of the binade's increments up to the tie
-    const int nties = min(ntie_all, SEQSUM_TIES_MAX);
-    if (ntie_all > SEQSUM_TIES_MAX && tid == 0) s.bad = 1;
-#pragma unroll
-    for (int k = 0; k < PER; ++k) {
         if (tie[k]) {
             if (trank < SEQSUM_TIES_MAX) {
                 s.sslot[trank] = slv[k];
-                s.sd[trank] = (int)((tpre[k] - s.hpre[slv[k]]) & 1);
+                s.sd[trank] = (int)(cur & 1);
             }
             ++trank;
         }
     }
-    // (5b) warps 0-1, one binade slot per thread: the binades in order (64 slots as two ballots)
-    // and their increment totals
-    if (tid < SEQSUM_SLOTS) {
+    __syncthreads();
+    // (5) warp 0: the totals of the second scan, the binades present (64 slots as two ballots),
+    // the ties per binade, then lane 0 walks the binades in order.
+    if (warp == 0) {
+        long long wt = lane < nw ? s.wsum[1][lane] : 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) wt += __shfl_xor_sync(0xffffffffu, wt, o);
+        const long long total = wt & LOW48;
+        const int ntie_all = (int)(wt >> 48);
         const unsigned long long mask = (unsigned long long)__ballot_sync(0xffffffffu, s.head[lane] >= 0) |
                                         ((unsigned long long)__ballot_sync(0xffffffffu, s.head[lane + 32] >= 0) << 32);
-        const int sl = tid;
-        if ((mask >> sl) & 1ULL) {
-            const unsigned long long above = sl < 63 ? mask & (~0ULL << (sl + 1)) : 0ULL;
-            const long long nxt = above ? s.hpre[__ffsll((long long)above) - 1] : total;
-            const int r = __popcll(mask & ((1ULL << sl) - 1ULL));
-            s.wph[r] = s.phead[sl];
-            s.we[r] = sl - eoff;
-            s.wadd[r] = nxt - s.hpre[sl];
+        // per binade: the first tie's parity d_0 (relative to the head's prefix) and the changes
+        // d_j xor d_(j-1) between consecutive ties (the head's parity cancels in those)
+        const int nties = min(ntie_all, SEQSUM_TIES_MAX);
+        for (int r = lane; r < nties; r += 32) {
+            const int sl = s.sslot[r];
+            if (r == 0 || s.sslot[r - 1] != sl) s.d0[sl] = (s.sd[r] ^ (int)(s.hpre[sl] & 1)) & 1;
+            else atomicAdd(&s.x[sl], (s.sd[r] ^ s.sd[r - 1]) & 1);
         }
-        if (tid == 0) s.nbin = __popcll(mask);
-    }
-    __syncthreads();
-    // (5c) per binade: the first tie's parity and the changes between consecutive ties
-    for (int r = tid; r < nties; r += nt) {
-        const int sl = s.sslot[r];
-        if (r == 0 || s.sslot[r - 1] != sl) s.d0[sl] = s.sd[r];
-        else atomicAdd(&s.x[sl], s.sd[r] ^ s.sd[r - 1]);
-    }
-    __syncthreads();
-    // (5d) the walk (warp 0, every lane the same chain; lane 0 keeps the result). Lane j holds
-    // binades j and j + 32 in registers; the chain takes them by shuffles.
-    if (warp == 0) {
-        bool ok = !s.bad;
-        float S = 0.0f;
-        const int nb = s.nbin;
-        float ph[2];
-        int ee[2], dd[2];
-        long long ad[2];
+        __syncwarp();
+        // one record per binade present, in order (lanes j and j + 32 take slots j and j + 32):
+        //   .x  the head term's bits
+        //   .y  the binade's exponent field (e + 127) << 23, or ~0 when it is subnormal or
+        //       beyond the largest finite binade
+        //   .z  the first tie's parity d_0, or -1 without ties: the round-up on entry is
+        //       ((S/u + d_0) & 1) & (d_0 >= 0 ? 1 : 0)
+        //   .w  the increments up to the next head plus the later ties' round-ups, saturated at
+        //       2^25 (the binade's integer S/u stays below 2^24, so more fails anyway)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const int j = lane + 32 * h;
-            ph[h] = 0.0f;
-            ee[h] = 0;
-            dd[h] = -1;
-            ad[h] = 0;
-            if (j < nb) {
-                const int sl = s.we[j] + eoff;  // x is 0 without ties
-                ph[h] = s.wph[j];
-                ee[h] = s.we[j];
-                dd[h] = s.d0[sl];
-                ad[h] = s.wadd[j] + s.x[sl];
+            const int sl = lane + 32 * h;
+            if ((mask >> sl) & 1ULL) {
+                const unsigned long long above = sl < 63 ? mask & (~0ULL << (sl + 1)) : 0ULL;
+                const long long nxt = above ? s.hpre[__ffsll((long long)above) - 1] : total;
+                const long long add = nxt - s.hpre[sl] + s.x[sl];
+                const int e = sl - eoff;
+                int4 w;
+                w.x = __float_as_int(s.phead[sl]);
+                w.y = e >= -126 && e <= 127 ? (e + 127) << 23 : -1;
+                w.z = s.d0[sl];
+                w.w = (int)min(add, (long long)(1 << 25));
+                s.walk[__popcll(mask & ((1ULL << sl) - 1ULL))] = w;
             }
         }
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-#pragma unroll 4
-            for (int jj = 0; jj < 32; ++jj) {
-                if (!ok || 32 * h + jj >= nb) break;
-                const float p = __shfl_sync(0xffffffffu, ph[h], jj);
-                const int e = __shfl_sync(0xffffffffu, ee[h], jj), d = __shfl_sync(0xffffffffu, dd[h], jj);
-                const long long add = __shfl_sync(0xffffffffu, ad[h], jj);
-                S = S + p;
-                const unsigned int b = __float_as_uint(S);
-                long long Sb = (long long)((b & 0x7fffffu) | 0x800000u);  // S / u
-                Sb += d >= 0 ? ((Sb + d) & 1) : 0;
-                Sb += add;
-                ok = (int)(b >> 23) - 127 == e && e >= -126 && Sb < (1LL << 24);
-                S = __uint_as_float(((unsigned int)(e + 127) << 23) | ((unsigned int)Sb & 0x7fffffu));
-            }
-        }
+        __syncwarp();
         if (lane == 0) {
+            // the walk: S = fl(S + p_head) must land in binade e, then S/u += the round-up on
+            // entry and the binade's increments, which must stay below 2^24
+            const int nb = __popcll(mask);
+            bool ok = !s.bad && ntie_all <= SEQSUM_TIES_MAX;
+            float S = 0.0f;
+#pragma unroll 4
+            for (int r = 0; r < nb; ++r) {
+                const int4 w = s.walk[r];
+                S = S + __int_as_float(w.x);
+                const int bS = __float_as_int(S);
+                const int Sb = (bS & 0x7fffff) | 0x800000;  // S / u
+                const int up = (Sb + w.z) & (w.z >= 0 ? 1 : 0);
+                const int Sn = Sb + w.w + up;
+                ok = ok && (bS & 0x7f800000) == w.y && Sn < (1 << 24);
+                S = __int_as_float(w.y | (Sn & 0x7fffff));
+            }
             if (!ok) {  // fallback: the reference's loop as is
                 S = 0.0f;
                 for (int i = 0; i < n; ++i) {
