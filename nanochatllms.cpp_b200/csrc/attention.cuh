@@ -320,12 +320,7 @@ __device__ __forceinline__ void att_softmax(float* p, int n, int last, float mx,
     const float m = __uint_as_float((mk & 0x80000000u) ? (mk ^ 0x80000000u) : ~mk);
     for (int j = tid; j < n; j += ATT_THREADS) p[j] = j <= last ? expf_ref(p[j] - m) : 0.0f;
     __syncthreads();
-    if (tid == 0) {
-        float sum = 0.0f;
-#pragma unroll 8
-        for (int j = 0; j <= last; ++j) sum = sum + p[j];  // keys > last add +0.0f
-        stat[1] = sum;
-    }
+    if (tid == 0) stat[1] = serial_sum_smem(p, last + 1);  // keys > last add +0.0f
     __syncthreads();
     const float sum = stat[1];
     for (int blk = warp; blk * GTN_QBLK < n; blk += ATT_THREADS / 32) {
