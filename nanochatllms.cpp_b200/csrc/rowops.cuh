@@ -80,8 +80,13 @@ static __global__ void k_norm(const uint8_t* x, long xs, long hs, uint8_t* out, 
     if (!LAYER && n > 256) {
         // the sequential sum of squares, computed exactly in parallel (seqsum.cuh); short rows
         // (OpenELM's 64-wide head norms) take the serial loop below, which is faster there
+        // the fewest terms per thread in registers that hold the row: the unrolled per-term work
+        // is that much shorter (the decode step's cluster norm runs the 4-term form too)
         __shared__ SeqSumSmem ss;
-        const float sq = seq_sum_squares(v, n, ss, reinterpret_cast<int*>(v + n));
+        int* scratch = reinterpret_cast<int*>(v + n);
+        const int per = (n + (int)blockDim.x - 1) / (int)blockDim.x;
+        const float sq = per <= 4 ? seq_sum_squares<4>(v, n, ss, scratch)
+                                  : (per <= 5 ? seq_sum_squares<5>(v, n, ss, scratch) : seq_sum_squares(v, n, ss, scratch));
         if (threadIdx.x == 0) {
             stat[0] = 0.0f;
             stat[1] = sqrtf(sq / (float)n);
