@@ -160,6 +160,41 @@ def test_rms_norm_sequential_sum_adversarial(orc, gpu, D):
         assert np.array_equal(got[r * D * 4:(r + 1) * D * 4], want[r * D * 4:(r + 1) * D * 4]), f"row {r}"
 
 
+@pytest.mark.parametrize("D", [2048, 2304])
+def test_rms_norm_sequential_sum_many_rows(orc, gpu, D):
+    """1,024 seeded rows of mixed distributions (Gaussian with outlier dimensions, Q8-dequantized
+    residual blocks, coarse grids with many rounding ties, wide log-uniform ranges): the exact
+    parallel sum of squares must equal the serial loop bit for bit on every one."""
+    rng = np.random.default_rng(77 + D)
+    M = 1024
+    x = np.empty((M, D), np.float64)
+    for r in range(M):
+        kind = r % 6
+        if kind == 0:
+            v = rng.standard_normal(D) * 10.0 ** rng.uniform(-3, 3)
+        elif kind == 1:
+            v = rng.standard_normal(D)
+            v[rng.integers(0, D, 4)] *= rng.uniform(10, 200)
+        elif kind == 2:
+            d = rng.uniform(1e-3, 1.0, (D + 31) // 32).astype(np.float16).astype(np.float64)
+            v = rng.integers(-127, 128, D) * np.repeat(d, 32)[:D]
+        elif kind == 3:
+            v = rng.integers(-8, 9, D) * 2.0 ** int(rng.integers(-10, 10))
+        elif kind == 4:
+            v = np.sign(rng.standard_normal(D)) * 10.0 ** rng.uniform(-6, 4, D)
+        else:
+            v = rng.standard_normal(D) * np.where(rng.random(D) < 0.5, 0.0, 1.0)
+        x[r] = v
+    x = x.astype(np.float32)
+    w = fp16_vec(rng, D)
+    out = torch.zeros(M * D * 4, dtype=torch.uint8, device=gpu)
+    G.rms_norm(G.GT(to_dev(x, gpu), F32, (M, D)), G.GT(to_dev(w, gpu), F16, (D,)), G.GT(out, F32, (M, D)))
+    want = orc.rms_norm(x.view(np.uint8).ravel().copy(), F32, M, D, w, 0)
+    got = from_dev(out)
+    bad = [r for r in range(M) if not np.array_equal(got[r * D * 4:(r + 1) * D * 4], want[r * D * 4:(r + 1) * D * 4])]
+    assert not bad, f"rows {bad[:10]} of {len(bad)}"
+
+
 @pytest.mark.parametrize("dt", [Q8, F16])
 def test_rms_norm_3d(orc, gpu, dt):
     rng = np.random.default_rng(3 + dt)
