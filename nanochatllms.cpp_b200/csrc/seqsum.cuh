@@ -26,13 +26,13 @@
 //      and the ties before its chunk, so heads record their increment prefix and ties land in
 //      index order;
 //  (5) one warp: per binade the increments from its head to the next head and the tie parities
-//      d_j; then one thread walks the binades in order, reading them from shared memory:
-//      S = fl(S + p_head) (an exact IEEE add) must land in binade e, then S/u += increments +
-//      round-ups, which must stay below 2^24.
+//      d_j, packed into one 16-byte record per binade; then one thread walks the records in
+//      order: S = fl(S + p_head) (an exact IEEE add) must land in binade e, then S/u +=
+//      increments + round-ups, in 32-bit integers, which must stay below 2^24.
 // Each scan takes one CTA barrier, the tail one and the result one more: four barriers when the
-// caller supplies the largest term, six otherwise. (A walk that passed the binades between the lanes of a warp
-// by shuffles ran about 1,100-1,700 cycles per binade on sm_100a; the single-thread walk runs
-// about 80.)
+// caller supplies the largest term, six otherwise. (A walk that passed the binades between the
+// lanes of a warp by shuffles ran about 1,100-1,700 cycles per binade on sm_100a; the
+// single-thread walk over the records runs about 80.)
 // Any failed check (a mispredicted crossing, a term below the fixed-point resolution, a subnormal
 // binade, a non-finite term, more ties than the list holds) makes the CTA fall back to the plain
 // sequential loop, so the result is always bit-identical to the serial sum.
