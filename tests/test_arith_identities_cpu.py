@@ -32,3 +32,26 @@ def test_block_lane_sums_fit_the_exact_range():
     lane = np.array([-q8, -q4, 0, q4, q8], np.int64)
     via_bias = (lane + BIAS_BITS).astype(np.int32).view(np.float32) - BIAS
     assert np.array_equal(via_bias, lane.astype(np.float32))
+
+
+def test_fp16_products_are_exact_in_fp32():
+    """The exact fp16 GEMM (csrc/matmul.cuh `k_gemm_f16`) adds each fp16 x fp16 product into the
+    reference's fp32 lane chain with one fused multiply-add. That equals the reference's separate
+    multiply and add because the product of two fp16 values (11-bit significands, exponents
+    -24..15) is exact in fp32: fma(a, b, c) = RN(a*b + c) = RN(fl(a*b) + c) when fl(a*b) == a*b."""
+    # every pair of significands (hidden bit included) at exponent 0 ...
+    sig = (1024 + np.arange(1024, dtype=np.float64)) / 1024.0
+    a, b = np.meshgrid(sig, sig)
+    exact = a * b  # float64 holds the 22-bit product exactly
+    assert np.array_equal((a.astype(np.float32) * b.astype(np.float32)).astype(np.float64), exact)
+    # ... and pairs drawn from every finite fp16 value, subnormals and the extremes included
+    rng = np.random.default_rng(16)
+    bits = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+    vals = bits.view(np.float16)
+    vals = vals[np.isfinite(vals)]
+    x = rng.choice(vals, 2_000_000).astype(np.float64)
+    y = rng.choice(vals, 2_000_000).astype(np.float64)
+    x = np.concatenate([x, vals.astype(np.float64)])
+    y = np.concatenate([y, np.full(vals.size, 65504.0)])  # the largest magnitude against all
+    exact = x * y
+    assert np.array_equal((x.astype(np.float32) * y.astype(np.float32)).astype(np.float64), exact)
